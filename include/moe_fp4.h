@@ -1,0 +1,167 @@
+/*
+ * moe_fp4.h — C ABI of libmoe_fp4.so, the B200 (sm_100a) MXFP4 grouped-MoE
+ * expert path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (cudaStream_t / CUstream passed as void*), launches asynchronously on that
+ * stream and returns an MFI_* status code.  On failure the message of
+ * mfi_last_error() (per thread) says what was wrong; argument errors use the
+ * reference binding's TORCH_CHECK wording where one exists.  Nothing here
+ * allocates device memory: operations that need scratch take a caller-owned
+ * workspace whose size the matching *_workspace_bytes() function returns.
+ *
+ * Data formats (reference quant/fp4_format.py:17-148,
+ * quant/quantize_mxfp4.py:110-160):
+ *   packed  uint8 (rows, Kp/2)  two E2M1 nibbles per byte, element 2k in the
+ *                               low nibble of byte k
+ *   scales  uint8 (rows, Kp/32) E8M0 codes, value 2^(code-127)
+ *   Kp = ceil(K/32)*32; padding elements are zero nibbles.
+ *
+ * Citations are paths inside the reference project
+ * (shuimenwang/moe_fused_inference).
+ */
+#ifndef MOE_FP4_H
+#define MOE_FP4_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum mfi_status {
+  MFI_OK = 0,
+  MFI_ERR_ARG = 1,        /* invalid argument (shape, pointer, size)          */
+  MFI_ERR_CUDA = 2,       /* a CUDA call or kernel launch failed               */
+  MFI_ERR_WORKSPACE = 3,  /* caller workspace smaller than *_workspace_bytes() */
+};
+
+/* Element type codes for activation inputs. */
+enum mfi_dtype { MFI_F32 = 0, MFI_F16 = 1, MFI_BF16 = 2 };
+
+/* Message describing the last failed call on this host thread ("" if none). */
+const char* mfi_last_error(void);
+
+/* Library ABI version (bumped when a signature changes). */
+int mfi_version(void);
+
+/* ------------------------------------------------------------------------
+ * Quantisers
+ * ------------------------------------------------------------------------ */
+
+/* Activation quantiser: bf16 x (M, K) row-major -> xq (M, Kp/2), xsc (M, Kp/32).
+ * Replaces mxfp4v2::launch_prequant_v2 (src/ext/mxfp4_decode.cu:304-309), bound
+ * by prequant() (src/ext/mxfp4_decode_binding.cpp:65-81).  Every byte of xq
+ * and xsc is written (padding included), so no zero-fill is needed.  Bit-exact
+ * with quantize_expert_tensor (quant/quantize_mxfp4.py:110-160). */
+int mfi_prequant(const void* x_bf16, uint8_t* xq, uint8_t* xsc, int M, int K, int Kp,
+                 void* stream);
+
+/* General row quantiser: x of dtype MFI_* with row stride ld_x elements.
+ * half_roundtrip = 1 rounds every element through fp16 first, the cast the
+ * reference's mxfp4_linear binding applies to non-half inputs
+ * (src/ext/mxfp4_binding.cpp:31).  Columns [K, Kp) are zero padding (Kp a
+ * multiple of 32, Kp >= K).  Also the bit-exact device form of the weight
+ * quantiser quantize_expert_tensor (quant/quantize_mxfp4.py:110-160). */
+int mfi_quantize_rows(const void* x, int dtype, long long ld_x, int half_roundtrip,
+                      uint8_t* xq, uint8_t* xsc, int M, int K, int Kp, void* stream);
+
+/* ------------------------------------------------------------------------
+ * GEMMs (y = A . W^T, fp32 out)
+ * ------------------------------------------------------------------------ */
+
+/* Pre-quantised linear: y (M, N) fp32 = Q(x) . W^T.
+ * Replaces mxfp4v2::launch_lin_pq_v2 (src/ext/mxfp4_decode.cu:311-318), bound
+ * by lin_pq() (src/ext/mxfp4_decode_binding.cpp:84-98). */
+int mfi_lin_pq(const uint8_t* xq, const uint8_t* xsc, const uint8_t* wp, const uint8_t* wsc,
+               float* y, int M, int N, int K, int Kp, void* stream);
+
+/* Linear with on-the-fly activation quantisation: x (M, ld_x) of dtype
+ * MFI_* (non-half inputs rounded through fp16 like the reference binding),
+ * columns [0, min(ld_x, Kp)) quantised per 32 block and the rest zero,
+ * multiplied by the packed W (N, Kp/2)/(N, Kp/32) -> y (M, N) fp32.
+ * Replaces mxfp4::launch_mxfp4_linear (src/ext/mxfp4_linear.cu:200-206),
+ * bound by forward() (src/ext/mxfp4_binding.cpp:21-45). */
+size_t mfi_linear_workspace_bytes(int M, int Kp);
+int mfi_mxfp4_linear(const void* x, int dtype, int ld_x, const uint8_t* wp, const uint8_t* wsc,
+                     float* y, int M, int N, int Kp, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* ------------------------------------------------------------------------
+ * Grouped MoE operators behind device pointer tables
+ * ------------------------------------------------------------------------ */
+
+/* Grouped gate/up.  wp_tab/wsc_tab: device arrays of 2*E*M pointers in the
+ * reference order [token m: gate e0..e(E-1), up e0..e(E-1)]; gu (M*E, 2N) fp32
+ * with gate in columns [0,N) and up in [N,2N).  Entries that point at the
+ * same weight share one pass over it.
+ * Replaces mxfp4v2::launch_gateup_v2 (src/ext/mxfp4_decode.cu:320-328), bound
+ * by moe_gateup()/moe_gateup_tab() (src/ext/mxfp4_decode_binding.cpp:101-120,
+ * 177-192). */
+size_t mfi_moe_gateup_workspace_bytes(int E, int M);
+int mfi_moe_gateup(const uint8_t* xq, const uint8_t* xsc, const uint8_t* const* wp_tab,
+                   const uint8_t* const* wsc_tab, float* gu, int E, int M, int N, int K, int Kp,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* Fused SwiGLU + down.  gu (M*E, 2K) fp32 from mfi_moe_gateup; h = silu(g)*u
+ * in fp32, requantised per 32 block; yd (M*E, N) fp32 = Q(h) . Wd^T with
+ * wp_tab/wsc_tab of E*M pointers in order m*E + e.
+ * Replaces mxfp4v2::launch_down_silu_v2 (src/ext/mxfp4_decode.cu:330-338),
+ * bound by moe_down()/moe_down_tab() (src/ext/mxfp4_decode_binding.cpp:123-142,
+ * 194-209). */
+size_t mfi_moe_down_workspace_bytes(int E, int M, int K);
+int mfi_moe_down(const float* gu, const uint8_t* const* wp_tab, const uint8_t* const* wsc_tab,
+                 float* yd, int E, int M, int N, int K, int Kp, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
+/* Top-k combine: out[m, c] = sum_{e < min(E, 8)} w[m, e] * yd[(m*E + e)*ystride + c]
+ * in fp32, sequential in e (the reference kernel sums at most 8 slots).
+ * Replaces mxfp4v2::launch_combine_v2 (src/ext/mxfp4_decode.cu:340-344), bound
+ * by moe_combine() (src/ext/mxfp4_decode_binding.cpp:145-158). */
+int mfi_moe_combine(const float* yd, int ystride, const float* w, int E, float* out, int M, int N,
+                    void* stream);
+
+/* ------------------------------------------------------------------------
+ * Fused device-routed MoE layer (no reference counterpart as a single call:
+ * it fulfils the reference's unimplemented K1/K2/K3 stubs
+ * src/kernels/k1_router_topk_sort.cu, k2_mxfp4_grouped_gemm.cu,
+ * k3_deterministic_combine.cu, and performs model_runner_v2's MoE block
+ * runtime/model_runner_v2.py:183-208 / :266-290 without host round trips).
+ * ------------------------------------------------------------------------ */
+typedef struct mfi_moe_weights {
+  const uint8_t* gate_wp;   /* (E, inter, hidden/2)  */
+  const uint8_t* gate_sc;   /* (E, inter, hidden/32) */
+  const uint8_t* up_wp;     /* (E, inter, hidden/2)  */
+  const uint8_t* up_sc;     /* (E, inter, hidden/32) */
+  const uint8_t* down_wp;   /* (E, hidden, inter/2)  */
+  const uint8_t* down_sc;   /* (E, hidden, inter/32) */
+  const uint8_t* router_wp; /* (E, hidden/2)         */
+  const uint8_t* router_sc; /* (E, hidden/32)        */
+  int n_experts;            /* E <= 256                               */
+  int hidden;               /* multiple of 32                         */
+  int inter;                /* multiple of 32                         */
+  int top_k;                /* 1..min(E, 32)                          */
+} mfi_moe_weights;
+
+/* x: bf16 (T, hidden) -> out fp32 (T, hidden); topi int32 (T, top_k) and
+ * topw fp32 (T, top_k) receive the routing; logits fp32 (T, E) may be NULL.
+ * T <= 4096 / top_k. */
+size_t mfi_moe_layer_workspace_bytes(int T, int hidden, int inter, int n_experts, int top_k);
+int mfi_moe_layer(const mfi_moe_weights* w, const void* x_bf16, int T, float* out, int32_t* topi,
+                  float* topw, float* logits, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
+/* As mfi_moe_layer, recording six caller-created cudaEvent_t (passed as void*)
+ * on the stream at the stage boundaries: [0] start, [1] after routing,
+ * [2] after the gate/up GEMV, [3] after SwiGLU requantisation, [4] after the
+ * down GEMV, [5] after the combine — per-kernel timing for benchmarks. */
+int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float* out,
+                     int32_t* topi, float* topw, float* logits, void* workspace,
+                     size_t workspace_bytes, void* const* events, int n_events, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_FP4_H */

@@ -1,0 +1,84 @@
+"""ctypes binding of libmoe_fp4.so (C ABI declared in include/moe_fp4.h).
+
+The library is built in-tree by ``python -m moe_fused_inference_b200.build``
+(``__graft_entry__.build()`` does it too).  There is no fallback: if the
+shared object is missing or fails to load, every operator raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "lib", "libmoe_fp4.so")
+
+_lock = threading.Lock()
+_lib = None
+
+# Every symbol include/moe_fp4.h declares: name -> (restype, argtypes).
+_VP = ctypes.c_void_p
+_I = ctypes.c_int
+_LL = ctypes.c_longlong
+_SZ = ctypes.c_size_t
+SIGNATURES = {
+    "mfi_last_error": (ctypes.c_char_p, []),
+    "mfi_version": (_I, []),
+    "mfi_prequant": (_I, [_VP, _VP, _VP, _I, _I, _I, _VP]),
+    "mfi_quantize_rows": (_I, [_VP, _I, _LL, _I, _VP, _VP, _I, _I, _I, _VP]),
+    "mfi_lin_pq": (_I, [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP]),
+    "mfi_linear_workspace_bytes": (_SZ, [_I, _I]),
+    "mfi_mxfp4_linear": (_I, [_VP, _I, _I, _VP, _VP, _VP, _I, _I, _I, _VP, _SZ, _VP]),
+    "mfi_moe_gateup_workspace_bytes": (_SZ, [_I, _I]),
+    "mfi_moe_gateup": (_I, [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _VP, _SZ, _VP]),
+    "mfi_moe_down_workspace_bytes": (_SZ, [_I, _I, _I]),
+    "mfi_moe_down": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _VP, _SZ, _VP]),
+    "mfi_moe_combine": (_I, [_VP, _I, _VP, _I, _VP, _I, _I, _VP]),
+    "mfi_moe_layer_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
+    "mfi_moe_layer": (_I, [_VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _SZ, _VP]),
+    "mfi_moe_layer_ex": (_I, [_VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _SZ, _VP, _I, _VP]),
+}
+
+MFI_F32, MFI_F16, MFI_BF16 = 0, 1, 2
+
+
+class MoEWeights(ctypes.Structure):
+    """Mirror of ``mfi_moe_weights`` (include/moe_fp4.h)."""
+
+    _fields_ = [
+        ("gate_wp", _VP), ("gate_sc", _VP), ("up_wp", _VP), ("up_sc", _VP),
+        ("down_wp", _VP), ("down_sc", _VP), ("router_wp", _VP), ("router_sc", _VP),
+        ("n_experts", _I), ("hidden", _I), ("inter", _I), ("top_k", _I),
+    ]
+
+
+class MfiError(RuntimeError):
+    """A libmoe_fp4 call returned a non-zero status."""
+
+
+def load():
+    """Load (once) and return the ctypes handle; raise if the library is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"{LIB_PATH} is not built; run `python -m moe_fused_inference_b200.build` "
+                "(there is no CPU fallback)")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        msg = load().mfi_last_error().decode(errors="replace")
+        raise MfiError(f"{what}: {msg} (status {status})")

@@ -1,0 +1,343 @@
+// capi.cu — the extern "C" surface of libmoe_fp4.so (declared in include/moe_fp4.h).
+//
+// Each entry point validates its arguments (messages follow the reference
+// binding's TORCH_CHECK wording, src/ext/mxfp4_decode_binding.cpp and
+// src/ext/mxfp4_binding.cpp), carves its scratch out of the caller's
+// workspace, launches on the caller's stream and checks the launch — the
+// reference launches never call cudaGetLastError.
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/moe_fp4.h"
+#include "mx_common.cuh"
+#include "work.cuh"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return MFI_OK;
+  return fail(MFI_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// The library carries its own (static) CUDA runtime, whose current device is
+// separate from the caller's.  Select the caller's stream's device so launches
+// land where the stream lives.
+inline cudaStream_t as_stream(void* s) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(s);
+  if (st) {
+    int want = -1, cur = -1;
+    if (cudaStreamGetDevice(st, &want) == cudaSuccess && cudaGetDevice(&cur) == cudaSuccess &&
+        want != cur)
+      cudaSetDevice(want);
+  }
+  return st;
+}
+inline int ceil32(int k) { return (k + 31) / 32 * 32; }
+
+// Bump allocator over a caller-owned workspace (256-byte aligned pieces).
+struct Carve {
+  uint8_t* base;
+  size_t used = 0;
+  explicit Carve(void* p) : base(static_cast<uint8_t*>(p)) {}
+  template <class T>
+  T* take(size_t count) {
+    used = (used + 255) & ~size_t(255);
+    T* p = reinterpret_cast<T*>(base ? base + used : nullptr);
+    used += count * sizeof(T);
+    return p;
+  }
+};
+
+constexpr int kGemvMaxCtas = 148 * 4;
+
+bool bad_ptr(const void* p) { return p == nullptr; }
+
+}  // namespace
+
+extern "C" {
+
+const char* mfi_last_error(void) { return g_err.c_str(); }
+
+int mfi_version(void) { return 1; }
+
+// ---------------------------------------------------------------------------
+int mfi_quantize_rows(const void* x, int dtype, long long ld_x, int half_roundtrip, uint8_t* xq,
+                      uint8_t* xsc, int M, int K, int Kp, void* stream) {
+  if (M < 0 || K < 0) return fail(MFI_ERR_ARG, "M and K must be non-negative");
+  if (Kp < K || Kp % 32 != 0) return fail(MFI_ERR_ARG, "Kp must be a multiple of 32 and >= K");
+  if (dtype != MFI_F32 && dtype != MFI_F16 && dtype != MFI_BF16)
+    return fail(MFI_ERR_ARG, "dtype must be MFI_F32, MFI_F16 or MFI_BF16");
+  if (M == 0 || K == 0) return MFI_OK;
+  if (bad_ptr(x) || bad_ptr(xq) || bad_ptr(xsc)) return fail(MFI_ERR_ARG, "null pointer");
+  if (ld_x < K) return fail(MFI_ERR_ARG, "ld_x must be >= K");
+  mfi::QuantArgs a{x, long(ld_x), dtype, half_roundtrip ? 1 : 0, xq, xsc, M, K, Kp};
+  return cuda_status(mfi::launch_quant_rows(a, as_stream(stream)), "quantize_rows launch");
+}
+
+int mfi_prequant(const void* x_bf16, uint8_t* xq, uint8_t* xsc, int M, int K, int Kp,
+                 void* stream) {
+  return mfi_quantize_rows(x_bf16, MFI_BF16, K, 0, xq, xsc, M, K, Kp, stream);
+}
+
+// ---------------------------------------------------------------------------
+int mfi_lin_pq(const uint8_t* xq, const uint8_t* xsc, const uint8_t* wp, const uint8_t* wsc,
+               float* y, int M, int N, int K, int Kp, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return fail(MFI_ERR_ARG, "M, N, K must be non-negative");
+  if (Kp <= 0 || Kp % 32 != 0) return fail(MFI_ERR_ARG, "Kp must be a positive multiple of 32");
+  if (M == 0 || N == 0) return MFI_OK;
+  if (bad_ptr(xq) || bad_ptr(xsc) || bad_ptr(wp) || bad_ptr(wsc) || bad_ptr(y))
+    return fail(MFI_ERR_ARG, "null pointer");
+  return cuda_status(
+      mfi::launch_dense_gemv(xq, xsc, wp, wsc, y, N, M, N, Kp, as_stream(stream)), "lin_pq launch");
+}
+
+size_t mfi_linear_workspace_bytes(int M, int Kp) {
+  Carve c(nullptr);
+  c.take<uint8_t>(size_t(M) * (Kp / 2));
+  c.take<uint8_t>(size_t(M) * (Kp / 32));
+  return c.used + 256;
+}
+
+int mfi_mxfp4_linear(const void* x, int dtype, int ld_x, const uint8_t* wp, const uint8_t* wsc,
+                     float* y, int M, int N, int Kp, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+  if (M < 0 || N < 0 || ld_x <= 0) return fail(MFI_ERR_ARG, "M, N must be >= 0 and K > 0");
+  if (Kp <= 0 || Kp % 32 != 0) return fail(MFI_ERR_ARG, "Kp must be a positive multiple of 32");
+  if (M == 0 || N == 0) return MFI_OK;
+  if (bad_ptr(x) || bad_ptr(wp) || bad_ptr(wsc) || bad_ptr(y) || bad_ptr(workspace))
+    return fail(MFI_ERR_ARG, "null pointer");
+  if (workspace_bytes < mfi_linear_workspace_bytes(M, Kp))
+    return fail(MFI_ERR_WORKSPACE, "workspace too small for mxfp4_linear");
+  Carve c(workspace);
+  uint8_t* xq = c.take<uint8_t>(size_t(M) * (Kp / 2));
+  uint8_t* xsc = c.take<uint8_t>(size_t(M) * (Kp / 32));
+  // the reference kernel reads x columns [0, min(K, Kp)) and treats the rest as zero
+  const int k_eff = ld_x < Kp ? ld_x : Kp;
+  const int half_rt = dtype == MFI_F16 ? 0 : 1;
+  int st = mfi_quantize_rows(x, dtype, ld_x, half_rt, xq, xsc, M, k_eff, Kp, stream);
+  if (st != MFI_OK) return st;
+  return cuda_status(
+      mfi::launch_dense_gemv(xq, xsc, wp, wsc, y, N, M, N, Kp, as_stream(stream)),
+      "mxfp4_linear gemm launch");
+}
+
+// ---------------------------------------------------------------------------
+size_t mfi_moe_gateup_workspace_bytes(int E, int M) {
+  const size_t P = size_t(2) * E * M;
+  Carve c(nullptr);
+  c.take<int>(1);
+  c.take<mfi::GroupDesc>(P);
+  c.take<mfi::EntryDesc>(P);
+  return c.used + 256;
+}
+
+int mfi_moe_gateup(const uint8_t* xq, const uint8_t* xsc, const uint8_t* const* wp_tab,
+                   const uint8_t* const* wsc_tab, float* gu, int E, int M, int N, int K, int Kp,
+                   void* workspace, size_t workspace_bytes, void* stream) {
+  (void)K;
+  if (E <= 0 || M <= 0 || N <= 0) return fail(MFI_ERR_ARG, "E, M, N must be positive");
+  if (Kp <= 0 || Kp % 32 != 0) return fail(MFI_ERR_ARG, "Kp must be a positive multiple of 32");
+  const long long P = 2LL * E * M;
+  if (P > mfi::kBuildGroupsMaxP) return fail(MFI_ERR_ARG, "pointer table longer than 4096 entries");
+  if (bad_ptr(xq) || bad_ptr(xsc) || bad_ptr(wp_tab) || bad_ptr(wsc_tab) || bad_ptr(gu) ||
+      bad_ptr(workspace))
+    return fail(MFI_ERR_ARG, "null pointer");
+  if (workspace_bytes < mfi_moe_gateup_workspace_bytes(E, M))
+    return fail(MFI_ERR_WORKSPACE, "workspace too small for moe_gateup");
+  Carve c(workspace);
+  int* ng = c.take<int>(1);
+  auto* groups = c.take<mfi::GroupDesc>(P);
+  auto* entries = c.take<mfi::EntryDesc>(P);
+  cudaStream_t s = as_stream(stream);
+  int st = cuda_status(mfi::launch_build_groups(wp_tab, wsc_tab, int(P), 0, E, N, groups, ng,
+                                                entries, s),
+                       "moe_gateup grouping launch");
+  if (st != MFI_OK) return st;
+  return cuda_status(mfi::launch_grouped_gemv(groups, ng, int(P), entries, xq, xsc, gu, N, Kp,
+                                              kGemvMaxCtas, s),
+                     "moe_gateup gemv launch");
+}
+
+size_t mfi_moe_down_workspace_bytes(int E, int M, int K) {
+  const size_t P = size_t(E) * M;
+  const int Kp = ceil32(K);
+  Carve c(nullptr);
+  c.take<int>(1);
+  c.take<mfi::GroupDesc>(P);
+  c.take<mfi::EntryDesc>(P);
+  c.take<uint8_t>(P * (Kp / 2));
+  c.take<uint8_t>(P * (Kp / 32));
+  return c.used + 256;
+}
+
+int mfi_moe_down(const float* gu, const uint8_t* const* wp_tab, const uint8_t* const* wsc_tab,
+                 float* yd, int E, int M, int N, int K, int Kp, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+  if (E <= 0 || M <= 0 || N <= 0 || K <= 0) return fail(MFI_ERR_ARG, "E, M, N, K must be positive");
+  if (Kp != ceil32(K)) return fail(MFI_ERR_ARG, "Kp must equal ceil32(K)");
+  const long long P = 1LL * E * M;
+  if (P > mfi::kBuildGroupsMaxP) return fail(MFI_ERR_ARG, "pointer table longer than 4096 entries");
+  if (bad_ptr(gu) || bad_ptr(wp_tab) || bad_ptr(wsc_tab) || bad_ptr(yd) || bad_ptr(workspace))
+    return fail(MFI_ERR_ARG, "null pointer");
+  if (workspace_bytes < mfi_moe_down_workspace_bytes(E, M, K))
+    return fail(MFI_ERR_WORKSPACE, "workspace too small for moe_down");
+  Carve c(workspace);
+  int* ng = c.take<int>(1);
+  auto* groups = c.take<mfi::GroupDesc>(P);
+  auto* entries = c.take<mfi::EntryDesc>(P);
+  uint8_t* hq = c.take<uint8_t>(P * (Kp / 2));
+  uint8_t* hsc = c.take<uint8_t>(P * (Kp / 32));
+  cudaStream_t s = as_stream(stream);
+  int st = cuda_status(mfi::launch_swiglu_quant(gu, 2L * K, nullptr, int(P), nullptr, hq, hsc, K,
+                                                Kp, s),
+                       "moe_down swiglu launch");
+  if (st != MFI_OK) return st;
+  st = cuda_status(mfi::launch_build_groups(wp_tab, wsc_tab, int(P), 1, E, N, groups, ng, entries,
+                                            s),
+                   "moe_down grouping launch");
+  if (st != MFI_OK) return st;
+  return cuda_status(mfi::launch_grouped_gemv(groups, ng, int(P), entries, hq, hsc, yd, N, Kp,
+                                              kGemvMaxCtas, s),
+                     "moe_down gemv launch");
+}
+
+int mfi_moe_combine(const float* yd, int ystride, const float* w, int E, float* out, int M, int N,
+                    void* stream) {
+  if (E <= 0 || M < 0 || N < 0) return fail(MFI_ERR_ARG, "E must be positive, M and N non-negative");
+  if (ystride < N) return fail(MFI_ERR_ARG, "ystride must be >= N");
+  if (M == 0 || N == 0) return MFI_OK;
+  if (bad_ptr(yd) || bad_ptr(w) || bad_ptr(out)) return fail(MFI_ERR_ARG, "null pointer");
+  const int e_sum = E < 8 ? E : 8;
+  return cuda_status(mfi::launch_combine(yd, ystride, w, E, e_sum, out, M, N, as_stream(stream)),
+                     "moe_combine launch");
+}
+
+// ---------------------------------------------------------------------------
+namespace {
+struct LayerScratch {
+  unsigned* done;
+  int* n_gu;
+  int* n_dn;
+  int* n_active;
+  uint8_t* xq;
+  uint8_t* xsc;
+  float* logits;
+  mfi::GroupDesc* g_gu;
+  mfi::EntryDesc* e_gu;
+  mfi::GroupDesc* g_dn;
+  mfi::EntryDesc* e_dn;
+  float* gu;
+  uint8_t* hq;
+  uint8_t* hsc;
+  float* yd;
+  size_t bytes;
+};
+
+LayerScratch carve_layer(void* ws, int T, int H, int Mi, int E, int k) {
+  Carve c(ws);
+  LayerScratch s;
+  const size_t P = size_t(T) * k;
+  s.done = c.take<unsigned>(1);
+  s.n_gu = c.take<int>(1);
+  s.n_dn = c.take<int>(1);
+  s.n_active = c.take<int>(1);
+  s.xq = c.take<uint8_t>(size_t(T) * (H / 2));
+  s.xsc = c.take<uint8_t>(size_t(T) * (H / 32));
+  s.logits = c.take<float>(size_t(T) * E);
+  s.g_gu = c.take<mfi::GroupDesc>(size_t(2) * E);
+  s.e_gu = c.take<mfi::EntryDesc>(2 * P);
+  s.g_dn = c.take<mfi::GroupDesc>(size_t(E));
+  s.e_dn = c.take<mfi::EntryDesc>(P);
+  s.gu = c.take<float>(P * 2 * Mi);
+  s.hq = c.take<uint8_t>(P * (Mi / 2));
+  s.hsc = c.take<uint8_t>(P * (Mi / 32));
+  s.yd = c.take<float>(P * H);
+  s.bytes = c.used + 256;
+  return s;
+}
+}  // namespace
+
+size_t mfi_moe_layer_workspace_bytes(int T, int hidden, int inter, int n_experts, int top_k) {
+  return carve_layer(nullptr, T, hidden, inter, n_experts, top_k).bytes;
+}
+
+int mfi_moe_layer(const mfi_moe_weights* w, const void* x_bf16, int T, float* out, int32_t* topi,
+                  float* topw, float* logits, void* workspace, size_t workspace_bytes,
+                  void* stream) {
+  return mfi_moe_layer_ex(w, x_bf16, T, out, topi, topw, logits, workspace, workspace_bytes,
+                          nullptr, 0, stream);
+}
+
+int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float* out,
+                     int32_t* topi, float* topw, float* logits, void* workspace,
+                     size_t workspace_bytes, void* const* events, int n_events, void* stream) {
+  if (events && n_events < 6) return fail(MFI_ERR_ARG, "events must hold 6 cudaEvent_t handles");
+  if (!w) return fail(MFI_ERR_ARG, "null weights");
+  const int E = w->n_experts, H = w->hidden, Mi = w->inter, k = w->top_k;
+  if (E <= 0 || E > mfi::kRouteMaxE) return fail(MFI_ERR_ARG, "n_experts must be in [1, 256]");
+  if (H <= 0 || H % 32 != 0 || Mi <= 0 || Mi % 32 != 0)
+    return fail(MFI_ERR_ARG, "hidden and inter must be positive multiples of 32");
+  if (k <= 0 || k > E || k > 32) return fail(MFI_ERR_ARG, "top_k must be in [1, min(E, 32)]");
+  if (T < 0 || (long long)T * k > mfi::kRouteMaxPairs)
+    return fail(MFI_ERR_ARG, "T * top_k must be <= 4096");
+  if (T == 0) return MFI_OK;
+  if (bad_ptr(x_bf16) || bad_ptr(out) || bad_ptr(topi) || bad_ptr(topw) || bad_ptr(workspace) ||
+      bad_ptr(w->gate_wp) || bad_ptr(w->gate_sc) || bad_ptr(w->up_wp) || bad_ptr(w->up_sc) ||
+      bad_ptr(w->down_wp) || bad_ptr(w->down_sc) || bad_ptr(w->router_wp) || bad_ptr(w->router_sc))
+    return fail(MFI_ERR_ARG, "null pointer");
+  if (workspace_bytes < mfi_moe_layer_workspace_bytes(T, H, Mi, E, k))
+    return fail(MFI_ERR_WORKSPACE, "workspace too small for moe_layer");
+  LayerScratch s = carve_layer(workspace, T, H, Mi, E, k);
+  cudaStream_t st = as_stream(stream);
+  auto mark = [&](int i) -> int {
+    if (!events) return MFI_OK;
+    return cuda_status(cudaEventRecord(reinterpret_cast<cudaEvent_t>(events[i]), st),
+                       "moe_layer event record");
+  };
+  int rc = mark(0);
+  if (rc != MFI_OK) return rc;
+  rc = cuda_status(cudaMemsetAsync(s.done, 0, sizeof(unsigned), st), "moe_layer memset");
+  if (rc != MFI_OK) return rc;
+  mfi::QuantArgs qa{x_bf16, long(H), mfi::kBF16, 0, s.xq, s.xsc, T, H, H};
+  rc = cuda_status(mfi::launch_quant_rows(qa, st), "moe_layer quantize launch");
+  if (rc != MFI_OK) return rc;
+  mfi::RouteArgs ra{};
+  ra.xq = s.xq; ra.xsc = s.xsc; ra.wr = w->router_wp; ra.sr = w->router_sc;
+  ra.T = T; ra.H = H; ra.E = E; ra.k = k;
+  ra.logits = logits ? logits : s.logits;
+  ra.topi = topi; ra.topw = topw; ra.done = s.done;
+  ra.gate_wp = w->gate_wp; ra.gate_sc = w->gate_sc; ra.up_wp = w->up_wp; ra.up_sc = w->up_sc;
+  ra.down_wp = w->down_wp; ra.down_sc = w->down_sc; ra.Mi = Mi;
+  ra.g_gu = s.g_gu; ra.e_gu = s.e_gu; ra.n_gu = s.n_gu;
+  ra.g_dn = s.g_dn; ra.e_dn = s.e_dn; ra.n_dn = s.n_dn; ra.n_active = s.n_active;
+  rc = cuda_status(mfi::launch_route(ra, st), "moe_layer route launch");
+  if (rc != MFI_OK || (rc = mark(1)) != MFI_OK) return rc;
+  const int P = T * k;
+  const int max_groups = E < P ? E : P;
+  rc = cuda_status(mfi::launch_grouped_gemv(s.g_gu, s.n_gu, 2 * max_groups, s.e_gu, s.xq, s.xsc,
+                                            s.gu, Mi, H, kGemvMaxCtas, st),
+                   "moe_layer gate/up launch");
+  if (rc != MFI_OK || (rc = mark(2)) != MFI_OK) return rc;
+  rc = cuda_status(mfi::launch_swiglu_quant(s.gu, 2L * Mi, nullptr, P, nullptr, s.hq, s.hsc, Mi,
+                                            Mi, st),
+                   "moe_layer swiglu launch");
+  if (rc != MFI_OK || (rc = mark(3)) != MFI_OK) return rc;
+  rc = cuda_status(mfi::launch_grouped_gemv(s.g_dn, s.n_dn, max_groups, s.e_dn, s.hq, s.hsc, s.yd,
+                                            H, Mi, kGemvMaxCtas, st),
+                   "moe_layer down launch");
+  if (rc != MFI_OK || (rc = mark(4)) != MFI_OK) return rc;
+  rc = cuda_status(mfi::launch_combine(s.yd, H, topw, k, k, out, T, H, st),
+                   "moe_layer combine launch");
+  if (rc != MFI_OK) return rc;
+  return mark(5);
+}
+
+}  // extern "C"

@@ -1,0 +1,75 @@
+// work.cuh — work-list types and launch entry points shared by the kernels
+// and the C ABI (capi.cu).  Host-visible only through include/moe_fp4.h.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace mfi {
+
+// One weight matrix and the activation rows that multiply it.
+struct GroupDesc {
+  const uint8_t* wp;   // (N, Kp/2) packed nibbles
+  const uint8_t* wsc;  // (N, Kp/32) E8M0 codes
+  int first;           // index of the group's first EntryDesc
+  int count;           // number of entries
+};
+
+// One activation row of a group and where its output row goes.
+struct EntryDesc {
+  int act_row;         // row of the packed activations
+  int pad;
+  long long out_off;   // element offset of the output row (column n adds n)
+};
+
+struct QuantArgs {
+  const void* x;
+  long ld_x;          // row stride of x in elements
+  int dtype;          // DType (mx_common.cuh)
+  int half_rt;        // 1: round each element through fp16 first (mxfp4_linear semantics)
+  uint8_t* xq;        // (M, Kp/2)
+  uint8_t* xsc;       // (M, Kp/32)
+  int M, K, Kp;
+};
+
+struct RouteArgs {
+  const uint8_t* xq;   // (T, H/2)
+  const uint8_t* xsc;  // (T, H/32)
+  const uint8_t* wr;   // (E, H/2)
+  const uint8_t* sr;   // (E, H/32)
+  int T, H, E, k;
+  float* logits;       // (T, E) or null
+  int* topi;           // (T, k)
+  float* topw;         // (T, k)
+  unsigned* done;      // completion counter, zero before the launch
+  const uint8_t* gate_wp; const uint8_t* gate_sc;
+  const uint8_t* up_wp; const uint8_t* up_sc;
+  const uint8_t* down_wp; const uint8_t* down_sc;
+  int Mi;
+  GroupDesc* g_gu; EntryDesc* e_gu; int* n_gu;   // 2 groups per active expert
+  GroupDesc* g_dn; EntryDesc* e_dn; int* n_dn;   // 1 group per active expert
+  int* n_active;
+};
+
+constexpr int kRouteMaxE = 256;
+constexpr int kRouteMaxPairs = 4096;
+constexpr int kBuildGroupsMaxP = 4096;
+
+cudaError_t launch_quant_rows(const QuantArgs& a, cudaStream_t stream);
+cudaError_t launch_swiglu_quant(const float* gu, long ld_gu, const int* rows, int n_rows,
+                                const int* n_rows_dev, uint8_t* hq, uint8_t* hsc, int K, int Kp,
+                                cudaStream_t stream);
+size_t gemv_smem_bytes(int Kp);
+cudaError_t launch_grouped_gemv(const GroupDesc* groups, const int* n_groups_dev, int n_groups_host,
+                                const EntryDesc* entries, const uint8_t* xq, const uint8_t* xsc,
+                                float* y, int N, int Kp, int max_ctas, cudaStream_t stream);
+cudaError_t launch_dense_gemv(const uint8_t* xq, const uint8_t* xsc, const uint8_t* wp,
+                              const uint8_t* wsc, float* y, long long ldy, int M, int N, int Kp,
+                              cudaStream_t stream);
+cudaError_t launch_build_groups(const uint8_t* const* wp_tab, const uint8_t* const* wsc_tab, int P,
+                                int mode, int E, int N, GroupDesc* groups, int* n_groups,
+                                EntryDesc* entries, cudaStream_t stream);
+cudaError_t launch_combine(const float* yd, long ystride, const float* w, int E, int E_sum,
+                           float* out, int M, int N, cudaStream_t stream);
+cudaError_t launch_route(const RouteArgs& a, cudaStream_t stream);
+
+}  // namespace mfi
