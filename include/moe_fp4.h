@@ -139,7 +139,7 @@ typedef struct mfi_moe_weights {
   const uint8_t* router_wp; /* (E, hidden/2)         */
   const uint8_t* router_sc; /* (E, hidden/32)        */
   int n_experts;            /* E <= 256                               */
-  int hidden;               /* multiple of 32                         */
+  int hidden;               /* multiple of 32, <= 4096                */
   int inter;                /* multiple of 32                         */
   int top_k;                /* 1..min(E, 32)                          */
 } mfi_moe_weights;

@@ -26,6 +26,10 @@ LIB = os.path.join(LIBDIR, "libmoe_fp4.so")
 INCLUDE = os.path.join(os.path.dirname(PKG), "include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+# Shared cudart: one runtime instance per process, shared with torch (the
+# same arrangement torch.utils.cpp_extension uses), so the current device and
+# stream-capture state are common to both.
+CUDA_LIB = os.path.join(os.path.dirname(os.path.dirname(shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc")), "lib64")
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",
               "--expt-relaxed-constexpr", "-ftz=false", "-prec-div=true", "-prec-sqrt=true",
               "-fmad=true"]
@@ -55,14 +59,16 @@ def build(verbose: bool = False, ptxas_v: bool = False, force: bool = False) -> 
         if (not force and os.path.exists(obj)
                 and os.path.getmtime(obj) >= max(os.path.getmtime(src), hdr_mtime)):
             continue
-        cmd = [nvcc, *ARCH, *NVCC_FLAGS, "-I", CSRC, "-I", INCLUDE, "-c", src, "-o", obj]
+        cmd = [nvcc, *ARCH, *NVCC_FLAGS, "-cudart", "shared", "-I", CSRC, "-I", INCLUDE, "-c", src,
+               "-o", obj]
         if ptxas_v:
             cmd += ["-Xptxas", "-v"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
     if force or not os.path.exists(LIB) or any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs):
-        cmd = [nvcc, *ARCH, "-shared", "-o", LIB + ".tmp", *objs]
+        cmd = [nvcc, *ARCH, "-shared", "-cudart", "shared", "-o", LIB + ".tmp", *objs,
+               "-Xlinker", f"-rpath,{CUDA_LIB}"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

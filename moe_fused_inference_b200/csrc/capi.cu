@@ -27,19 +27,9 @@ int cuda_status(cudaError_t e, const char* what) {
   return fail(MFI_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
-// The library carries its own (static) CUDA runtime, whose current device is
-// separate from the caller's.  Select the caller's stream's device so launches
-// land where the stream lives.
-inline cudaStream_t as_stream(void* s) {
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(s);
-  if (st) {
-    int want = -1, cur = -1;
-    if (cudaStreamGetDevice(st, &want) == cudaSuccess && cudaGetDevice(&cur) == cudaSuccess &&
-        want != cur)
-      cudaSetDevice(want);
-  }
-  return st;
-}
+// The library links the shared CUDA runtime, so it shares the caller's current
+// device; the stream must belong to that device (as with any torch extension).
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 inline int ceil32(int k) { return (k + 31) / 32 * 32; }
 
 // Bump allocator over a caller-owned workspace (256-byte aligned pieces).
@@ -283,8 +273,8 @@ int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float*
   if (!w) return fail(MFI_ERR_ARG, "null weights");
   const int E = w->n_experts, H = w->hidden, Mi = w->inter, k = w->top_k;
   if (E <= 0 || E > mfi::kRouteMaxE) return fail(MFI_ERR_ARG, "n_experts must be in [1, 256]");
-  if (H <= 0 || H % 32 != 0 || Mi <= 0 || Mi % 32 != 0)
-    return fail(MFI_ERR_ARG, "hidden and inter must be positive multiples of 32");
+  if (H <= 0 || H % 32 != 0 || Mi <= 0 || Mi % 32 != 0 || H > 4096)
+    return fail(MFI_ERR_ARG, "hidden and inter must be positive multiples of 32, hidden <= 4096");
   if (k <= 0 || k > E || k > 32) return fail(MFI_ERR_ARG, "top_k must be in [1, min(E, 32)]");
   if (T < 0 || (long long)T * k > mfi::kRouteMaxPairs)
     return fail(MFI_ERR_ARG, "T * top_k must be <= 4096");

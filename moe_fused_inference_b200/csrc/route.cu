@@ -25,6 +25,7 @@ __device__ __forceinline__ bool better(float v, int i, float w, int j) {
   return v > w || (v == w && i < j);
 }
 
+template <int kMaxBlk>
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   __shared__ float s_logit[kMaxE];
   __shared__ unsigned s_last;
@@ -34,18 +35,49 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   const int nb = a.H >> 5;
 
   // ---- logits for token t --------------------------------------------------
-  for (int e = warp; e < a.E; e += nwarp) {
-    double acc = 0.0;
-    for (int b = lane; b < nb; b += 32) {
-      const uint4 xa = ldg_u4(a.xq + long(t) * (a.H >> 1) + b * 16);
-      const uint4 wb = ldg_u4(a.wr + long(e) * (a.H >> 1) + b * 16);
-      const int s = block_dot_i(xa, wb);
-      const int ex = int(a.xsc[long(t) * nb + b]) + int(a.sr[long(e) * nb + b]) - 256;
-      acc += double(s) * exp2i_d(ex);
+  // Each lane owns blocks b = lane + 32*j; the token's blocks are loaded once,
+  // the router rows of all experts of this warp are in flight together.
+  uint4 xa[kMaxBlk];
+  int xs[kMaxBlk];
+#pragma unroll
+  for (int j = 0; j < kMaxBlk; ++j) {
+    const int b = lane + 32 * j;
+    if (b < nb) {
+      xa[j] = ldg_u4(a.xq + long(t) * (a.H >> 1) + b * 16);
+      xs[j] = a.xsc[long(t) * nb + b];
+    }
+  }
+  for (int e0 = warp; e0 < a.E; e0 += 4 * nwarp) {
+    uint4 wv[4][kMaxBlk];
+    int ws[4][kMaxBlk];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int e = e0 + u * nwarp;
+#pragma unroll
+      for (int j = 0; j < kMaxBlk; ++j) {
+        const int b = lane + 32 * j;
+        if (e < a.E && b < nb) {
+          wv[u][j] = ldg_u4(a.wr + long(e) * (a.H >> 1) + b * 16);
+          ws[u][j] = a.sr[long(e) * nb + b];
+        }
+      }
     }
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (lane == 0) s_logit[e] = float(acc);
+    for (int u = 0; u < 4; ++u) {
+      const int e = e0 + u * nwarp;
+      double acc = 0.0;
+#pragma unroll
+      for (int j = 0; j < kMaxBlk; ++j) {
+        const int b = lane + 32 * j;
+        if (e < a.E && b < nb) {
+          const int s = block_dot_i(xa[j], wv[u][j]);
+          acc += double(s) * exp2i_d(xs[j] + ws[u][j] - 256);
+        }
+      }
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+      if (lane == 0 && e < a.E) s_logit[e] = float(acc);
+    }
   }
   __syncthreads();
   if (a.logits)
@@ -93,25 +125,45 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   if (!s_last) return;
   __threadfence();
 
+  // Work lists: per active expert one gate group, one up group and one down
+  // group.  The position of an entry inside its expert's list comes from a
+  // shared-memory cursor; the order does not affect any result because every
+  // entry owns its output row.
   __shared__ int s_cnt[kMaxE];
   __shared__ int s_off[kMaxE];
   __shared__ int s_act[kMaxE];  // active index of expert e, or -1
+  __shared__ int s_cur[kMaxE];
   const int P = a.T * a.k;
-  for (int e = threadIdx.x; e < a.E; e += blockDim.x) s_cnt[e] = 0;
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x) { s_cnt[e] = 0; s_cur[e] = 0; }
   __syncthreads();
   for (int i = threadIdx.x; i < P; i += blockDim.x) atomicAdd(&s_cnt[__ldcg(a.topi + i)], 1);
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int off = 0, na = 0;
-    for (int e = 0; e < a.E; ++e) {
-      s_off[e] = off;
-      off += s_cnt[e];
-      s_act[e] = s_cnt[e] > 0 ? na++ : -1;
+  if (warp == 0) {
+    // exclusive scans of counts and of "active" flags over E <= 256 experts
+    int run_off = 0, run_act = 0;
+    for (int e0 = 0; e0 < a.E; e0 += 32) {
+      const int e = e0 + lane;
+      const int c = e < a.E ? s_cnt[e] : 0;
+      int inc = c, act = c > 0 ? 1 : 0;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, inc, off);
+        const int w = __shfl_up_sync(0xffffffffu, act, off);
+        if (lane >= off) { inc += v; act += w; }
+      }
+      if (e < a.E) {
+        s_off[e] = run_off + inc - c;
+        s_act[e] = c > 0 ? run_act + act - 1 : -1;
+      }
+      run_off += __shfl_sync(0xffffffffu, inc, 31);
+      run_act += __shfl_sync(0xffffffffu, act, 31);
     }
-    *a.n_gu = 2 * na;
-    *a.n_dn = na;
-    *a.n_active = na;
-    *a.done = 0u;  // ready for the next call
+    if (lane == 0) {
+      *a.n_gu = 2 * run_act;
+      *a.n_dn = run_act;
+      *a.n_active = run_act;
+      *a.done = 0u;  // ready for the next call
+    }
   }
   __syncthreads();
   const long gstride = long(a.Mi) * (a.H >> 1), gsstride = long(a.Mi) * (a.H >> 5);
@@ -130,28 +182,31 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
     g.first = first;
     g.wp = a.down_wp + e * dstride; g.wsc = a.down_sc + e * dsstride;
     a.g_dn[ai] = g;
-    // entries of expert e in (token, slot) order
-    int pos = first;
-    for (int i = 0; i < P; ++i) {
-      if (__ldcg(a.topi + i) != e) continue;
-      EntryDesc d;
-      d.pad = 0;
-      d.act_row = i / a.k;
-      d.out_off = (long long)i * 2 * a.Mi;
-      a.e_gu[pos] = d;
-      d.out_off += a.Mi;
-      a.e_gu[P + pos] = d;
-      d.act_row = i;
-      d.out_off = (long long)i * a.H;
-      a.e_dn[pos] = d;
-      ++pos;
-    }
+  }
+  for (int i = threadIdx.x; i < P; i += blockDim.x) {
+    const int e = __ldcg(a.topi + i);
+    const int pos = s_off[e] + atomicAdd(&s_cur[e], 1);
+    EntryDesc d;
+    d.pad = 0;
+    d.act_row = i / a.k;
+    d.out_off = (long long)i * 2 * a.Mi;
+    a.e_gu[pos] = d;
+    d.out_off += a.Mi;
+    a.e_gu[P + pos] = d;
+    d.act_row = i;
+    d.out_off = (long long)i * a.H;
+    a.e_dn[pos] = d;
   }
 }
 
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t stream) {
   if (a.T <= 0) return cudaSuccess;
-  route_kernel<<<a.T, kRouteThreads, 0, stream>>>(a);
+  if (a.H <= 2048)
+    route_kernel<2><<<a.T, kRouteThreads, 0, stream>>>(a);
+  else if (a.H <= 4096)
+    route_kernel<4><<<a.T, kRouteThreads, 0, stream>>>(a);
+  else
+    return cudaErrorInvalidValue;
   return cudaGetLastError();
 }
 
