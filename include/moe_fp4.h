@@ -46,6 +46,12 @@ const char* mfi_last_error(void);
 /* Library ABI version (bumped when a signature changes). */
 int mfi_version(void);
 
+/* Device error flag of the current device: 0 while healthy; non-zero after a
+ * kernel's bounded wait (2 s) timed out and the kernel returned early (1 load
+ * producer, 2 MMA issuer, 3 epilogue).  Synchronous; clear != 0 resets it.
+ * Returns -1 if the flag cannot be read. */
+int mfi_device_error(int clear);
+
 /* ------------------------------------------------------------------------
  * Quantisers
  * ------------------------------------------------------------------------ */
@@ -71,11 +77,15 @@ int mfi_quantize_rows(const void* x, int dtype, long long ld_x, int half_roundtr
  * GEMMs (y = A . W^T, fp32 out)
  * ------------------------------------------------------------------------ */
 
-/* Pre-quantised linear: y (M, N) fp32 = Q(x) . W^T.
+/* Pre-quantised linear: y (M, N) fp32 = Q(x) . W^T.  M >= 64 runs on the
+ * tcgen05 tensor cores and needs mfi_lin_pq_workspace_bytes() of workspace
+ * (0 below that, where a CUDA-core GEMV runs and workspace may be NULL).
  * Replaces mxfp4v2::launch_lin_pq_v2 (src/ext/mxfp4_decode.cu:311-318), bound
  * by lin_pq() (src/ext/mxfp4_decode_binding.cpp:84-98). */
+size_t mfi_lin_pq_workspace_bytes(int M, int N, int Kp);
 int mfi_lin_pq(const uint8_t* xq, const uint8_t* xsc, const uint8_t* wp, const uint8_t* wsc,
-               float* y, int M, int N, int K, int Kp, void* stream);
+               float* y, int M, int N, int K, int Kp, void* workspace, size_t workspace_bytes,
+               void* stream);
 
 /* Linear with on-the-fly activation quantisation: x (M, ld_x) of dtype
  * MFI_* (non-half inputs rounded through fp16 like the reference binding),
@@ -83,7 +93,7 @@ int mfi_lin_pq(const uint8_t* xq, const uint8_t* xsc, const uint8_t* wp, const u
  * multiplied by the packed W (N, Kp/2)/(N, Kp/32) -> y (M, N) fp32.
  * Replaces mxfp4::launch_mxfp4_linear (src/ext/mxfp4_linear.cu:200-206),
  * bound by forward() (src/ext/mxfp4_binding.cpp:21-45). */
-size_t mfi_linear_workspace_bytes(int M, int Kp);
+size_t mfi_linear_workspace_bytes(int M, int N, int Kp);
 int mfi_mxfp4_linear(const void* x, int dtype, int ld_x, const uint8_t* wp, const uint8_t* wsc,
                      float* y, int M, int N, int Kp, void* workspace, size_t workspace_bytes,
                      void* stream);

@@ -27,8 +27,10 @@ SIGNATURES = {
     "mfi_version": (_I, []),
     "mfi_prequant": (_I, [_VP, _VP, _VP, _I, _I, _I, _VP]),
     "mfi_quantize_rows": (_I, [_VP, _I, _LL, _I, _VP, _VP, _I, _I, _I, _VP]),
-    "mfi_lin_pq": (_I, [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP]),
-    "mfi_linear_workspace_bytes": (_SZ, [_I, _I]),
+    "mfi_device_error": (_I, [_I]),
+    "mfi_lin_pq_workspace_bytes": (_SZ, [_I, _I, _I]),
+    "mfi_lin_pq": (_I, [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP, _SZ, _VP]),
+    "mfi_linear_workspace_bytes": (_SZ, [_I, _I, _I]),
     "mfi_mxfp4_linear": (_I, [_VP, _I, _I, _VP, _VP, _VP, _I, _I, _I, _VP, _SZ, _VP]),
     "mfi_moe_gateup_workspace_bytes": (_SZ, [_I, _I]),
     "mfi_moe_gateup": (_I, [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _VP, _SZ, _VP]),

@@ -47,6 +47,9 @@ struct Carve {
 };
 
 constexpr int kGemvMaxCtas = 148 * 4;
+// Rows of activations from which the tcgen05 tensor-core GEMM replaces the
+// CUDA-core GEMV (one 128-row MMA tile is then at least half used).
+constexpr int kTcMinM = 64;
 
 bool bad_ptr(const void* p) { return p == nullptr; }
 
@@ -78,22 +81,52 @@ int mfi_prequant(const void* x_bf16, uint8_t* xq, uint8_t* xsc, int M, int K, in
 }
 
 // ---------------------------------------------------------------------------
+size_t mfi_lin_pq_workspace_bytes(int M, int N, int Kp) {
+  if (M < kTcMinM) return 0;
+  Carve c(nullptr);
+  c.take<uint8_t>(mfi::sf_atoms_bytes(M, Kp, 128));
+  c.take<uint8_t>(mfi::sf_atoms_bytes(N, Kp, 256));
+  return c.used + 256;
+}
+
+// Tensor-core GEMM of pre-quantised operands: scale factors re-laid out into
+// atoms in the workspace, then one tcgen05 kernel.
+static int tc_linear(const uint8_t* xq, const uint8_t* xsc, const uint8_t* wp, const uint8_t* wsc,
+                     float* y, int M, int N, int Kp, Carve& c, cudaStream_t s) {
+  uint8_t* sfa = c.take<uint8_t>(mfi::sf_atoms_bytes(M, Kp, 128));
+  uint8_t* sfb = c.take<uint8_t>(mfi::sf_atoms_bytes(N, Kp, 256));
+  int st = cuda_status(mfi::launch_sf_atoms(xsc, Kp / 32, M, Kp, 128, sfa, s), "sf atoms (A)");
+  if (st != MFI_OK) return st;
+  st = cuda_status(mfi::launch_sf_atoms(wsc, Kp / 32, N, Kp, 256, sfb, s), "sf atoms (B)");
+  if (st != MFI_OK) return st;
+  return cuda_status(mfi::launch_tc_gemm(xq, sfa, wp, sfb, y, N, M, N, Kp,
+                                         mfi::device_error_flag(), s),
+                     "tcgen05 gemm launch");
+}
+
 int mfi_lin_pq(const uint8_t* xq, const uint8_t* xsc, const uint8_t* wp, const uint8_t* wsc,
-               float* y, int M, int N, int K, int Kp, void* stream) {
+               float* y, int M, int N, int K, int Kp, void* workspace, size_t workspace_bytes,
+               void* stream) {
   if (M < 0 || N < 0 || K < 0) return fail(MFI_ERR_ARG, "M, N, K must be non-negative");
   if (Kp <= 0 || Kp % 32 != 0) return fail(MFI_ERR_ARG, "Kp must be a positive multiple of 32");
   if (M == 0 || N == 0) return MFI_OK;
   if (bad_ptr(xq) || bad_ptr(xsc) || bad_ptr(wp) || bad_ptr(wsc) || bad_ptr(y))
     return fail(MFI_ERR_ARG, "null pointer");
-  return cuda_status(
-      mfi::launch_dense_gemv(xq, xsc, wp, wsc, y, N, M, N, Kp, as_stream(stream)), "lin_pq launch");
+  cudaStream_t s = as_stream(stream);
+  if (M >= kTcMinM && mfi::tc_gemm_supported(xq, wp, Kp)) {
+    if (bad_ptr(workspace) || workspace_bytes < mfi_lin_pq_workspace_bytes(M, N, Kp))
+      return fail(MFI_ERR_WORKSPACE, "workspace too small for lin_pq");
+    Carve c(workspace);
+    return tc_linear(xq, xsc, wp, wsc, y, M, N, Kp, c, s);
+  }
+  return cuda_status(mfi::launch_dense_gemv(xq, xsc, wp, wsc, y, N, M, N, Kp, s), "lin_pq launch");
 }
 
-size_t mfi_linear_workspace_bytes(int M, int Kp) {
+size_t mfi_linear_workspace_bytes(int M, int N, int Kp) {
   Carve c(nullptr);
   c.take<uint8_t>(size_t(M) * (Kp / 2));
   c.take<uint8_t>(size_t(M) * (Kp / 32));
-  return c.used + 256;
+  return c.used + mfi_lin_pq_workspace_bytes(M, N, Kp) + 256;
 }
 
 int mfi_mxfp4_linear(const void* x, int dtype, int ld_x, const uint8_t* wp, const uint8_t* wsc,
@@ -104,7 +137,7 @@ int mfi_mxfp4_linear(const void* x, int dtype, int ld_x, const uint8_t* wp, cons
   if (M == 0 || N == 0) return MFI_OK;
   if (bad_ptr(x) || bad_ptr(wp) || bad_ptr(wsc) || bad_ptr(y) || bad_ptr(workspace))
     return fail(MFI_ERR_ARG, "null pointer");
-  if (workspace_bytes < mfi_linear_workspace_bytes(M, Kp))
+  if (workspace_bytes < mfi_linear_workspace_bytes(M, N, Kp))
     return fail(MFI_ERR_WORKSPACE, "workspace too small for mxfp4_linear");
   Carve c(workspace);
   uint8_t* xq = c.take<uint8_t>(size_t(M) * (Kp / 2));
@@ -114,9 +147,22 @@ int mfi_mxfp4_linear(const void* x, int dtype, int ld_x, const uint8_t* wp, cons
   const int half_rt = dtype == MFI_F16 ? 0 : 1;
   int st = mfi_quantize_rows(x, dtype, ld_x, half_rt, xq, xsc, M, k_eff, Kp, stream);
   if (st != MFI_OK) return st;
-  return cuda_status(
-      mfi::launch_dense_gemv(xq, xsc, wp, wsc, y, N, M, N, Kp, as_stream(stream)),
-      "mxfp4_linear gemm launch");
+  cudaStream_t s = as_stream(stream);
+  if (M >= kTcMinM && mfi::tc_gemm_supported(xq, wp, Kp))
+    return tc_linear(xq, xsc, wp, wsc, y, M, N, Kp, c, s);
+  return cuda_status(mfi::launch_dense_gemv(xq, xsc, wp, wsc, y, N, M, N, Kp, s),
+                     "mxfp4_linear gemm launch");
+}
+
+int mfi_device_error(int clear) {
+  int v = 0;
+  if (cudaMemcpy(&v, mfi::device_error_flag(), sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return -1;
+  if (clear && v) {
+    const int z = 0;
+    cudaMemcpy(mfi::device_error_flag(), &z, sizeof(int), cudaMemcpyHostToDevice);
+  }
+  return v;
 }
 
 // ---------------------------------------------------------------------------

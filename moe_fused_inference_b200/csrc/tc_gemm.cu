@@ -1,0 +1,310 @@
+// tc_gemm.cu — tcgen05 block-scaled MXFP4 GEMM, y (M, N) fp32 = A . B^T.
+//
+// Replaces the reference's prefill GEMM mxfp4_linear_kernel
+// (src/ext/mxfp4_linear.cu:106-198: mma.sync m16n8k64 block_scale, sm_120a
+// only, one 16x32 output tile per CTA with scalar nibble gathers) with the
+// sm_100a tensor-core path:
+//
+//   * tile 128 (M) x 256 (N) x 256 (K) per stage, 4 stages in shared memory;
+//   * warp 0 (one elected thread): TMA 2-D loads of the A and B tiles
+//     (128-byte swizzle, zero fill outside the tensor) and bulk copies of the
+//     scale-factor atoms, all completing on the stage's mbarrier;
+//   * warp 1: allocates 512 TMEM columns, copies the stage's scale factors
+//     into TMEM (tcgen05.cp 32x128b.warpx4) and issues 4
+//     tcgen05.mma.kind::mxf4.block_scale (M=128, N=256, K=64) per stage, the
+//     fp32 accumulator living in TMEM columns [0, 256); tcgen05.commit frees
+//     the smem stage and, after the last stage, signals the epilogue;
+//   * warps 2-5: tcgen05.ld the accumulator (one row per thread) and store it.
+//
+// Operands are the reference's packed formats: rows of Kp/2 bytes (two E2M1
+// per byte, low nibble first — the K-major FP4 operand order), plus E8M0
+// scales re-laid out once into 512-byte atoms (see sf_atoms_kernel).
+// Every wait is bounded (2 s); on timeout the kernel records an error code in
+// the caller's flag, drains its own loads and frees TMEM before returning.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "tc_ptx.cuh"
+#include "work.cuh"
+
+namespace mfi {
+
+using namespace tc;
+
+constexpr int kBM = 128, kBN = 256, kBK = 256;  // BK in elements (128 bytes of FP4)
+constexpr int kStages = 4;
+constexpr int kABytes = kBM * kBK / 2;                       // 16 KB
+constexpr int kBBytes = kBN * kBK / 2;                       // 32 KB
+constexpr int kSFABytes = (kBM / 128) * (kBK / 128) * 512;   // 1 KB
+constexpr int kSFBBytes = (kBN / 128) * (kBK / 128) * 512;   // 2 KB
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemSFA = 256;      // 2 chunks x 4 columns
+constexpr uint32_t kTmemSFB = 256 + 8;  // 2 chunks x 2 row blocks x 4 columns
+constexpr int kGemmThreads = 192;
+
+size_t tc_gemm_smem_bytes() {
+  return 1024 + size_t(kStages) * (kABytes + kBBytes + kSFABytes + kSFBBytes) +
+         8 * (2 * kStages + 1) + 16;
+}
+
+struct TcGemmArgs {
+  int M, N, Kp;
+  int kc_pad;              // scale atoms per 128-row block along K (even)
+  const uint8_t* sfa;      // (ceil(M/128)) x kc_pad x 512
+  const uint8_t* sfb;      // (ceil(N/256)*2) x kc_pad x 512
+  float* y;
+  long long ldy;
+  int* err;
+};
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    tc_gemm_mxf4_kernel(const __grid_constant__ CUtensorMap tma_a,
+                        const __grid_constant__ CUtensorMap tma_b, TcGemmArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + kStages * kABytes;
+  uint8_t* sSFA = sB + kStages * kBBytes;
+  uint8_t* sSFB = sSFA + kStages * kSFABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sSFB + kStages * kSFBBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* accb = empty + kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tile = blockIdx.x, m_tile = blockIdx.y;
+  const int k_tiles = (p.Kp + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accb, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      prefetch_tmap(&tma_a);
+      prefetch_tmap(&tma_b);
+      int issued = 0;
+      bool ok = true;
+      for (int kt = 0; kt < k_tiles; ++kt) {
+        const int s = kt % kStages;
+        const uint32_t ph = (kt / kStages) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, p.err, 1)) { ok = false; break; }
+        mbar_expect_tx(&full[s], kABytes + kBBytes + kSFABytes + kSFBBytes);
+        tma_load_2d(sA + s * kABytes, &tma_a, kt * (kBK / 2), m_tile * kBM, &full[s]);
+        tma_load_2d(sB + s * kBBytes, &tma_b, kt * (kBK / 2), n_tile * kBN, &full[s]);
+        bulk_load(sSFA + s * kSFABytes, p.sfa + (size_t(m_tile) * p.kc_pad + 2 * kt) * 512, 1024,
+                  &full[s]);
+        bulk_load(sSFB + s * kSFBBytes, p.sfb + (size_t(2 * n_tile) * p.kc_pad + 2 * kt) * 512,
+                  1024, &full[s]);
+        bulk_load(sSFB + s * kSFBBytes + 1024,
+                  p.sfb + (size_t(2 * n_tile + 1) * p.kc_pad + 2 * kt) * 512, 1024, &full[s]);
+        issued = kt + 1;
+      }
+      if (!ok) {
+        // drain our own copies before the CTA can exit
+        for (int kt = (issued > kStages ? issued - kStages : 0); kt < issued; ++kt)
+          mbar_wait(&full[kt % kStages], (kt / kStages) & 1, nullptr, 0);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      bool ok = true;
+      for (int kt = 0; kt < k_tiles; ++kt) {
+        const int s = kt % kStages;
+        const uint32_t ph = (kt / kStages) & 1;
+        if (!mbar_wait(&full[s], ph, p.err, 2)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(sA + s * kABytes);
+        const uint32_t b_base = smem_u32(sB + s * kBBytes);
+        const uint32_t sfa_base = smem_u32(sSFA + s * kSFABytes);
+        const uint32_t sfb_base = smem_u32(sSFB + s * kSFBBytes);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          tmem_cp_sf(tmem + kTmemSFA + 4 * c, make_sdesc(sfa_base + c * 512, 0, 128, kLayoutNone));
+#pragma unroll
+          for (int rb = 0; rb < 2; ++rb)
+            tmem_cp_sf(tmem + kTmemSFB + 8 * c + 4 * rb,
+                       make_sdesc(sfb_base + rb * 1024 + c * 512, 0, 128, kLayoutNone));
+        }
+#pragma unroll
+        for (int kb = 0; kb < 4; ++kb) {
+          const int c = kb >> 1;
+          const uint32_t byte = uint32_t(kb & 1) * 2;
+          const uint64_t adesc = make_sdesc(a_base + kb * 32, 16, 1024, kLayoutSW128);
+          const uint64_t bdesc = make_sdesc(b_base + kb * 32, 16, 1024, kLayoutSW128);
+          const uint32_t idesc = make_idesc_mxf4(kBM, kBN, int(byte), int(byte));
+          const uint32_t tsfa = (tmem + kTmemSFA + 4 * c) | (byte << 30);
+          const uint32_t tsfb = (tmem + kTmemSFB + 8 * c) | (byte << 30);
+          mma_mxf4(tmem, adesc, bdesc, idesc, (kt | kb) != 0 ? 1u : 0u, tsfa, tsfb);
+        }
+        tc_commit(&empty[s]);
+      }
+      if (ok) tc_commit(accb);
+    }
+  } else {
+    const bool ok = mbar_wait(accb, 0, p.err, 3);
+    tc_fence_after();
+    if (ok) {
+      const int lane_base = (warp & 3) * 32;
+      const int row = m_tile * kBM + lane_base + lane;
+      float* yrow = p.y + (long long)row * p.ldy;
+      const bool vec = (p.ldy % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.y) & 15) == 0);
+#pragma unroll 1
+      for (int c0 = 0; c0 < kBN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem + (uint32_t(lane_base) << 16) + uint32_t(c0), r);
+        tmem_ld_wait();
+        const int col0 = n_tile * kBN + c0;
+        if (row < p.M && col0 < p.N) {
+          if (vec && col0 + 32 <= p.N) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(yrow + col0 + j) =
+                  make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                              __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < p.N) yrow[col0 + j] = __uint_as_float(r[j]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Row-major E8M0 codes (R, nb) -> 512-byte atoms.  Atom (rb, kc) holds rows
+// rb*128 .. rb*128+127 and K blocks kc*4 .. kc*4+3; inside it byte
+// (r % 32)*16 + ((r % 128) / 32)*4 + (k % 4).  This is the layout that one
+// tcgen05.cp 32x128b.warpx4 moves into the 4 TMEM columns the MMA reads for a
+// 128-row operand.  Rows >= R and blocks >= nb are filled with code 127 (1.0).
+// ---------------------------------------------------------------------------
+__global__ void sf_atoms_kernel(const uint8_t* __restrict__ src, long long src_ld, int R, int nb,
+                                int row_blocks, int kc_pad, uint8_t* __restrict__ dst) {
+  const long long total = (long long)row_blocks * kc_pad * 512;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int within = int(i & 511);
+    const long long atom = i >> 9;
+    const int kc = int(atom % kc_pad);
+    const int rb = int(atom / kc_pad);
+    const int r = rb * 128 + (within >> 4) + 32 * ((within & 15) >> 2);
+    const int k = kc * 4 + (within & 3);
+    dst[i] = (r < R && k < nb) ? src[(long long)r * src_ld + k] : uint8_t(127);
+  }
+}
+
+size_t sf_atoms_bytes(int R, int Kp, int row_align) {
+  const int rb = (R + row_align - 1) / row_align * (row_align / 128);
+  const int kc_pad = 2 * ((Kp + kBK - 1) / kBK);
+  return size_t(rb) * kc_pad * 512;
+}
+
+cudaError_t launch_sf_atoms(const uint8_t* src, long long src_ld, int R, int Kp, int row_align,
+                            uint8_t* dst, cudaStream_t stream) {
+  const int rb = (R + row_align - 1) / row_align * (row_align / 128);
+  const int kc_pad = 2 * ((Kp + kBK - 1) / kBK);
+  const long long total = (long long)rb * kc_pad * 512;
+  if (total == 0) return cudaSuccess;
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  sf_atoms_kernel<<<unsigned(blocks), 256, 0, stream>>>(src, src_ld, R, Kp / 32, rb, kc_pad, dst);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Device-wide error flag: 0 while healthy; a kernel whose bounded wait timed
+// out stores a non-zero code (1 producer, 2 MMA issuer, 3 epilogue).
+__device__ int g_device_error;
+
+int* device_error_flag() {
+  static int* addr[64] = {nullptr};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+    addr[dev] = static_cast<int*>(p);
+  }
+  return addr[dev];
+}
+
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D uint8 tensor (rows x row_bytes, row stride row_bytes), box 128 bytes x box_rows,
+// 128-byte swizzle, zero fill outside the tensor.
+static bool make_tmap(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows,
+                      uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {row_bytes, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool tc_gemm_supported(const void* a, const void* b, int Kp) {
+  return (reinterpret_cast<uintptr_t>(a) % 16 == 0) && (reinterpret_cast<uintptr_t>(b) % 16 == 0) &&
+         (Kp % 32 == 0) && Kp > 0;
+}
+
+cudaError_t launch_tc_gemm(const uint8_t* a, const uint8_t* sfa_atoms, const uint8_t* b,
+                           const uint8_t* sfb_atoms, float* y, long long ldy, int M, int N, int Kp,
+                           int* err, cudaStream_t stream) {
+  if (M == 0 || N == 0) return cudaSuccess;
+  CUtensorMap ta, tb;
+  if (!make_tmap(&ta, a, uint64_t(Kp / 2), uint64_t(M), kBM) ||
+      !make_tmap(&tb, b, uint64_t(Kp / 2), uint64_t(N), kBN))
+    return cudaErrorInvalidValue;
+  static bool attr_set = false;
+  const size_t smem = tc_gemm_smem_bytes();
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_mxf4_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  TcGemmArgs p;
+  p.M = M; p.N = N; p.Kp = Kp;
+  p.kc_pad = 2 * ((Kp + kBK - 1) / kBK);
+  p.sfa = sfa_atoms; p.sfb = sfb_atoms; p.y = y; p.ldy = ldy; p.err = err;
+  dim3 grid((N + kBN - 1) / kBN, (M + kBM - 1) / kBM);
+  tc_gemm_mxf4_kernel<<<grid, kGemmThreads, smem, stream>>>(ta, tb, p);
+  return cudaGetLastError();
+}
+
+}  // namespace mfi

@@ -72,4 +72,17 @@ cudaError_t launch_combine(const float* yd, long ystride, const float* w, int E,
                            float* out, int M, int N, cudaStream_t stream);
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t stream);
 
+// tcgen05 MXFP4 GEMM (tc_gemm.cu)
+size_t tc_gemm_smem_bytes();
+bool tc_gemm_supported(const void* a, const void* b, int Kp);
+size_t sf_atoms_bytes(int R, int Kp, int row_align);
+cudaError_t launch_sf_atoms(const uint8_t* src, long long src_ld, int R, int Kp, int row_align,
+                            uint8_t* dst, cudaStream_t stream);
+cudaError_t launch_tc_gemm(const uint8_t* a, const uint8_t* sfa_atoms, const uint8_t* b,
+                           const uint8_t* sfb_atoms, float* y, long long ldy, int M, int N, int Kp,
+                           int* err, cudaStream_t stream);
+
+// Device-wide error flag written by kernels whose bounded waits time out.
+int* device_error_flag();
+
 }  // namespace mfi

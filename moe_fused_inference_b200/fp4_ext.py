@@ -108,7 +108,7 @@ class _LinearExt:
         y = torch.empty((M, N), dtype=torch.float32, device=x.device)
         if M == 0 or N == 0:
             return y
-        ws = _workspace(lib.mfi_linear_workspace_bytes(M, Kp), x.device)
+        ws = _workspace(lib.mfi_linear_workspace_bytes(M, N, Kp), x.device)
         st = lib.mfi_mxfp4_linear(_ptr(x), _DTYPE[x.dtype], K, _ptr(wp), _ptr(wsc), _ptr(y),
                                   M, N, Kp, _ptr(ws), ws.numel(), _stream(x.device))
         _lib.check(st, "forward")
@@ -152,8 +152,9 @@ class _DecodeExt:
         _check(xq.shape[0] >= M, "xq has fewer than M rows")
         y = torch.empty((M, N), dtype=torch.float32, device=xq.device)
         if M and N:
+            ws = _workspace(lib.mfi_lin_pq_workspace_bytes(M, N, Kp), xq.device)
             _lib.check(lib.mfi_lin_pq(_ptr(xq), _ptr(xsc), _ptr(wp), _ptr(wsc), _ptr(y), M, N, K, Kp,
-                                      _stream(xq.device)), "lin_pq")
+                                      _ptr(ws), ws.numel(), _stream(xq.device)), "lin_pq")
         return y
 
     @staticmethod

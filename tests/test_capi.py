@@ -46,14 +46,14 @@ def test_workspace_queries_are_pure_host(lib):
     assert lib.mfi_version() == 1
     assert lib.mfi_moe_layer_workspace_bytes(64, 2048, 768, 128, 8) > 64 * 8 * 2048 * 4
     assert lib.mfi_moe_gateup_workspace_bytes(8, 1) >= 16 * (24 + 16)
-    assert lib.mfi_linear_workspace_bytes(16, 2048) >= 16 * (1024 + 64)
+    assert lib.mfi_linear_workspace_bytes(16, 256, 2048) >= 16 * (1024 + 64)
 
 
 def test_argument_errors_report_status_and_message(lib):
     st = lib.mfi_quantize_rows(None, 9, 0, 0, None, None, 1, 32, 32, None)
     assert st == 1
     assert b"dtype" in lib.mfi_last_error()
-    st = lib.mfi_lin_pq(None, None, None, None, None, 1, 8, 64, 48, None)
+    st = lib.mfi_lin_pq(None, None, None, None, None, 1, 8, 64, 48, None, 0, None)
     assert st == 1 and b"Kp" in lib.mfi_last_error()
     with pytest.raises(_lib.MfiError):
         _lib.check(lib.mfi_moe_combine(None, 4, None, 0, None, 1, 4, None), "moe_combine")
