@@ -98,6 +98,22 @@ int mfi_mxfp4_linear(const void* x, int dtype, int ld_x, const uint8_t* wp, cons
                      float* y, int M, int N, int Kp, void* workspace, size_t workspace_bytes,
                      void* stream);
 
+/* Allocation-free mxfp4_linear (no counterpart in the reference: its
+ * bindings always allocate through torch).  For callers that cannot allocate
+ * device memory — a plugin whose host program owns all GPU memory, an FFI
+ * caller without the framework's allocator, a hot path that must not call
+ * cudaMalloc — the scratch of mfi_mxfp4_linear comes from a 4 MiB static
+ * device array inside the library instead of a caller workspace.  Same
+ * arguments and results as mfi_mxfp4_linear minus the workspace.  Shapes with
+ * mfi_linear_workspace_bytes(M, N, Kp) > 4 MiB are rejected with
+ * MFI_ERR_WORKSPACE.  The first call on each device looks up the array's
+ * device address and should happen before any stream capture.  All calls on
+ * a device share the array (it keeps the last call's contents; nothing needs
+ * to start at zero), so calls that overlap on the GPU race: serialise them.
+ * Allocates nothing (no cudaMalloc, cudaFree or allocating library call). */
+int mfi_mxfp4_linear_noalloc(const void* x, int dtype, int ld_x, const uint8_t* wp,
+                             const uint8_t* wsc, float* y, int M, int N, int Kp, void* stream);
+
 /* ------------------------------------------------------------------------
  * Grouped MoE operators behind device pointer tables
  * ------------------------------------------------------------------------ */

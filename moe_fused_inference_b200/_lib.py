@@ -32,6 +32,7 @@ SIGNATURES = {
     "mfi_lin_pq": (_I, [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP, _SZ, _VP]),
     "mfi_linear_workspace_bytes": (_SZ, [_I, _I, _I]),
     "mfi_mxfp4_linear": (_I, [_VP, _I, _I, _VP, _VP, _VP, _I, _I, _I, _VP, _SZ, _VP]),
+    "mfi_mxfp4_linear_noalloc": (_I, [_VP, _I, _I, _VP, _VP, _VP, _I, _I, _I, _VP]),
     "mfi_moe_gateup_workspace_bytes": (_SZ, [_I, _I]),
     "mfi_moe_gateup": (_I, [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _VP, _SZ, _VP]),
     "mfi_moe_down_workspace_bytes": (_SZ, [_I, _I, _I]),

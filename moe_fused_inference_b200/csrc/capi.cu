@@ -55,6 +55,10 @@ bool bad_ptr(const void* p) { return p == nullptr; }
 
 }  // namespace
 
+namespace mfi {
+int set_last_error(int code, const char* msg) { return fail(code, msg); }
+}  // namespace mfi
+
 extern "C" {
 
 const char* mfi_last_error(void) { return g_err.c_str(); }

@@ -85,4 +85,7 @@ cudaError_t launch_tc_gemm(const uint8_t* a, const uint8_t* sfa_atoms, const uin
 // Device-wide error flag written by kernels whose bounded waits time out.
 int* device_error_flag();
 
+// Record a message for mfi_last_error() on this host thread; returns code.
+int set_last_error(int code, const char* msg);
+
 }  // namespace mfi
