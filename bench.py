@@ -289,9 +289,9 @@ def run_ours(args, world, rank, local):
     tokens = T * N_LAYERS * args.steps * world
     value = tokens / (ms_max / 1e3)
 
-    # ---- roofline of the dominant kernel (grouped GEMV: gate/up + down) ----
+    # ---- roofline of the dominant kernel (tensor-core expert GEMMs: gate/up + down) ----
     peak, peak_kind = measured_peaks()
-    gemv_ms = stage[1] + stage[3]  # per step, summed over the 48 layer calls
+    gemv_ms = stage[2] + stage[3]  # per step, summed over the 48 layer calls
     w_bytes = uniq * EXPERT_BYTES  # per step
     achieved = w_bytes / (gemv_ms / 1e3) / 1e9
     layer_ms = sum(stage)
@@ -330,8 +330,8 @@ def run_ours(args, world, rank, local):
                    "global_batch": T * world, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2: 48 distinct layer weight sets (15.4 GB) per step",
                    "unique_experts_per_layer": uniq / N_LAYERS},
-        "gpu_launches": 6 * N_LAYERS * args.steps,
-        "roofline": {"bound": "hbm", "kernel": "grouped_gemv_kernel (gate/up + down launches)",
+        "gpu_launches": 6 * N_LAYERS * args.steps,  # quant, route, gather, gate/up, down, combine
+        "roofline": {"bound": "hbm", "kernel": "moe_tc_kernel (gate/up + down launches)",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind,
                      "algorithmic_bytes_per_step": w_bytes,
@@ -340,7 +340,7 @@ def run_ours(args, world, rank, local):
                      "layer": {"achieved": layer_bytes / (layer_ms / 1e3) / 1e9,
                                "frac": layer_bytes / (layer_ms / 1e3) / 1e9 / peak,
                                "stage_ms_per_step": dict(zip(
-                                   ["route", "gate_up", "swiglu", "down", "combine"], stage))}},
+                                   ["route", "gather", "gate_up", "down", "combine"], stage))}},
         "e2e": {"value": e2e_value, "unit": "tokens/s",
                 "h2d_bytes_per_step": int(Xh.numel() * Xh.element_size()),
                 "d2h_bytes_per_step": int(Oh.numel() * Oh.element_size())},

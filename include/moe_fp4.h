@@ -168,7 +168,17 @@ typedef struct mfi_moe_weights {
   int hidden;               /* multiple of 32, <= 4096                */
   int inter;                /* multiple of 32                         */
   int top_k;                /* 1..min(E, 32)                          */
+  const void* prepared;     /* scale atoms from mfi_moe_prepare, or NULL */
 } mfi_moe_weights;
+
+/* Tensor-core form of the layer's expert scales.  When hidden and inter are
+ * multiples of 256, mfi_moe_layer runs its expert GEMMs on the tcgen05 tensor
+ * cores and needs `prepared`: a caller-owned buffer of
+ * mfi_moe_prepared_bytes() filled once per weight set by mfi_moe_prepare (the
+ * E8M0 scales re-laid out into the 512-byte atoms the MMA reads).  Other
+ * shapes use a CUDA-core path and ignore it. */
+size_t mfi_moe_prepared_bytes(int n_experts, int hidden, int inter);
+int mfi_moe_prepare(const mfi_moe_weights* w, void* prepared, size_t prepared_bytes, void* stream);
 
 /* x: bf16 (T, hidden) -> out fp32 (T, hidden); topi int32 (T, top_k) and
  * topw fp32 (T, top_k) receive the routing; logits fp32 (T, E) may be NULL.
@@ -179,9 +189,11 @@ int mfi_moe_layer(const mfi_moe_weights* w, const void* x_bf16, int T, float* ou
                   void* stream);
 
 /* As mfi_moe_layer, recording six caller-created cudaEvent_t (passed as void*)
- * on the stream at the stage boundaries: [0] start, [1] after routing,
- * [2] after the gate/up GEMV, [3] after SwiGLU requantisation, [4] after the
- * down GEMV, [5] after the combine — per-kernel timing for benchmarks. */
+ * on the stream at the stage boundaries, for per-kernel timing:
+ * tensor-core shapes: [0] start, [1] after quantise + route, [2] after the
+ * chunk gather, [3] after gate/up (+ SwiGLU requant), [4] after down,
+ * [5] after the combine; other shapes: [2] after the gate/up GEMV, [3] after
+ * SwiGLU requantisation, [4] after the down GEMV. */
 int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float* out,
                      int32_t* topi, float* topw, float* logits, void* workspace,
                      size_t workspace_bytes, void* const* events, int n_events, void* stream);

@@ -267,6 +267,7 @@ struct LayerScratch {
   int* n_gu;
   int* n_dn;
   int* n_active;
+  int* n_chunks;
   uint8_t* xq;
   uint8_t* xsc;
   float* logits;
@@ -274,21 +275,35 @@ struct LayerScratch {
   mfi::EntryDesc* e_gu;
   mfi::GroupDesc* g_dn;
   mfi::EntryDesc* e_dn;
+  mfi::ChunkDesc* chunks;
+  int* perm;
   float* gu;
   uint8_t* hq;
   uint8_t* hsc;
+  uint8_t* xp;
+  uint8_t* xp_atoms;
+  uint8_t* hp;
+  uint8_t* hp_atoms;
   float* yd;
+  int max_chunks;
   size_t bytes;
 };
+
+// Expert GEMMs on tensor cores when the tile shapes divide the layer.
+bool layer_uses_tc(int H, int Mi) { return H % 256 == 0 && Mi % 256 == 0; }
 
 LayerScratch carve_layer(void* ws, int T, int H, int Mi, int E, int k) {
   Carve c(ws);
   LayerScratch s;
   const size_t P = size_t(T) * k;
+  const bool tc = layer_uses_tc(H, Mi);
+  s.max_chunks = int((size_t(E) < P ? size_t(E) : P) + (P + 31) / 32);
+  const size_t rows = size_t(s.max_chunks) * 32;
   s.done = c.take<unsigned>(1);
   s.n_gu = c.take<int>(1);
   s.n_dn = c.take<int>(1);
   s.n_active = c.take<int>(1);
+  s.n_chunks = c.take<int>(1);
   s.xq = c.take<uint8_t>(size_t(T) * (H / 2));
   s.xsc = c.take<uint8_t>(size_t(T) * (H / 32));
   s.logits = c.take<float>(size_t(T) * E);
@@ -296,14 +311,45 @@ LayerScratch carve_layer(void* ws, int T, int H, int Mi, int E, int k) {
   s.e_gu = c.take<mfi::EntryDesc>(2 * P);
   s.g_dn = c.take<mfi::GroupDesc>(size_t(E));
   s.e_dn = c.take<mfi::EntryDesc>(P);
-  s.gu = c.take<float>(P * 2 * Mi);
-  s.hq = c.take<uint8_t>(P * (Mi / 2));
-  s.hsc = c.take<uint8_t>(P * (Mi / 32));
+  s.chunks = c.take<mfi::ChunkDesc>(size_t(s.max_chunks));
+  s.perm = c.take<int>(rows);
+  if (tc) {
+    s.gu = nullptr;
+    s.hq = s.hsc = nullptr;
+    s.xp = c.take<uint8_t>(rows * (H / 2));
+    s.xp_atoms = c.take<uint8_t>(size_t(s.max_chunks) * (H / 128) * 512);
+    s.hp = c.take<uint8_t>(rows * (Mi / 2));
+    s.hp_atoms = c.take<uint8_t>(size_t(s.max_chunks) * (Mi / 128) * 512);
+  } else {
+    s.gu = c.take<float>(P * 2 * Mi);
+    s.hq = c.take<uint8_t>(P * (Mi / 2));
+    s.hsc = c.take<uint8_t>(P * (Mi / 32));
+    s.xp = s.xp_atoms = s.hp = s.hp_atoms = nullptr;
+  }
   s.yd = c.take<float>(P * H);
   s.bytes = c.used + 256;
   return s;
 }
 }  // namespace
+
+size_t mfi_moe_prepared_bytes(int n_experts, int hidden, int inter) {
+  if (!layer_uses_tc(hidden, inter)) return 0;
+  return mfi::moe_prepared_bytes(n_experts, hidden, inter);
+}
+
+int mfi_moe_prepare(const mfi_moe_weights* w, void* prepared, size_t prepared_bytes,
+                    void* stream) {
+  if (!w) return fail(MFI_ERR_ARG, "null weights");
+  const int E = w->n_experts, H = w->hidden, Mi = w->inter;
+  if (!layer_uses_tc(H, Mi)) return MFI_OK;
+  if (bad_ptr(prepared) || bad_ptr(w->gate_sc) || bad_ptr(w->up_sc) || bad_ptr(w->down_sc))
+    return fail(MFI_ERR_ARG, "null pointer");
+  if (prepared_bytes < mfi::moe_prepared_bytes(E, H, Mi))
+    return fail(MFI_ERR_WORKSPACE, "prepared buffer smaller than mfi_moe_prepared_bytes()");
+  return cuda_status(mfi::launch_moe_prepare(w->gate_sc, w->up_sc, w->down_sc, E, H, Mi,
+                                             static_cast<uint8_t*>(prepared), as_stream(stream)),
+                     "moe_prepare launch");
+}
 
 size_t mfi_moe_layer_workspace_bytes(int T, int hidden, int inter, int n_experts, int top_k) {
   return carve_layer(nullptr, T, hidden, inter, n_experts, top_k).bytes;
@@ -358,22 +404,47 @@ int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float*
   ra.down_wp = w->down_wp; ra.down_sc = w->down_sc; ra.Mi = Mi;
   ra.g_gu = s.g_gu; ra.e_gu = s.e_gu; ra.n_gu = s.n_gu;
   ra.g_dn = s.g_dn; ra.e_dn = s.e_dn; ra.n_dn = s.n_dn; ra.n_active = s.n_active;
+  ra.chunks = s.chunks; ra.n_chunks = s.n_chunks; ra.perm = s.perm;
   rc = cuda_status(mfi::launch_route(ra, st), "moe_layer route launch");
   if (rc != MFI_OK || (rc = mark(1)) != MFI_OK) return rc;
   const int P = T * k;
-  const int max_groups = E < P ? E : P;
-  rc = cuda_status(mfi::launch_grouped_gemv(s.g_gu, s.n_gu, 2 * max_groups, s.e_gu, s.xq, s.xsc,
-                                            s.gu, Mi, H, kGemvMaxCtas, st),
-                   "moe_layer gate/up launch");
-  if (rc != MFI_OK || (rc = mark(2)) != MFI_OK) return rc;
-  rc = cuda_status(mfi::launch_swiglu_quant(s.gu, 2L * Mi, nullptr, P, nullptr, s.hq, s.hsc, Mi,
-                                            Mi, st),
-                   "moe_layer swiglu launch");
-  if (rc != MFI_OK || (rc = mark(3)) != MFI_OK) return rc;
-  rc = cuda_status(mfi::launch_grouped_gemv(s.g_dn, s.n_dn, max_groups, s.e_dn, s.hq, s.hsc, s.yd,
-                                            H, Mi, kGemvMaxCtas, st),
-                   "moe_layer down launch");
-  if (rc != MFI_OK || (rc = mark(4)) != MFI_OK) return rc;
+  if (layer_uses_tc(H, Mi)) {
+    if (bad_ptr(w->prepared)) return fail(MFI_ERR_ARG, "weights.prepared is null (mfi_moe_prepare)");
+    rc = cuda_status(mfi::launch_gather_chunks(s.xq, s.xsc, s.perm, s.n_chunks, s.max_chunks, k, H,
+                                               s.xp, s.xp_atoms, st),
+                     "moe_layer gather launch");
+    if (rc != MFI_OK || (rc = mark(2)) != MFI_OK) return rc;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    mfi::MoeTcLaunch L{};
+    L.E = E; L.H = H; L.Mi = Mi; L.max_chunks = s.max_chunks; L.grid = sms;
+    L.gate_wp = w->gate_wp; L.up_wp = w->up_wp; L.down_wp = w->down_wp;
+    L.prepared = static_cast<const uint8_t*>(w->prepared);
+    L.chunks = s.chunks; L.n_chunks = s.n_chunks; L.perm = s.perm;
+    L.xp = s.xp; L.xp_atoms = s.xp_atoms; L.hp = s.hp; L.hp_atoms = s.hp_atoms; L.yd = s.yd;
+    L.err = mfi::device_error_flag();
+    L.gate_up = true;
+    rc = cuda_status(mfi::launch_moe_tc(L, st), "moe_layer gate/up (tensor cores) launch");
+    if (rc != MFI_OK || (rc = mark(3)) != MFI_OK) return rc;
+    L.gate_up = false;
+    rc = cuda_status(mfi::launch_moe_tc(L, st), "moe_layer down (tensor cores) launch");
+    if (rc != MFI_OK || (rc = mark(4)) != MFI_OK) return rc;
+  } else {
+    const int max_groups = E < P ? E : P;
+    rc = cuda_status(mfi::launch_grouped_gemv(s.g_gu, s.n_gu, 2 * max_groups, s.e_gu, s.xq, s.xsc,
+                                              s.gu, Mi, H, kGemvMaxCtas, st),
+                     "moe_layer gate/up launch");
+    if (rc != MFI_OK || (rc = mark(2)) != MFI_OK) return rc;
+    rc = cuda_status(mfi::launch_swiglu_quant(s.gu, 2L * Mi, nullptr, P, nullptr, s.hq, s.hsc, Mi,
+                                              Mi, st),
+                     "moe_layer swiglu launch");
+    if (rc != MFI_OK || (rc = mark(3)) != MFI_OK) return rc;
+    rc = cuda_status(mfi::launch_grouped_gemv(s.g_dn, s.n_dn, max_groups, s.e_dn, s.hq, s.hsc,
+                                              s.yd, H, Mi, kGemvMaxCtas, st),
+                     "moe_layer down launch");
+    if (rc != MFI_OK || (rc = mark(4)) != MFI_OK) return rc;
+  }
   rc = cuda_status(mfi::launch_combine(s.yd, H, topw, k, k, out, T, H, st),
                    "moe_layer combine launch");
   if (rc != MFI_OK) return rc;

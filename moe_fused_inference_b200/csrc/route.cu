@@ -133,6 +133,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   __shared__ int s_off[kMaxE];
   __shared__ int s_act[kMaxE];  // active index of expert e, or -1
   __shared__ int s_cur[kMaxE];
+  __shared__ int s_cbase[kMaxE];  // first chunk of expert e
   const int P = a.T * a.k;
   for (int e = threadIdx.x; e < a.E; e += blockDim.x) { s_cnt[e] = 0; s_cur[e] = 0; }
   __syncthreads();
@@ -140,28 +141,33 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   __syncthreads();
   if (warp == 0) {
     // exclusive scans of counts and of "active" flags over E <= 256 experts
-    int run_off = 0, run_act = 0;
+    int run_off = 0, run_act = 0, run_ch = 0;
     for (int e0 = 0; e0 < a.E; e0 += 32) {
       const int e = e0 + lane;
       const int c = e < a.E ? s_cnt[e] : 0;
-      int inc = c, act = c > 0 ? 1 : 0;
+      const int nch = (c + 31) / 32;
+      int inc = c, act = c > 0 ? 1 : 0, ch = nch;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
         const int v = __shfl_up_sync(0xffffffffu, inc, off);
         const int w = __shfl_up_sync(0xffffffffu, act, off);
-        if (lane >= off) { inc += v; act += w; }
+        const int x = __shfl_up_sync(0xffffffffu, ch, off);
+        if (lane >= off) { inc += v; act += w; ch += x; }
       }
       if (e < a.E) {
         s_off[e] = run_off + inc - c;
         s_act[e] = c > 0 ? run_act + act - 1 : -1;
+        s_cbase[e] = run_ch + ch - nch;
       }
       run_off += __shfl_sync(0xffffffffu, inc, 31);
       run_act += __shfl_sync(0xffffffffu, act, 31);
+      run_ch += __shfl_sync(0xffffffffu, ch, 31);
     }
     if (lane == 0) {
       *a.n_gu = 2 * run_act;
       *a.n_dn = run_act;
       *a.n_active = run_act;
+      if (a.n_chunks) *a.n_chunks = run_ch;
       *a.done = 0u;  // ready for the next call
     }
   }
@@ -182,10 +188,21 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
     g.first = first;
     g.wp = a.down_wp + e * dstride; g.wsc = a.down_sc + e * dsstride;
     a.g_dn[ai] = g;
+    if (a.chunks) {
+      for (int c = 0; c * 32 < cnt; ++c) {
+        ChunkDesc cd;
+        cd.expert = e;
+        cd.count = min(32, cnt - 32 * c);
+        a.chunks[s_cbase[e] + c] = cd;
+        for (int r = cd.count; r < 32; ++r) a.perm[(s_cbase[e] + c) * 32 + r] = -1;
+      }
+    }
   }
   for (int i = threadIdx.x; i < P; i += blockDim.x) {
     const int e = __ldcg(a.topi + i);
-    const int pos = s_off[e] + atomicAdd(&s_cur[e], 1);
+    const int pil = atomicAdd(&s_cur[e], 1);  // position in expert e's list
+    const int pos = s_off[e] + pil;
+    if (a.perm) a.perm[(s_cbase[e] + pil / 32) * 32 + pil % 32] = i;
     EntryDesc d;
     d.pad = 0;
     d.act_row = i / a.k;

@@ -25,6 +25,7 @@
 #include <cudaTypedefs.h>
 
 #include "tc_ptx.cuh"
+#include "tmap.cuh"
 #include "work.cuh"
 
 namespace mfi {
@@ -246,35 +247,6 @@ int* device_error_flag() {
     addr[dev] = static_cast<int*>(p);
   }
   return addr[dev];
-}
-
-// ---------------------------------------------------------------------------
-static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    cudaDriverEntryPointQueryResult q;
-    void* p = nullptr;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
-// 2-D uint8 tensor (rows x row_bytes, row stride row_bytes), box 128 bytes x box_rows,
-// 128-byte swizzle, zero fill outside the tensor.
-static bool make_tmap(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows,
-                      uint32_t box_rows) {
-  auto fn = encode_fn();
-  if (!fn) return false;
-  cuuint64_t dims[2] = {row_bytes, rows};
-  cuuint64_t strides[1] = {row_bytes};
-  cuuint32_t box[2] = {128, box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 bool tc_gemm_supported(const void* a, const void* b, int Kp) {

@@ -31,6 +31,12 @@ struct QuantArgs {
   int M, K, Kp;
 };
 
+// Up to 32 tokens routed to one expert (one MMA N-tile of the decode path).
+struct ChunkDesc {
+  int expert;
+  int count;
+};
+
 struct RouteArgs {
   const uint8_t* xq;   // (T, H/2)
   const uint8_t* xsc;  // (T, H/32)
@@ -48,6 +54,10 @@ struct RouteArgs {
   GroupDesc* g_gu; EntryDesc* e_gu; int* n_gu;   // 2 groups per active expert
   GroupDesc* g_dn; EntryDesc* e_dn; int* n_dn;   // 1 group per active expert
   int* n_active;
+  // tensor-core decode path: 32-token chunks per expert
+  ChunkDesc* chunks;   // [max_chunks]
+  int* n_chunks;
+  int* perm;           // [max_chunks * 32]: chunk row -> pair index, -1 padding
 };
 
 constexpr int kRouteMaxE = 256;
@@ -81,6 +91,27 @@ cudaError_t launch_sf_atoms(const uint8_t* src, long long src_ld, int R, int Kp,
 cudaError_t launch_tc_gemm(const uint8_t* a, const uint8_t* sfa_atoms, const uint8_t* b,
                            const uint8_t* sfb_atoms, float* y, long long ldy, int M, int N, int Kp,
                            int* err, cudaStream_t stream);
+
+// Decode expert GEMMs on tensor cores (moe_tc.cu).
+struct MoeTcLaunch {
+  bool gate_up;
+  int E, H, Mi, max_chunks, grid;
+  const uint8_t* gate_wp; const uint8_t* up_wp; const uint8_t* down_wp;
+  const uint8_t* prepared;           // scale atoms from launch_moe_prepare
+  const ChunkDesc* chunks; const int* n_chunks; const int* perm;
+  const uint8_t* xp; const uint8_t* xp_atoms;   // gathered chunk activations
+  uint8_t* hp; uint8_t* hp_atoms;               // requantised h (gate/up output)
+  float* yd;                                    // per-pair down output
+  int* err;
+};
+size_t moe_prepared_bytes(int E, int H, int Mi);
+cudaError_t launch_moe_prepare(const uint8_t* gate_sc, const uint8_t* up_sc,
+                               const uint8_t* down_sc, int E, int H, int Mi, uint8_t* prepared,
+                               cudaStream_t stream);
+cudaError_t launch_gather_chunks(const uint8_t* xq, const uint8_t* xsc, const int* perm,
+                                 const int* n_chunks, int max_chunks, int k, int H, uint8_t* xp,
+                                 uint8_t* xp_atoms, cudaStream_t stream);
+cudaError_t launch_moe_tc(const MoeTcLaunch& L, cudaStream_t stream);
 
 // Device-wide error flag written by kernels whose bounded waits time out.
 int* device_error_flag();

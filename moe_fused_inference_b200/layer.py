@@ -141,12 +141,22 @@ class MoELayer:
             raise RuntimeError("top_k must be in [1, min(E, 32)]")
         self.w = weights
         self.top_k = top_k
+        lib = _lib.load()
         self._cw = _lib.MoEWeights(
             weights.gate_wp.data_ptr(), weights.gate_sc.data_ptr(),
             weights.up_wp.data_ptr(), weights.up_sc.data_ptr(),
             weights.down_wp.data_ptr(), weights.down_sc.data_ptr(),
             weights.router_wp.data_ptr(), weights.router_sc.data_ptr(),
-            weights.n_experts, weights.hidden, weights.inter, top_k)
+            weights.n_experts, weights.hidden, weights.inter, top_k, None)
+        # tensor-core scale atoms, built once per weight set (mfi_moe_prepare)
+        nprep = int(lib.mfi_moe_prepared_bytes(weights.n_experts, weights.hidden, weights.inter))
+        self.prepared = None
+        if nprep:
+            dev = weights.gate_wp.device
+            self.prepared = torch.empty(nprep, dtype=torch.uint8, device=dev)
+            self._cw.prepared = self.prepared.data_ptr()
+            _lib.check(lib.mfi_moe_prepare(ctypes.byref(self._cw), self.prepared.data_ptr(), nprep,
+                                           _stream(dev)), "moe_prepare")
         self._ws = {}
 
     def workspace_bytes(self, T: int) -> int:
