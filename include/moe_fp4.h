@@ -171,12 +171,14 @@ typedef struct mfi_moe_weights {
   const void* prepared;     /* scale atoms from mfi_moe_prepare, or NULL */
 } mfi_moe_weights;
 
-/* Tensor-core form of the layer's expert scales.  When hidden and inter are
+/* Tensor-core form of the layer's expert weights.  When hidden and inter are
  * multiples of 256, mfi_moe_layer runs its expert GEMMs on the tcgen05 tensor
  * cores and needs `prepared`: a caller-owned buffer of
- * mfi_moe_prepared_bytes() filled once per weight set by mfi_moe_prepare (the
- * E8M0 scales re-laid out into the 512-byte atoms the MMA reads).  Other
- * shapes use a CUDA-core path and ignore it. */
+ * mfi_moe_prepared_bytes() (the size of the packed expert weights and scales)
+ * filled once per weight set by mfi_moe_prepare — the weights cut into
+ * per-stage 128-row x 256-K blocks stored in shared-memory order with their
+ * E8M0 scale atoms, so each pipeline stage is one contiguous bulk copy.
+ * Other shapes use a CUDA-core path and ignore it. */
 size_t mfi_moe_prepared_bytes(int n_experts, int hidden, int inter);
 int mfi_moe_prepare(const mfi_moe_weights* w, void* prepared, size_t prepared_bytes, void* stream);
 

@@ -268,6 +268,7 @@ struct LayerScratch {
   int* n_dn;
   int* n_active;
   int* n_chunks;
+  int* cursor;
   uint8_t* xq;
   uint8_t* xsc;
   float* logits;
@@ -286,6 +287,7 @@ struct LayerScratch {
   uint8_t* hp_atoms;
   float* yd;
   int max_chunks;
+  int T_pad;
   size_t bytes;
 };
 
@@ -298,8 +300,11 @@ LayerScratch carve_layer(void* ws, int T, int H, int Mi, int E, int k) {
   const size_t P = size_t(T) * k;
   const bool tc = layer_uses_tc(H, Mi);
   s.max_chunks = int((size_t(E) < P ? size_t(E) : P) + (P + 31) / 32);
-  const size_t rows = size_t(s.max_chunks) * 32;
-  s.done = c.take<unsigned>(1);
+  s.T_pad = (T + 31) / 32 * 32;
+  const size_t rows = size_t(E) * s.T_pad;  // per-expert regions of T_pad rows
+  // completion counter and per-expert cursors: one region, zeroed per call
+  s.done = c.take<unsigned>(1 + size_t(E));
+  s.cursor = reinterpret_cast<int*>(s.done + 1);
   s.n_gu = c.take<int>(1);
   s.n_dn = c.take<int>(1);
   s.n_active = c.take<int>(1);
@@ -317,9 +322,9 @@ LayerScratch carve_layer(void* ws, int T, int H, int Mi, int E, int k) {
     s.gu = nullptr;
     s.hq = s.hsc = nullptr;
     s.xp = c.take<uint8_t>(rows * (H / 2));
-    s.xp_atoms = c.take<uint8_t>(size_t(s.max_chunks) * (H / 128) * 512);
+    s.xp_atoms = c.take<uint8_t>(rows / 32 * (H / 128) * 512);
     s.hp = c.take<uint8_t>(rows * (Mi / 2));
-    s.hp_atoms = c.take<uint8_t>(size_t(s.max_chunks) * (Mi / 128) * 512);
+    s.hp_atoms = c.take<uint8_t>(rows / 32 * (Mi / 128) * 512);
   } else {
     s.gu = c.take<float>(P * 2 * Mi);
     s.hq = c.take<uint8_t>(P * (Mi / 2));
@@ -342,11 +347,13 @@ int mfi_moe_prepare(const mfi_moe_weights* w, void* prepared, size_t prepared_by
   if (!w) return fail(MFI_ERR_ARG, "null weights");
   const int E = w->n_experts, H = w->hidden, Mi = w->inter;
   if (!layer_uses_tc(H, Mi)) return MFI_OK;
-  if (bad_ptr(prepared) || bad_ptr(w->gate_sc) || bad_ptr(w->up_sc) || bad_ptr(w->down_sc))
+  if (bad_ptr(prepared) || bad_ptr(w->gate_wp) || bad_ptr(w->gate_sc) || bad_ptr(w->up_wp) ||
+      bad_ptr(w->up_sc) || bad_ptr(w->down_wp) || bad_ptr(w->down_sc))
     return fail(MFI_ERR_ARG, "null pointer");
   if (prepared_bytes < mfi::moe_prepared_bytes(E, H, Mi))
     return fail(MFI_ERR_WORKSPACE, "prepared buffer smaller than mfi_moe_prepared_bytes()");
-  return cuda_status(mfi::launch_moe_prepare(w->gate_sc, w->up_sc, w->down_sc, E, H, Mi,
+  return cuda_status(mfi::launch_moe_prepare(w->gate_wp, w->gate_sc, w->up_wp, w->up_sc,
+                                             w->down_wp, w->down_sc, E, H, Mi,
                                              static_cast<uint8_t*>(prepared), as_stream(stream)),
                      "moe_prepare launch");
 }
@@ -385,43 +392,52 @@ int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float*
   cudaStream_t st = as_stream(stream);
   auto mark = [&](int i) -> int {
     if (!events) return MFI_OK;
-    return cuda_status(cudaEventRecord(reinterpret_cast<cudaEvent_t>(events[i]), st),
+    // While the stream is being captured into a CUDA graph an external record
+    // becomes an event node, so the stage times stay measurable on replay.
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(st, &cs);
+    const unsigned flags = cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : 0u;
+    return cuda_status(cudaEventRecordWithFlags(reinterpret_cast<cudaEvent_t>(events[i]), st, flags),
                        "moe_layer event record");
   };
   int rc = mark(0);
   if (rc != MFI_OK) return rc;
-  rc = cuda_status(cudaMemsetAsync(s.done, 0, sizeof(unsigned), st), "moe_layer memset");
+  rc = cuda_status(cudaMemsetAsync(s.done, 0, sizeof(unsigned) * (1 + size_t(E)), st),
+                   "moe_layer memset");
   if (rc != MFI_OK) return rc;
-  mfi::QuantArgs qa{x_bf16, long(H), mfi::kBF16, 0, s.xq, s.xsc, T, H, H};
-  rc = cuda_status(mfi::launch_quant_rows(qa, st), "moe_layer quantize launch");
-  if (rc != MFI_OK) return rc;
+  if ((reinterpret_cast<uintptr_t>(x_bf16) & 15) != 0)
+    return fail(MFI_ERR_ARG, "x must be 16-byte aligned");
+  const bool tc = layer_uses_tc(H, Mi);
   mfi::RouteArgs ra{};
+  ra.x = x_bf16;
   ra.xq = s.xq; ra.xsc = s.xsc; ra.wr = w->router_wp; ra.sr = w->router_sc;
   ra.T = T; ra.H = H; ra.E = E; ra.k = k;
   ra.logits = logits ? logits : s.logits;
   ra.topi = topi; ra.topw = topw; ra.done = s.done;
   ra.gate_wp = w->gate_wp; ra.gate_sc = w->gate_sc; ra.up_wp = w->up_wp; ra.up_sc = w->up_sc;
   ra.down_wp = w->down_wp; ra.down_sc = w->down_sc; ra.Mi = Mi;
-  ra.g_gu = s.g_gu; ra.e_gu = s.e_gu; ra.n_gu = s.n_gu;
-  ra.g_dn = s.g_dn; ra.e_dn = s.e_dn; ra.n_dn = s.n_dn; ra.n_active = s.n_active;
+  ra.g_gu = tc ? nullptr : s.g_gu; ra.e_gu = tc ? nullptr : s.e_gu; ra.n_gu = s.n_gu;
+  ra.g_dn = tc ? nullptr : s.g_dn; ra.e_dn = tc ? nullptr : s.e_dn; ra.n_dn = s.n_dn;
+  ra.n_active = s.n_active;
   ra.chunks = s.chunks; ra.n_chunks = s.n_chunks; ra.perm = s.perm;
+  ra.cursor = tc ? s.cursor : nullptr;
+  ra.xp = tc ? s.xp : nullptr;
+  ra.xp_atoms = tc ? s.xp_atoms : nullptr;
+  ra.T_pad = s.T_pad;
   rc = cuda_status(mfi::launch_route(ra, st), "moe_layer route launch");
   if (rc != MFI_OK || (rc = mark(1)) != MFI_OK) return rc;
   const int P = T * k;
-  if (layer_uses_tc(H, Mi)) {
+  if (tc) {
     if (bad_ptr(w->prepared)) return fail(MFI_ERR_ARG, "weights.prepared is null (mfi_moe_prepare)");
-    rc = cuda_status(mfi::launch_gather_chunks(s.xq, s.xsc, s.perm, s.n_chunks, s.max_chunks, k, H,
-                                               s.xp, s.xp_atoms, st),
-                     "moe_layer gather launch");
-    if (rc != MFI_OK || (rc = mark(2)) != MFI_OK) return rc;
+    if ((rc = mark(2)) != MFI_OK) return rc;  // the chunk rows were written by the route kernel
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     mfi::MoeTcLaunch L{};
     L.E = E; L.H = H; L.Mi = Mi; L.max_chunks = s.max_chunks; L.grid = sms;
-    L.gate_wp = w->gate_wp; L.up_wp = w->up_wp; L.down_wp = w->down_wp;
     L.prepared = static_cast<const uint8_t*>(w->prepared);
-    L.chunks = s.chunks; L.n_chunks = s.n_chunks; L.perm = s.perm;
+    L.counts = s.cursor; L.perm = s.perm;
+    L.rows = E * s.T_pad;
     L.xp = s.xp; L.xp_atoms = s.xp_atoms; L.hp = s.hp; L.hp_atoms = s.hp_atoms; L.yd = s.yd;
     L.err = mfi::device_error_flag();
     L.gate_up = true;

@@ -37,22 +37,38 @@ using namespace tc;
 
 namespace {
 
-constexpr int kStages = 8;
+#ifndef MFI_TC_STAGES
+#define MFI_TC_STAGES 8
+#endif
+#ifndef MFI_TC_CTAS_PER_SM
+#define MFI_TC_CTAS_PER_SM 1
+#endif
+constexpr int kStages = MFI_TC_STAGES;
+constexpr int kCtasPerSm = MFI_TC_CTAS_PER_SM;
 constexpr int kA = 16384;      // 128 rows x 128 B
 constexpr int kB = 4096;       // 32 rows x 128 B
 constexpr int kSF = 1024;      // two 512-byte atoms (2 x 128 K)
 constexpr int kStageBytes = kA + kB + 2 * kSF;
+// stage layout in shared memory: A (16 KB) | SFA (1 KB) | SFB (1 KB) | B (4 KB)
+constexpr int kOffSFA = kA, kOffSFB = kA + kSF, kOffB = kA + 2 * kSF;
+// prepared weight block in HBM: the A tile of one k-stage, already in the
+// 128-byte-swizzled shared-memory order, followed by its two scale atoms
+constexpr int kWBlock = kA + kSF;
 constexpr int kThreads = 192;
-constexpr uint32_t kTmemCols = 128;
-constexpr uint32_t kTmemSFA = 64;
-constexpr uint32_t kTmemSFB = 72;
+constexpr int kAccBufs = 4;     // TMEM accumulators (32 fp32 columns each)
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemSFA = kAccBufs * 32;
+constexpr uint32_t kTmemSFB = kTmemSFA + 8;
 constexpr int kChunk = 32;     // tokens per chunk (MMA N)
 
+constexpr int kMaxExperts = 256;
+constexpr int kMaxChunks = kMaxExperts + 4096 / kChunk;
+
 struct MoeTcArgs {
-  const ChunkDesc* chunks;
-  const int* n_chunks;
-  const int* perm;             // chunk row -> (token * k + slot), -1 for padding
-  const uint8_t* sfa;          // weight scale atoms
+  const int* counts;           // tokens routed to each expert (route.cu cursors)
+  int E, T_pad;
+  const int* perm;             // row -> (token * k + slot) for the rows of each expert region
+  const uint8_t* wblocks;      // prepared weight blocks [expert][tile][k-stage][kWBlock]
   const uint8_t* sfb;          // chunk scale atoms [chunk][kc_pad][512]
   int K;                       // reduction length (hidden or inter), multiple of 256
   int tiles;                   // weight tiles per chunk
@@ -72,31 +88,52 @@ __device__ __forceinline__ void named_bar_sync(int id, int n) {
 }
 
 template <bool kGateUp>
-__global__ void __launch_bounds__(kThreads, 1)
-    moe_tc_kernel(const __grid_constant__ CUtensorMap tma_a0,
-                  const __grid_constant__ CUtensorMap tma_a1,
-                  const __grid_constant__ CUtensorMap tma_b, MoeTcArgs p) {
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
+    moe_tc_kernel(const __grid_constant__ CUtensorMap tma_b, MoeTcArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* ring = smem;
-  float* su = reinterpret_cast<float*>(ring + kStages * kStageBytes);  // [64][33]
-  float* sh = su + 64 * 33;                                           // [32][65]
-  uint64_t* full = reinterpret_cast<uint64_t*>(sh + 32 * 65);
+  float* s_gu = reinterpret_cast<float*>(ring + kStages * kStageBytes);  // [2][128][33]
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_gu + 2 * 128 * 33);
   uint64_t* empty = full + kStages;
   uint64_t* acc_full = empty + kStages;
-  uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* acc_empty = acc_full + kAccBufs;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + kAccBufs);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int k_stages = p.K / 256;
+
+  // chunk table from the per-expert token counts: chunk -> (expert, c), expert
+  // e's tokens fill rows [e*T_pad, e*T_pad + count) in chunks of 32
+  __shared__ int s_cnt[kMaxExperts];
+  __shared__ int s_chunk[kMaxChunks];
+  __shared__ int s_nchunks;
+  for (int e = threadIdx.x; e < p.E; e += blockDim.x) s_cnt[e] = p.counts[e];
+  __syncthreads();
+  if (warp == 0) {
+    int run = 0;
+    for (int e0 = 0; e0 < p.E; e0 += 32) {
+      const int e = e0 + lane;
+      const int nch = e < p.E ? (s_cnt[e] + kChunk - 1) / kChunk : 0;
+      int inc = nch;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, inc, off);
+        if (lane >= off) inc += v;
+      }
+      for (int c = 0; c < nch; ++c) s_chunk[run + inc - nch + c] = e | (c << 16);
+      run += __shfl_sync(0xffffffffu, inc, 31);
+    }
+    if (lane == 0) s_nchunks = run;
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kAccBufs; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 4);
     }
@@ -107,35 +144,36 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int n_items = *p.n_chunks * p.tiles;
+  const int n_items = s_nchunks * p.tiles;
+  auto chunk_desc = [&](int chunk) {
+    ChunkDesc cd;
+    const int v = s_chunk[chunk];
+    cd.expert = v & 0xffff;
+    const int c = v >> 16;
+    cd.count = min(kChunk, s_cnt[cd.expert] - kChunk * c);
+    cd.row0 = cd.expert * p.T_pad + kChunk * c;
+    cd.pad = 0;
+    return cd;
+  };
 
   if (warp == 0) {
     if (elect_one()) {
-      prefetch_tmap(&tma_a0);
-      if (kGateUp) prefetch_tmap(&tma_a1);
       prefetch_tmap(&tma_b);
       uint32_t it = 0;
       bool ok = true;
       for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
-        const int chunk = item / p.tiles, tile = item % p.tiles;
-        const int e = p.chunks[chunk].expert;
+        const int tile = item % p.tiles;
+        const ChunkDesc cd = chunk_desc(item / p.tiles);
+        const int e = cd.expert;
         for (int ks = 0; ks < k_stages; ++ks, ++it) {
           const int s = it % kStages;
           if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, p.err, 1)) { ok = false; break; }
           uint8_t* st = ring + s * kStageBytes;
           mbar_expect_tx(&full[s], kStageBytes);
-          if (kGateUp) {
-            const int row = e * p.inter + tile * 64;
-            tma_load_2d(st, &tma_a0, ks * 128, row, &full[s]);
-            tma_load_2d(st + kA / 2, &tma_a1, ks * 128, row, &full[s]);
-          } else {
-            tma_load_2d(st, &tma_a0, ks * 128, e * p.hidden + tile * 128, &full[s]);
-          }
-          tma_load_2d(st + kA, &tma_b, ks * 128, chunk * kChunk, &full[s]);
-          const size_t arow = kGateUp ? size_t(e) * p.tiles + tile
-                                      : (size_t(e) * p.hidden + size_t(tile) * 128) / 128;
-          bulk_load(st + kA + kB, p.sfa + (arow * p.kc_pad + 2 * ks) * 512, kSF, &full[s]);
-          bulk_load(st + kA + kB + kSF, p.sfb + (size_t(chunk) * p.kc_pad + 2 * ks) * 512, kSF,
+          const size_t blk = (size_t(e) * p.tiles + tile) * k_stages + ks;
+          bulk_load(st, p.wblocks + blk * kWBlock, kWBlock, &full[s]);
+          tma_load_2d(st + kOffB, &tma_b, ks * 128, cd.row0, &full[s]);
+          bulk_load(st + kOffSFB, p.sfb + (size_t(cd.row0 / kChunk) * p.kc_pad + 2 * ks) * 512, kSF,
                     &full[s]);
         }
       }
@@ -145,8 +183,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0, acc_it = 0;
       bool ok = true;
       for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++acc_it) {
-        const uint32_t buf = acc_it & 1;
-        if (!mbar_wait(&acc_empty[buf], ((acc_it >> 1) & 1) ^ 1, p.err, 2)) { ok = false; break; }
+        const uint32_t buf = acc_it % kAccBufs;
+        if (!mbar_wait(&acc_empty[buf], ((acc_it / kAccBufs) & 1) ^ 1, p.err, 2)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d = tmem + buf * 32;
         for (int ks = 0; ks < k_stages; ++ks, ++it) {
@@ -156,16 +194,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t base = smem_u32(ring + s * kStageBytes);
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
-            tmem_cp_sf(tmem + kTmemSFA + 4 * c, make_sdesc(base + kA + kB + c * 512, 0, 128, kLayoutNone));
-            tmem_cp_sf(tmem + kTmemSFB + 4 * c,
-                       make_sdesc(base + kA + kB + kSF + c * 512, 0, 128, kLayoutNone));
+            tmem_cp_sf(tmem + kTmemSFA + 4 * c, make_sdesc(base + kOffSFA + c * 512, 0, 128, kLayoutNone));
+            tmem_cp_sf(tmem + kTmemSFB + 4 * c, make_sdesc(base + kOffSFB + c * 512, 0, 128, kLayoutNone));
           }
 #pragma unroll
           for (int kb = 0; kb < 4; ++kb) {
             const int c = kb >> 1;
             const uint32_t byte = uint32_t(kb & 1) * 2;
             mma_mxf4(d, make_sdesc(base + kb * 32, 16, 1024, kLayoutSW128),
-                     make_sdesc(base + kA + kb * 32, 16, 1024, kLayoutSW128),
+                     make_sdesc(base + kOffB + kb * 32, 16, 1024, kLayoutSW128),
                      make_idesc_mxf4(128, kChunk, int(byte), int(byte)), (ks | kb) != 0 ? 1u : 0u,
                      (tmem + kTmemSFA + 4 * c) | (byte << 30), (tmem + kTmemSFB + 4 * c) | (byte << 30));
           }
@@ -179,8 +216,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int et = threadIdx.x - 64;  // 0..127
     uint32_t acc_it = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++acc_it) {
-      const uint32_t buf = acc_it & 1;
-      if (!mbar_wait(&acc_full[buf], (acc_it >> 1) & 1, p.err, 3)) break;
+      const uint32_t buf = acc_it % kAccBufs;
+      const int chunk = item / p.tiles, tile = item % p.tiles;
+      // metadata loads issued before the wait so their latency overlaps it
+      const ChunkDesc cd = chunk_desc(chunk);
+      const int count = cd.count;
+      const int row0 = cd.row0;
+      const int my_pair = kGateUp ? 0 : p.perm[row0 + lane];
+      if (!mbar_wait(&acc_full[buf], (acc_it / kAccBufs) & 1, p.err, 3)) break;
       tc_fence_after();
       uint32_t r[32];
       tmem_ld_32x32b_x32(tmem + (uint32_t(lane_base) << 16) + buf * 32, r);
@@ -188,54 +231,72 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
-      const int chunk = item / p.tiles, tile = item % p.tiles;
-      const int count = p.chunks[chunk].count;
       if (kGateUp) {
-        if (lane_base >= 64) {
-          float* row = su + (lane_base - 64 + lane) * 33;
+        // rows 0-63 of the accumulator are gate outputs, rows 64-127 the up
+        // outputs of the same 64 columns; columns are the chunk's tokens
+        float* sg = s_gu + (acc_it & 1) * (128 * 33);
+        float* row = sg + (lane_base + lane) * 33;
 #pragma unroll
-          for (int n = 0; n < 32; ++n) row[n] = __uint_as_float(r[n]);
-        }
+        for (int n = 0; n < 32; ++n)
+          if (n < count) row[n] = __uint_as_float(r[n]);
         named_bar_sync(1, 128);
-        if (lane_base < 64) {
-          const int j = lane_base + lane;
-          const float* urow = su + j * 33;
+        // Only the chunk's `count` token columns are real: spread their
+        // count x 2 blocks of 32 outputs over the 128 threads, G threads per
+        // block (G a power of two in [2, 32]), q = 32 / G outputs per thread.
+        int G = 32;
+        while (G > 2 && 2 * count * G > 128) G >>= 1;
+        const int q = 32 / G;
+        const int task = et / G, sub = et % G;  // task = (token n, block b)
+        const int n = task >> 1, b = task & 1;
+        const bool active = n < count;          // uniform within each group of G
+        const int j0 = b * 32 + sub * q;
+        float h[16];
+        float am = 0.0f;
+        bool nan = false;
 #pragma unroll
-          for (int n = 0; n < 32; ++n) {
-            const float g = __uint_as_float(r[n]);
-            sh[n * 65 + j] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), urow[n]);
+        for (int i = 0; i < 16; ++i) {
+          h[i] = 0.0f;
+          if (active && i < q) {
+            const float g = sg[(j0 + i) * 33 + n];
+            const float u = sg[(64 + j0 + i) * 33 + n];
+            h[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+            am = fmaxf(am, fabsf(h[i]));
+            nan |= (h[i] != h[i]);
           }
         }
-        named_bar_sync(1, 128);
-        if (et < 64) {
-          const int n = et >> 1, b = et & 1;
-          if (n < count) {
-            const float* hv = sh + n * 65 + b * 32;
-            float am = 0.0f;
-            bool nan = false;
+        for (int off = 1; off < G; off <<= 1) {
+          am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+          nan |= __shfl_xor_sync(0xffffffffu, int(nan), off) != 0;
+        }
+        const BlockScale bs = block_scale(nan ? __uint_as_float(0x7fc00000u) : am);
+        uint32_t w0 = 0, w1 = 0;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              am = fmaxf(am, fabsf(hv[i]));
-              nan |= (hv[i] != hv[i]);
-            }
-            const BlockScale bs = block_scale(nan ? __uint_as_float(0x7fc00000u) : am);
-            uint32_t w[4] = {0, 0, 0, 0};
-#pragma unroll
-            for (int i = 0; i < 32; ++i) w[i >> 3] |= quant_nibble(hv[i], bs.inv) << (4 * (i & 7));
-            const int prow = chunk * kChunk + n;
-            *reinterpret_cast<uint4*>(p.hp + size_t(prow) * (p.inter / 2) + tile * 32 + b * 16) =
-                make_uint4(w[0], w[1], w[2], w[3]);
+        for (int i = 0; i < 8; ++i) {
+          if (i < q) w0 |= quant_nibble(h[i], bs.inv) << (4 * i);
+          if (8 + i < q) w1 |= quant_nibble(h[8 + i], bs.inv) << (4 * i);
+        }
+        // q = 1: pair the nibbles of neighbouring threads into one byte
+        const uint32_t nb_other = __shfl_xor_sync(0xffffffffu, w0, 1);
+        if (active) {
+          const int prow = row0 + n;
+          uint8_t* dst = p.hp + size_t(prow) * (p.inter / 2) + tile * 32 + b * 16 + (sub * q) / 2;
+          if (q == 16) *reinterpret_cast<uint2*>(dst) = make_uint2(w0, w1);
+          else if (q == 8) *reinterpret_cast<uint32_t*>(dst) = w0;
+          else if (q == 4) *reinterpret_cast<uint16_t*>(dst) = uint16_t(w0);
+          else if (q == 2) *dst = uint8_t(w0);
+          else if ((sub & 1) == 0) *dst = uint8_t(w0 | (nb_other << 4));
+          if (sub == 0) {
             const int kb = tile * 2 + b;
-            p.hp_atoms[(size_t(chunk) * (p.inter / 128) + kb / 4) * 512 + n * 16 + (kb & 3)] = bs.code;
+            p.hp_atoms[(size_t(row0 / kChunk) * (p.inter / 128) + kb / 4) * 512 + n * 16 + (kb & 3)] =
+                bs.code;
           }
         }
-        named_bar_sync(1, 128);
       } else {
         const int o = tile * 128 + lane_base + lane;
 #pragma unroll
         for (int n = 0; n < kChunk; ++n) {
-          if (n < count) {
-            const int pair = p.perm[chunk * kChunk + n];
+          if (n < count) {  // warp-uniform: columns past the chunk's tokens are skipped
+            const int pair = __shfl_sync(0xffffffffu, my_pair, n);
             p.yd[size_t(pair) * p.hidden + o] = __uint_as_float(r[n]);
           }
         }
@@ -251,8 +312,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 size_t moe_tc_smem() {
-  return 1024 + size_t(kStages) * kStageBytes + (64 * 33 + 32 * 65) * 4 +
-         8 * (2 * kStages + 4) + 16;
+  return 1024 + size_t(kStages) * kStageBytes + 2 * 128 * 33 * 4 + 8 * (2 * kStages + 2 * kAccBufs) +
+         16;
 }
 
 // ---------------------------------------------------------------------------
@@ -283,24 +344,64 @@ __global__ void __launch_bounds__(256) gather_chunks_kernel(const uint8_t* __res
   }
 }
 
-// Gate/up scale atoms for 128-row tiles made of 64 gate rows and the same 64
-// up rows: atom (e, tile, kc), rows 0-63 from gate, 64-127 from up.
-__global__ void gu_atoms_kernel(const uint8_t* __restrict__ gsc, const uint8_t* __restrict__ usc,
-                                int E, int Mi, int H, uint8_t* __restrict__ dst) {
-  const int tiles = Mi / 64, kc = H / 128, nb = H / 32;
-  const long long total = (long long)E * tiles * kc * 512;
+// Prepared weight blocks.  Block (e, tile, ks) holds rows r = 0..127 of the
+// tile (gate/up: rows 0-63 = gate rows tile*64 + r, rows 64-127 = the same up
+// rows; down: rows tile*128 + r) restricted to K elements [ks*256, ks*256+256),
+// i.e. 128 bytes per row, stored in the 128-byte-swizzle order TMA would
+// produce (16-byte chunk c of row r at r*128 + ((c ^ (r % 8)) * 16)), followed
+// by the two 512-byte scale atoms of those rows and K blocks.  One bulk copy
+// then moves a whole stage's weights and scales from contiguous HBM.
+__global__ void prepare_blocks_kernel(const uint8_t* __restrict__ wa, const uint8_t* __restrict__ sa,
+                                      const uint8_t* __restrict__ wb, const uint8_t* __restrict__ sb,
+                                      int E, int rows_per_e, int tile_rows, int K, bool paired,
+                                      uint8_t* __restrict__ dst) {
+  const int tiles = rows_per_e / tile_rows;
+  const int k_stages = K / 256;
+  const int nb = K / 32;
+  const long long n_blocks = (long long)E * tiles * k_stages;
+  const long long total = n_blocks * (kWBlock / 16);
   for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < total;
        q += (long long)gridDim.x * blockDim.x) {
-    const int within = int(q & 511);
-    const long long atom = q >> 9;
-    const int a = int(atom % kc);
-    const long long et = atom / kc;
+    const long long blk = q / (kWBlock / 16);
+    const int within = int(q % (kWBlock / 16)) * 16;  // byte offset inside the block
+    const int ks = int(blk % k_stages);
+    const long long et = blk / k_stages;
     const int tile = int(et % tiles), e = int(et / tiles);
-    const int r = (within >> 4) + 32 * ((within & 15) >> 2);
-    const int kb = a * 4 + (within & 3);
-    const uint8_t* src = r < 64 ? gsc : usc;
-    const int row = e * Mi + tile * 64 + (r & 63);
-    dst[q] = src[size_t(row) * nb + kb];
+    uint8_t* out = dst + blk * kWBlock + within;
+    if (within < kA) {
+      const int r = within >> 7;               // row inside the tile
+      const int cpos = (within >> 4) & 7;      // swizzled chunk position
+      const int c = cpos ^ (r & 7);            // logical 16-byte chunk
+      const uint8_t* w = wa;
+      int row;
+      if (paired) {
+        w = r < 64 ? wa : wb;
+        row = e * rows_per_e + tile * 64 + (r & 63);
+      } else {
+        row = e * rows_per_e + tile * 128 + r;
+      }
+      *reinterpret_cast<uint4*>(out) =
+          *reinterpret_cast<const uint4*>(w + size_t(row) * (K / 2) + ks * 128 + c * 16);
+    } else {
+      uint8_t v[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int off = within - kA + i;       // 0..1023 in the two atoms
+        const int atom = off >> 9, ob = off & 511;
+        const int r = (ob >> 4) + 32 * ((ob & 15) >> 2);
+        const int kb = (2 * ks + atom) * 4 + (ob & 3);
+        const uint8_t* sc = sa;
+        int row;
+        if (paired) {
+          sc = r < 64 ? sa : sb;
+          row = e * rows_per_e + tile * 64 + (r & 63);
+        } else {
+          row = e * rows_per_e + tile * 128 + r;
+        }
+        v[i] = sc[size_t(row) * nb + kb];
+      }
+      *reinterpret_cast<uint4*>(out) = *reinterpret_cast<const uint4*>(v);
+    }
   }
 }
 
@@ -308,18 +409,24 @@ __global__ void gu_atoms_kernel(const uint8_t* __restrict__ gsc, const uint8_t* 
 
 // ---------------------------------------------------------------------------
 size_t moe_prepared_bytes(int E, int H, int Mi) {
-  return size_t(E) * (Mi / 64) * (H / 128) * 512 + size_t(E) * (H / 128) * (Mi / 128) * 512;
+  const size_t gu = size_t(E) * (Mi / 64) * (H / 256);
+  const size_t dn = size_t(E) * (H / 128) * (Mi / 256);
+  return (gu + dn) * kWBlock;
 }
 
-cudaError_t launch_moe_prepare(const uint8_t* gate_sc, const uint8_t* up_sc,
-                               const uint8_t* down_sc, int E, int H, int Mi, uint8_t* prepared,
-                               cudaStream_t stream) {
+cudaError_t launch_moe_prepare(const uint8_t* gate_wp, const uint8_t* gate_sc,
+                               const uint8_t* up_wp, const uint8_t* up_sc,
+                               const uint8_t* down_wp, const uint8_t* down_sc, int E, int H, int Mi,
+                               uint8_t* prepared, cudaStream_t stream) {
   uint8_t* gu = prepared;
-  uint8_t* dn = prepared + size_t(E) * (Mi / 64) * (H / 128) * 512;
-  gu_atoms_kernel<<<148 * 8, 256, 0, stream>>>(gate_sc, up_sc, E, Mi, H, gu);
+  uint8_t* dn = prepared + size_t(E) * (Mi / 64) * (H / 256) * kWBlock;
+  prepare_blocks_kernel<<<148 * 8, 256, 0, stream>>>(gate_wp, gate_sc, up_wp, up_sc, E, Mi, 64, H,
+                                                     true, gu);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  return launch_sf_atoms(down_sc, Mi / 32, E * H, Mi, 128, dn, stream);
+  prepare_blocks_kernel<<<148 * 8, 256, 0, stream>>>(down_wp, down_sc, nullptr, nullptr, E, H, 128,
+                                                     Mi, false, dn);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_gather_chunks(const uint8_t* xq, const uint8_t* xsc, const int* perm,
@@ -344,12 +451,11 @@ static cudaError_t set_smem_once(const void* fn, bool* done) {
 cudaError_t launch_moe_tc(const MoeTcLaunch& L, cudaStream_t stream) {
   static bool smem_gu = false, smem_dn = false;
   const int E = L.E, H = L.H, Mi = L.Mi;
-  const uint8_t* prep_gu = L.prepared;
-  const uint8_t* prep_dn = L.prepared + size_t(E) * (Mi / 64) * (H / 128) * 512;
-  CUtensorMap a0, a1, b;
+  CUtensorMap b;
   MoeTcArgs p{};
-  p.chunks = L.chunks;
-  p.n_chunks = L.n_chunks;
+  p.counts = L.counts;
+  p.E = L.E;
+  p.T_pad = L.rows / L.E;
   p.perm = L.perm;
   p.inter = Mi;
   p.hidden = H;
@@ -357,32 +463,29 @@ cudaError_t launch_moe_tc(const MoeTcLaunch& L, cudaStream_t stream) {
   p.hp_atoms = L.hp_atoms;
   p.yd = L.yd;
   p.err = L.err;
-  const int grid = L.grid;
+  const int grid = L.grid * kCtasPerSm;
   if (L.gate_up) {
-    if (!get_tmap(&a0, L.gate_wp, H / 2, uint64_t(E) * Mi, 64) ||
-        !get_tmap(&a1, L.up_wp, H / 2, uint64_t(E) * Mi, 64) ||
-        !get_tmap(&b, L.xp, H / 2, uint64_t(L.max_chunks) * kChunk, kChunk))
+    if (!get_tmap(&b, L.xp, H / 2, uint64_t(L.rows), kChunk))
       return cudaErrorInvalidValue;
-    p.sfa = prep_gu;
+    p.wblocks = L.prepared;
     p.sfb = L.xp_atoms;
     p.K = H;
     p.tiles = Mi / 64;
     p.kc_pad = H / 128;
     cudaError_t e = set_smem_once(reinterpret_cast<const void*>(moe_tc_kernel<true>), &smem_gu);
     if (e != cudaSuccess) return e;
-    moe_tc_kernel<true><<<grid, kThreads, moe_tc_smem(), stream>>>(a0, a1, b, p);
+    moe_tc_kernel<true><<<grid, kThreads, moe_tc_smem(), stream>>>(b, p);
   } else {
-    if (!get_tmap(&a0, L.down_wp, Mi / 2, uint64_t(E) * H, 128) ||
-        !get_tmap(&b, L.hp, Mi / 2, uint64_t(L.max_chunks) * kChunk, kChunk))
+    if (!get_tmap(&b, L.hp, Mi / 2, uint64_t(L.rows), kChunk))
       return cudaErrorInvalidValue;
-    p.sfa = prep_dn;
+    p.wblocks = L.prepared + size_t(E) * (Mi / 64) * (H / 256) * kWBlock;
     p.sfb = L.hp_atoms;
     p.K = Mi;
     p.tiles = H / 128;
     p.kc_pad = Mi / 128;
     cudaError_t e = set_smem_once(reinterpret_cast<const void*>(moe_tc_kernel<false>), &smem_dn);
     if (e != cudaSuccess) return e;
-    moe_tc_kernel<false><<<grid, kThreads, moe_tc_smem(), stream>>>(a0, a0, b, p);
+    moe_tc_kernel<false><<<grid, kThreads, moe_tc_smem(), stream>>>(b, p);
   }
   return cudaGetLastError();
 }

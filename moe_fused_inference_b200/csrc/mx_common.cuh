@@ -84,6 +84,12 @@ __device__ __forceinline__ uint32_t quant_nibble(float v, float inv) {
   return c | (x < 0.0f ? 8u : 0u);
 }
 
+// Quantise 8 consecutive elements of a 32-element block held by a quad of
+// lanes (lanes 4q..4q+3 hold the block's 4 groups of 8).  All 32 lanes must
+// call it (full-mask shuffles); `live` = false lanes contribute zeros.
+// Returns the 8 nibbles packed LSB-first and the block's scale.
+__device__ __forceinline__ uint32_t quant_group8(const float (&v)[8], BlockScale& bs);
+
 // 8 nibbles -> two words of 4 signed int8 each, value = 2*e2m1 in [-12, 12].
 // lo holds elements 0-3, hi elements 4-7 (element order kept).
 __device__ __forceinline__ void nib8_to_i8(uint32_t w, uint32_t& lo, uint32_t& hi) {
@@ -148,6 +154,26 @@ __device__ __forceinline__ int dot_i8x32(const uint32_t* a8, const uint32_t* b8)
 // encoding folded into the exponent).
 __device__ __forceinline__ float block_value(int s, int sa, int sb) {
   return __fmul_rn(float(s), exp2i(sa + sb - 256));
+}
+
+__device__ __forceinline__ uint32_t quant_group8(const float (&v)[8], BlockScale& bs) {
+  float am = 0.0f;
+  bool has_nan = false;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    am = fmaxf(am, fabsf(v[i]));
+    has_nan |= (v[i] != v[i]);
+  }
+  am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+  am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+  has_nan |= __shfl_xor_sync(0xffffffffu, int(has_nan), 1) != 0;
+  has_nan |= __shfl_xor_sync(0xffffffffu, int(has_nan), 2) != 0;
+  // a NaN anywhere in the block gives code 127, like the reference's NaN max
+  bs = block_scale(has_nan ? __uint_as_float(0x7fc00000u) : am);
+  uint32_t word = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) word |= quant_nibble(v[i], bs.inv) << (4 * i);
+  return word;
 }
 
 __device__ __forceinline__ uint4 ldg_u4(const void* p) {

@@ -60,22 +60,8 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(QuantArgs a) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = __half2float(__float2half_rn(v[i]));
   }
-  float am = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(v[i]));
-  // NaN-propagating max across the quad (fmaxf drops NaN; keep the
-  // reference's behaviour of a NaN block max giving code 127).
-  bool has_nan = false;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) has_nan |= (v[i] != v[i]);
-  am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-  am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
-  has_nan |= __shfl_xor_sync(0xffffffffu, int(has_nan), 1) != 0;
-  has_nan |= __shfl_xor_sync(0xffffffffu, int(has_nan), 2) != 0;
-  const BlockScale bs = block_scale(has_nan ? __uint_as_float(0x7fc00000u) : am);
-  uint32_t word = 0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) word |= quant_nibble(v[i], bs.inv) << (4 * i);
+  BlockScale bs;
+  const uint32_t word = quant_group8(v, bs);
   if (!live) return;
   *reinterpret_cast<uint32_t*>(a.xq + long(row) * (a.Kp >> 1) + (k0 >> 1)) = word;
   if ((c8 & 3) == 0) a.xsc[long(row) * (a.Kp >> 5) + (c8 >> 2)] = bs.code;

@@ -29,29 +29,69 @@ template <int kMaxBlk>
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   __shared__ float s_logit[kMaxE];
   __shared__ unsigned s_last;
+  __shared__ __align__(16) uint8_t s_xq[kMaxBlk * 32 * 16];
+  __shared__ __align__(16) uint8_t s_xsc[kMaxBlk * 32];
   const int t = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nwarp = kRouteThreads / 32;
   const int nb = a.H >> 5;
 
+  // ---- quantise token t (the reference's prequant, fused) -------------------
+  // one thread per 8 elements, a quad per 32-element block (quant_group8)
+  for (int base = warp * 32; base < (a.H >> 3); base += kRouteThreads) {
+    const int c8 = base + lane;
+    const bool live = c8 < (a.H >> 3);
+    float v[8];
+    if (live) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(
+          reinterpret_cast<const __nv_bfloat16*>(a.x) + long(t) * a.H + c8 * 8);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h2[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+    }
+    BlockScale bs;
+    const uint32_t word = quant_group8(v, bs);
+    if (live) {
+      reinterpret_cast<uint32_t*>(s_xq)[c8] = word;
+      if ((c8 & 3) == 0) s_xsc[c8 >> 2] = bs.code;
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < (a.H >> 3); i += kRouteThreads)
+    reinterpret_cast<uint32_t*>(a.xq + long(t) * (a.H >> 1))[i] = reinterpret_cast<uint32_t*>(s_xq)[i];
+  for (int i = threadIdx.x; i < nb; i += kRouteThreads) a.xsc[long(t) * nb + i] = s_xsc[i];
+
   // ---- logits for token t --------------------------------------------------
-  // Each lane owns blocks b = lane + 32*j; the token's blocks are loaded once,
-  // the router rows of all experts of this warp are in flight together.
-  uint4 xa[kMaxBlk];
+  // Each lane owns blocks b = lane + 32*j: the token's nibbles for them are
+  // expanded to int8 once; the router rows of 4 experts per warp are in
+  // flight together.
+  uint32_t xa8[kMaxBlk][8];
   int xs[kMaxBlk];
 #pragma unroll
   for (int j = 0; j < kMaxBlk; ++j) {
     const int b = lane + 32 * j;
     if (b < nb) {
-      xa[j] = ldg_u4(a.xq + long(t) * (a.H >> 1) + b * 16);
-      xs[j] = a.xsc[long(t) * nb + b];
+      const uint4 q = reinterpret_cast<const uint4*>(s_xq)[b];
+      nib8_to_i8(q.x, xa8[j][0], xa8[j][1]);
+      nib8_to_i8(q.y, xa8[j][2], xa8[j][3]);
+      nib8_to_i8(q.z, xa8[j][4], xa8[j][5]);
+      nib8_to_i8(q.w, xa8[j][6], xa8[j][7]);
+      xs[j] = s_xsc[b];
     }
   }
-  for (int e0 = warp; e0 < a.E; e0 += 4 * nwarp) {
-    uint4 wv[4][kMaxBlk];
-    int ws[4][kMaxBlk];
+  constexpr int kU = kMaxBlk <= 2 ? 8 : 4;  // experts in flight per warp
+  for (int e0 = warp; e0 < a.E; e0 += kU * nwarp) {
+    uint4 wv[kU][kMaxBlk];
+    int ws[kU][kMaxBlk];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < kU; ++u) {
       const int e = e0 + u * nwarp;
 #pragma unroll
       for (int j = 0; j < kMaxBlk; ++j) {
@@ -62,62 +102,112 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
         }
       }
     }
+    double acc[kU];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < kU; ++u) {
       const int e = e0 + u * nwarp;
-      double acc = 0.0;
+      acc[u] = 0.0;
 #pragma unroll
       for (int j = 0; j < kMaxBlk; ++j) {
         const int b = lane + 32 * j;
         if (e < a.E && b < nb) {
-          const int s = block_dot_i(xa[j], wv[u][j]);
-          acc += double(s) * exp2i_d(xs[j] + ws[u][j] - 256);
+          const int s = block_dot_pre(wv[u][j], xa8[j]);
+          acc[u] += double(s) * exp2i_d(xs[j] + ws[u][j] - 256);
         }
       }
+    }
+    // xor-butterfly over the warp for all kU experts at once: at offset `off`
+    // each lane keeps half of its values and adds the partner's copy, so every
+    // value is the same pairwise sum as a per-expert butterfly 16,8,4,2,1
+    // (bit-identical), with kU-1 + 5 - log2(kU) shuffles instead of 5 kU.
+    int n = kU;
 #pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-      if (lane == 0 && e < a.E) s_logit[e] = float(acc);
+    for (int off = 16; off >= 1; off >>= 1) {
+      if (n > 1) {
+        const bool upper = (lane & off) != 0;
+        const int h = n >> 1;
+#pragma unroll
+        for (int i = 0; i < kU / 2; ++i) {
+          if (i < h) {
+            const double send = upper ? acc[i] : acc[i + h];
+            const double keep = upper ? acc[i + h] : acc[i];
+            acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+          }
+        }
+        n = h;
+      } else {
+        acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], off);
+      }
+    }
+    // after log2(kU) halving steps lane l holds expert index (l >> (5 - log2 kU))
+    constexpr int kLog = kU == 8 ? 3 : (kU == 4 ? 2 : (kU == 2 ? 1 : 0));
+    if ((lane & ((32 >> kLog) - 1)) == 0) {
+      const int u = lane >> (5 - kLog);
+      const int e = e0 + u * nwarp;
+      if (e < a.E) s_logit[e] = float(acc[0]);
     }
   }
   __syncthreads();
   if (a.logits)
     for (int e = threadIdx.x; e < a.E; e += blockDim.x) a.logits[long(t) * a.E + e] = s_logit[e];
 
-  // ---- top-k (warp 0) --------------------------------------------------------
-  if (warp == 0) {
-    unsigned long long taken = 0ull;  // bit i: expert lane + 32*i already selected
-    float selv = 0.f;
-    int seli = 0;
-    for (int j = 0; j < a.k; ++j) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-      for (int i = 0; lane + 32 * i < a.E; ++i) {
-        const int e = lane + 32 * i;
-        if ((taken >> i) & 1ull) continue;
-        const float v = s_logit[e];
-        if (bi == 0x7fffffff || better(v, e, bv, bi)) { bv = v; bi = e; }
-      }
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-        if (oi != 0x7fffffff && (bi == 0x7fffffff || better(ov, oi, bv, bi))) { bv = ov; bi = oi; }
-      }
-      if ((bi & 31) == lane && bi != 0x7fffffff) taken |= 1ull << (bi >> 5);
-      if (lane == j) { selv = bv; seli = bi; }
+  // ---- top-k ----------------------------------------------------------------
+  // Thread e computes the rank of expert e under the order (logit desc,
+  // index asc); rank < k places it in the top-k at that position.
+  __shared__ int s_sel[32];
+  __shared__ float s_selv[32];
+  for (int e = threadIdx.x; e < a.E; e += kRouteThreads) {
+    const float v = s_logit[e];
+    int rank = 0;
+    for (int j = 0; j < a.E; ++j) rank += better(s_logit[j], j, v, e) ? 1 : 0;
+    if (rank < a.k) {
+      s_sel[rank] = e;
+      s_selv[rank] = v;
     }
+  }
+  __syncthreads();
+  __shared__ int s_row[32];
+  if (warp == 0) {
     // weights: exp(l - max) over the selected, normalised by their sum
-    const float mx = __shfl_sync(0xffffffffu, selv, 0);
-    const float p = (lane < a.k) ? expf(selv - mx) : 0.f;
+    const float mx = s_selv[0];
+    const float p = (lane < a.k) ? expf(s_selv[lane < a.k ? lane : 0] - mx) : 0.f;
     float sum = 0.f;
     for (int j = 0; j < a.k; ++j) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, p, j));
     if (lane < a.k) {
-      a.topi[long(t) * a.k + lane] = seli;
+      a.topi[long(t) * a.k + lane] = s_sel[lane];
       a.topw[long(t) * a.k + lane] = __fdiv_rn(p, sum);
+      if (a.xp) {
+        // claim a row in each selected expert's region
+        const int e = s_sel[lane];
+        const int pos = atomicAdd(a.cursor + e, 1);
+        const int row = e * a.T_pad + pos;
+        s_row[lane] = row;
+        a.perm[row] = t * a.k + lane;
+      }
+    }
+  }
+  if (a.xp) {
+    // copy the quantised row into each claimed row, scales into the atoms
+    __syncthreads();
+    const int q16 = a.H >> 5;  // uint4 per row
+    for (int i = threadIdx.x; i < a.k * q16; i += kRouteThreads) {
+      const int j = i / q16, c = i % q16;
+      reinterpret_cast<uint4*>(a.xp + size_t(s_row[j]) * (a.H >> 1))[c] =
+          reinterpret_cast<const uint4*>(s_xq)[c];
+    }
+    const int kc = a.H >> 7;  // atoms per row
+    for (int i = threadIdx.x; i < a.k * kc; i += kRouteThreads) {
+      const int j = i / kc, c = i % kc;
+      const int row = s_row[j];
+      *reinterpret_cast<uint32_t*>(a.xp_atoms + (size_t(row >> 5) * kc + c) * 512 + (row & 31) * 16) =
+          reinterpret_cast<const uint32_t*>(s_xsc)[c];
     }
   }
 
   // ---- last CTA builds the per-expert work lists ----------------------------
+  // (CUDA-core path only; the tensor-core kernels rebuild their chunk table
+  // from the per-expert cursors themselves)
+  if (!a.g_gu) return;
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_last = (atomicAdd(a.done, 1u) == unsigned(gridDim.x) - 1u);
@@ -172,37 +262,43 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
     }
   }
   __syncthreads();
+  if (a.cursor)
+    for (int e = threadIdx.x; e < a.E; e += kRouteThreads) a.cursor[e] = 0;  // ready for next call
   const long gstride = long(a.Mi) * (a.H >> 1), gsstride = long(a.Mi) * (a.H >> 5);
   const long dstride = long(a.H) * (a.Mi >> 1), dsstride = long(a.H) * (a.Mi >> 5);
   for (int e = threadIdx.x; e < a.E; e += blockDim.x) {
     const int ai = s_act[e];
     if (ai < 0) continue;
     const int first = s_off[e], cnt = s_cnt[e];
-    GroupDesc g;
-    g.first = first; g.count = cnt;
-    g.wp = a.gate_wp + e * gstride; g.wsc = a.gate_sc + e * gsstride;
-    a.g_gu[2 * ai] = g;
-    g.first = P + first;
-    g.wp = a.up_wp + e * gstride; g.wsc = a.up_sc + e * gsstride;
-    a.g_gu[2 * ai + 1] = g;
-    g.first = first;
-    g.wp = a.down_wp + e * dstride; g.wsc = a.down_sc + e * dsstride;
-    a.g_dn[ai] = g;
+    if (a.g_gu) {
+      GroupDesc g;
+      g.first = first; g.count = cnt;
+      g.wp = a.gate_wp + e * gstride; g.wsc = a.gate_sc + e * gsstride;
+      a.g_gu[2 * ai] = g;
+      g.first = P + first;
+      g.wp = a.up_wp + e * gstride; g.wsc = a.up_sc + e * gsstride;
+      a.g_gu[2 * ai + 1] = g;
+      g.first = first;
+      g.wp = a.down_wp + e * dstride; g.wsc = a.down_sc + e * dsstride;
+      a.g_dn[ai] = g;
+    }
     if (a.chunks) {
       for (int c = 0; c * 32 < cnt; ++c) {
         ChunkDesc cd;
         cd.expert = e;
         cd.count = min(32, cnt - 32 * c);
+        cd.row0 = e * a.T_pad + 32 * c;
+        cd.pad = 0;
         a.chunks[s_cbase[e] + c] = cd;
-        for (int r = cd.count; r < 32; ++r) a.perm[(s_cbase[e] + c) * 32 + r] = -1;
+        for (int r = cd.count; r < 32; ++r) a.perm[cd.row0 + r] = -1;
       }
     }
   }
   for (int i = threadIdx.x; i < P; i += blockDim.x) {
+    if (!a.e_gu) continue;
     const int e = __ldcg(a.topi + i);
     const int pil = atomicAdd(&s_cur[e], 1);  // position in expert e's list
     const int pos = s_off[e] + pil;
-    if (a.perm) a.perm[(s_cbase[e] + pil / 32) * 32 + pil % 32] = i;
     EntryDesc d;
     d.pad = 0;
     d.act_row = i / a.k;

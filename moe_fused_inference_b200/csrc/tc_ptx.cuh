@@ -52,18 +52,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait: gives up after kWaitLimitNs, records `code` in *err (first
 // error wins) and returns false.  The caller then skips its remaining work.
+// try_wait suspends in hardware between polls; the clock and the shared error
+// flag (a global load) are only consulted every 1024 polls, so a wait that is
+// satisfied within a few microseconds costs no extra memory traffic.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  while (true) {
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (err && *reinterpret_cast<volatile int*>(err) != 0) return false;  // another role failed
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
-      if (err) atomicCAS(err, 0, code);
-      return false;
+    if ((i & 1023u) == 0) {
+      if (err && *reinterpret_cast<volatile int*>(err) != 0) return false;  // another role failed
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (err) atomicCAS(err, 0, code);
+        return false;
+      }
     }
-    __nanosleep(64);
   }
 }
 

@@ -35,11 +35,14 @@ struct QuantArgs {
 struct ChunkDesc {
   int expert;
   int count;
+  int row0;   // first row of the chunk in the per-expert activation regions
+  int pad;
 };
 
 struct RouteArgs {
-  const uint8_t* xq;   // (T, H/2)
-  const uint8_t* xsc;  // (T, H/32)
+  const void* x;       // bf16 (T, H): quantised inside the kernel into xq/xsc
+  uint8_t* xq;         // (T, H/2)
+  uint8_t* xsc;        // (T, H/32)
   const uint8_t* wr;   // (E, H/2)
   const uint8_t* sr;   // (E, H/32)
   int T, H, E, k;
@@ -54,10 +57,16 @@ struct RouteArgs {
   GroupDesc* g_gu; EntryDesc* e_gu; int* n_gu;   // 2 groups per active expert
   GroupDesc* g_dn; EntryDesc* e_dn; int* n_dn;   // 1 group per active expert
   int* n_active;
-  // tensor-core decode path: 32-token chunks per expert
+  // tensor-core decode path: 32-token chunks per expert.  Expert e owns rows
+  // [e*T_pad, (e+1)*T_pad) of xp / perm (T_pad = ceil32(T)); a token's row in
+  // its expert's region comes from the atomic cursor[e].
   ChunkDesc* chunks;   // [max_chunks]
   int* n_chunks;
-  int* perm;           // [max_chunks * 32]: chunk row -> pair index, -1 padding
+  int* perm;           // [E * T_pad]: row -> pair index (token * k + slot), -1 padding
+  int* cursor;         // [E], zero before the launch; reset by the kernel
+  uint8_t* xp;         // [E * T_pad][H/2] quantised rows per expert region
+  uint8_t* xp_atoms;   // [E * T_pad / 32][H/128][512] their scale atoms
+  int T_pad;
 };
 
 constexpr int kRouteMaxE = 256;
@@ -96,18 +105,20 @@ cudaError_t launch_tc_gemm(const uint8_t* a, const uint8_t* sfa_atoms, const uin
 struct MoeTcLaunch {
   bool gate_up;
   int E, H, Mi, max_chunks, grid;
-  const uint8_t* gate_wp; const uint8_t* up_wp; const uint8_t* down_wp;
-  const uint8_t* prepared;           // scale atoms from launch_moe_prepare
-  const ChunkDesc* chunks; const int* n_chunks; const int* perm;
-  const uint8_t* xp; const uint8_t* xp_atoms;   // gathered chunk activations
+  const uint8_t* prepared;           // weight blocks from launch_moe_prepare
+  const int* counts;                            // tokens per expert (route cursors)
+  const int* perm;
+  int rows;                                     // E * T_pad rows in xp / hp / perm
+  const uint8_t* xp; const uint8_t* xp_atoms;   // per-expert token rows (route.cu)
   uint8_t* hp; uint8_t* hp_atoms;               // requantised h (gate/up output)
   float* yd;                                    // per-pair down output
   int* err;
 };
 size_t moe_prepared_bytes(int E, int H, int Mi);
-cudaError_t launch_moe_prepare(const uint8_t* gate_sc, const uint8_t* up_sc,
-                               const uint8_t* down_sc, int E, int H, int Mi, uint8_t* prepared,
-                               cudaStream_t stream);
+cudaError_t launch_moe_prepare(const uint8_t* gate_wp, const uint8_t* gate_sc,
+                               const uint8_t* up_wp, const uint8_t* up_sc,
+                               const uint8_t* down_wp, const uint8_t* down_sc, int E, int H, int Mi,
+                               uint8_t* prepared, cudaStream_t stream);
 cudaError_t launch_gather_chunks(const uint8_t* xq, const uint8_t* xsc, const int* perm,
                                  const int* n_chunks, int max_chunks, int k, int H, uint8_t* xp,
                                  uint8_t* xp_atoms, cudaStream_t stream);
