@@ -20,9 +20,11 @@ Arms:
                      (runtime/model_runner.py:99-132, ported in oracle/moe_ref.py)
                      on the host cores, same metric and config, rank 0 only.
 
-Multi-GPU (torchrun): each rank runs the same per-GPU workload on its own GPU
-(weak scaling, no collective on the data path; expert parallelism is not in
-this benchmark yet), timed on the device and reduced with a max over ranks.
+Multi-GPU (torchrun, N ranks): expert parallelism (BASELINE config 5's
+sharding) — each rank holds 128/N experts of every layer and the full router,
+routes its own T tokens, and dispatch / combine are NCCL all-to-alls over
+NVLink (moe_fused_inference_b200/ep.py).  Per-GPU tokens stay at T (weak
+scaling); the step is timed on the device and reduced with a max over ranks.
 """
 
 from __future__ import annotations
@@ -52,6 +54,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--tokens", type=int, default=64, help="decode tokens per GPU (T)")
+    ap.add_argument("--layers", type=int, default=N_LAYERS,
+                    help="distinct MoE layers per step (48 = the model; fewer for profiling)")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="time plain launches instead of a captured CUDA graph")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-sample-s", type=float, default=15.0,
                     help="seconds of CPU work for the cpu_baseline sample")
@@ -235,55 +241,9 @@ def run_reference(args, world, rank):
 
 
 # ---------------------------------------------------------------------------
-def run_ours(args, world, rank, local):
-    from moe_fused_inference_b200.layer import MoELayer, random_layer_weights
-
-    dev = torch.device("cuda", local if world > 1 else 0)
-    T = args.tokens
-    layers = [MoELayer(random_layer_weights(E, H, MI, 0.02, seed=1000 * rank + l, device=dev), TOPK)
-              for l in range(N_LAYERS)]
-    g = torch.Generator(device=dev).manual_seed(7 + rank)
-    X = torch.randn((N_LAYERS, T, H), generator=g, device=dev).bfloat16()
-    out = torch.empty((N_LAYERS, T, H), dtype=torch.float32, device=dev)
-    topi = torch.empty((N_LAYERS, T, TOPK), dtype=torch.int32, device=dev)
-    topw = torch.empty((N_LAYERS, T, TOPK), dtype=torch.float32, device=dev)
-    stream = torch.cuda.current_stream(dev)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(N_LAYERS)]
-    for row in evs:
-        for e in row:
-            e.record(stream)  # creates the event handles before the library records them
-
-    def step(with_events):
-        for l in range(N_LAYERS):
-            layers[l](X[l], out=out[l], topi=topi[l], topw=topw[l],
-                      events=evs[l] if with_events else None)
-
-    for _ in range(args.warmup):
-        step(False)
-    torch.cuda.synchronize(dev)
-
-    # One step (48 layer calls) is captured in a CUDA graph and replayed:
-    # decode serving runs graphs, and replay removes the host's per-launch cost
-    # from the device-side measurement.  The timed graph has no stage events
-    # (each event node costs the timeline ~2-3 us); a second graph with the
-    # stage events is replayed once afterwards for the per-kernel breakdown.
-    cap = torch.cuda.Stream(dev)
-    cap.wait_stream(stream)
-    graph = torch.cuda.CUDAGraph()
-    graph_ev = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(cap):
-        step(True)  # warm the capture stream
-        torch.cuda.synchronize(dev)
-        with torch.cuda.graph(graph, stream=cap):
-            step(False)
-        with torch.cuda.graph(graph_ev, stream=cap):
-            step(True)
-    stream.wait_stream(cap)
-    for _ in range(args.warmup):
-        graph.replay()
-    torch.cuda.synchronize(dev)
-
-    # ---- device-resident timed region ----
+def timed_region(args, world, dev, stream, step):
+    """Clock-sampled, barrier-bracketed device timing of args.steps calls of
+    step(); returns (max-over-ranks ms, clocks)."""
     sampler = ClockSampler(dev.index if dev.index is not None else 0)
     sampler.start()
     barrier(world)
@@ -292,92 +252,288 @@ def run_ours(args, world, rank, local):
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
     for _ in range(args.steps):
-        graph.replay()
+        step()
     t1.record(stream)
     torch.cuda.synchronize(dev)
     barrier(world)
     clocks = sampler.stop()
-    ms = t0.elapsed_time(t1)
-    ms_max = max_over_ranks(ms, world)
-    ms_per_step = ms_max / args.steps
-    tokens = T * N_LAYERS * args.steps * world
-    value = tokens / (ms_max / 1e3)
+    return max_over_ranks(t0.elapsed_time(t1), world), clocks
 
-    # ---- per-stage times (graph with stage events, replayed after the timed region) ----
-    graph_ev.replay()
+
+def capture(dev, stream, fn, warm):
+    """Capture fn() into a CUDA graph on a side stream (after `warm` eager calls)."""
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(cap):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize(dev)
+        with torch.cuda.graph(graph, stream=cap):
+            fn()
+    stream.wait_stream(cap)
+    torch.cuda.synchronize(dev)
+    return graph
+
+
+def cpu_baseline(args, T, weights):
+    cpu_layer = make_cpu_layer(weights)
+    tok_s, n, _ = time_cpu_layer(cpu_layer, T, seconds=args.cpu_sample_s)
+    return {"value": tok_s, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n} layer calls x T={T} tokens, torch CPU bf16 with layer 0's weights "
+                      "dequantised (runtime/model_runner.py:99-132 ported)"}
+
+
+def run_ours(args, world, rank, local):
+    if world > 1:
+        return run_ep(args, world, rank, local)
+    from moe_fused_inference_b200.layer import MoELayer, random_layer_weights
+
+    dev = torch.device("cuda", 0)
+    T, NL = args.tokens, args.layers
+    layers = [MoELayer(random_layer_weights(E, H, MI, 0.02, seed=l, device=dev), TOPK)
+              for l in range(NL)]
+    g = torch.Generator(device=dev).manual_seed(7)
+    X = torch.randn((NL, T, H), generator=g, device=dev).bfloat16()
+    out = torch.empty((NL, T, H), dtype=torch.float32, device=dev)
+    topi = torch.empty((NL, T, TOPK), dtype=torch.int32, device=dev)
+    topw = torch.empty((NL, T, TOPK), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(NL)]
+    for row in evs:
+        for e in row:
+            e.record(stream)  # creates the event handles before the library records them
+
+    def step(with_events=False):
+        for l in range(NL):
+            layers[l](X[l], out=out[l], topi=topi[l], topw=topw[l],
+                      events=evs[l] if with_events else None)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+
+    # One step (NL layer calls) is captured in a CUDA graph and replayed:
+    # decode serving runs graphs, and replay removes the host's per-launch cost
+    # from the device-side measurement.  The timed graph has no stage events
+    # (each event node costs the timeline ~2-3 us); a second graph with the
+    # stage events is replayed once afterwards for the per-kernel breakdown.
+    graph = graph_ev = None
+    if not args.no_graph:
+        graph = capture(dev, stream, step, 1)
+        graph_ev = capture(dev, stream, lambda: step(True), 0)
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+
+    ms, clocks = timed_region(args, world, dev, stream, graph.replay if graph else step)
+    ms_per_step = ms / args.steps
+    tokens = T * NL * args.steps
+    value = tokens / (ms / 1e3)
+
+    # ---- per-stage times (stage events, after the timed region) ----
+    if graph_ev is not None:
+        graph_ev.replay()
+    else:
+        step(True)
     torch.cuda.synchronize(dev)
     stage = [0.0] * 5
-    for l in range(N_LAYERS):
+    for l in range(NL):
         for i in range(5):
             stage[i] += evs[l][i].elapsed_time(evs[l][i + 1])
-    uniq = sum(int(torch.unique(topi[l]).numel()) for l in range(N_LAYERS))
+    uniq = sum(int(torch.unique(topi[l]).numel()) for l in range(NL))
 
     # ---- roofline of the dominant kernel (tensor-core expert GEMMs: gate/up + down) ----
     peak, peak_kind = measured_peaks()
-    gemm_ms = stage[2] + stage[3]  # per step, summed over the 48 layer calls
+    gemm_ms = stage[2] + stage[3]  # per step, summed over the NL layer calls
     w_bytes = uniq * EXPERT_BYTES  # per step
     achieved = w_bytes / (gemm_ms / 1e3) / 1e9
-    layer_ms = ms_per_step
-    layer_bytes = (uniq * EXPERT_BYTES + N_LAYERS * (ROUTER_BYTES + T * H * 2 + T * H * 4 + T * TOPK * 8))
+    layer_bytes = (uniq * EXPERT_BYTES + NL * (ROUTER_BYTES + T * H * 2 + T * H * 4 + T * TOPK * 8))
     traffic = committed_traffic()
 
     del graph, graph_ev
     # ---- e2e through the public API with host buffers (plain per-call launches) ----
     Xh = X.cpu().pin_memory()
-    Oh = torch.empty((N_LAYERS, T, H), dtype=torch.float32).pin_memory()
+    Oh = torch.empty((NL, T, H), dtype=torch.float32).pin_memory()
     Xd = torch.empty_like(X)
-    barrier(world)
-    torch.cuda.synchronize(dev)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for s in range(args.steps):
+
+    def e2e_step():
         Xd.copy_(Xh, non_blocking=True)
-        for l in range(N_LAYERS):
+        for l in range(NL):
             layers[l](Xd[l], out=out[l], topi=topi[l], topw=topw[l])
         Oh.copy_(out, non_blocking=True)
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    barrier(world)
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+
+    e2e_ms, _ = timed_region(args, world, dev, stream, e2e_step)
     e2e_value = tokens / (e2e_ms / 1e3)
 
-    if rank != 0:
-        return
     line = {
         "metric": "MXFP4 MoE layer tokens/s (decode)", "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "mxfp4 (e2m1 x e2m1, fp32 accumulate)",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "mxfp4 (e2m1 x e2m1, fp32 accumulate)",
         "data": "synthetic (random-init weights N(0,0.02), activations N(0,1), seeded)",
         "config": {"workload": f"decode MoE layer, T={T} tokens/GPU, H=2048, E=128, top-8, Mi=768",
-                   "step": f"T tokens through {N_LAYERS} MoE layers with distinct weights, "
-                           "replayed as one captured CUDA graph (e2e: plain API calls)",
-                   "global_batch": T * world, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "l2": "inputs larger than L2: 48 distinct layer weight sets (15.4 GB) per step",
-                   "unique_experts_per_layer": uniq / N_LAYERS},
-        "gpu_launches": 6 * N_LAYERS * args.steps,  # quant, route, gather, gate/up, down, combine
+                   "step": f"T tokens through {NL} MoE layers with distinct weights, "
+                           + ("plain launches" if args.no_graph else "replayed as one captured CUDA graph")
+                           + " (e2e: plain API calls)",
+                   "global_batch": T, "parallelism": "single GPU",
+                   "l2": f"inputs larger than L2: {NL} distinct layer weight sets "
+                         f"({NL * E * EXPERT_BYTES / 1e9:.1f} GB) per step",
+                   "unique_experts_per_layer": uniq / NL},
+        "gpu_launches": 4 * NL * args.steps,  # route (+quantise), gate/up, down, combine
         "roofline": {"bound": "hbm", "kernel": "moe_tc_kernel (gate/up + down launches)",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind,
                      "algorithmic_bytes_per_step": w_bytes,
                      "traffic": (traffic or {}).get("bytes_per_layer_call"),
                      "traffic_source": (traffic or {}).get("source"),
-                     "layer": {"achieved": layer_bytes / (layer_ms / 1e3) / 1e9,
-                               "frac": layer_bytes / (layer_ms / 1e3) / 1e9 / peak,
-                               "stage_ms_per_step": dict(zip(
-                                   ["route", "gather", "gate_up", "down", "combine"], stage))}},
+                     "layer": {"achieved": layer_bytes / (ms_per_step / 1e3) / 1e9,
+                               "frac": layer_bytes / (ms_per_step / 1e3) / 1e9 / peak,
+                               "stage_ms_per_step": {"route": stage[0], "gate_up": stage[2],
+                                                     "down": stage[3], "combine": stage[4]}}},
         "e2e": {"value": e2e_value, "unit": "tokens/s",
                 "h2d_bytes_per_step": int(Xh.numel() * Xh.element_size()),
                 "d2h_bytes_per_step": int(Oh.numel() * Oh.element_size())},
         "clocks": clocks,
     }
-    if world == 1 and not args.no_cpu_baseline:
-        cpu_layer = make_cpu_layer(layers[0].w)
-        tok_s, n, _ = time_cpu_layer(cpu_layer, T, seconds=args.cpu_sample_s)
-        line["cpu_baseline"] = {"value": tok_s, "unit": "tokens/s", "cores": torch.get_num_threads(),
-                                "kind": "port",
-                                "sample": f"{n} layer calls x T={T} tokens, torch CPU bf16 with "
-                                          "layer 0's weights dequantised (runtime/model_runner.py:99-132 ported)"}
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args, T, layers[0].w)
+    print(json.dumps(line), flush=True)
+
+
+def run_ep(args, world, rank, local):
+    """Expert-parallel step over the torchrun ranks (NCCL all-to-all)."""
+    from moe_fused_inference_b200.ep import EPMoELayer, random_shard
+
+    dev = torch.device("cuda", local)
+    T, NL = args.tokens, args.layers
+    layers = [EPMoELayer(random_shard(E, world, rank, H, MI, 0.02, seed=l, device=dev), TOPK, T)
+              for l in range(NL)]
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    X = torch.randn((NL, T, H), generator=g, device=dev).bfloat16()
+    out = torch.empty((NL, T, H), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for l in range(NL):
+            layers[l](X[l], out=out[l])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    graph, graph_note = None, "plain launches"
+    if not args.no_graph:
+        # NCCL collectives are captured with the kernels; every rank must take
+        # the same path, so a capture failure anywhere makes all ranks time
+        # plain launches
+        import torch.distributed as dist
+        err = ""
+        try:
+            graph = capture(dev, stream, step, 1)
+        except Exception as e:  # noqa: BLE001
+            graph, err = None, f"{type(e).__name__}: {e}"[:200]
+        ok = torch.tensor([0.0 if graph is None else 1.0], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if ok.item() < 1.0:
+            graph = None
+            graph_note = "plain launches (graph capture failed: " + (err or "on another rank") + ")"
+        else:
+            graph_note = "one captured CUDA graph"
+            for _ in range(args.warmup):
+                graph.replay()
+        torch.cuda.synchronize(dev)
+
+    ms, clocks = timed_region(args, world, dev, stream, graph.replay if graph else step)
+    ms_per_step = ms / args.steps
+    tokens = T * NL * args.steps * world
+    value = tokens / (ms / 1e3)
+
+    # ---- expert-compute time per step (events around the local expert part) ----
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(NL)]
+    import torch.distributed as dist
+    for l in range(NL):
+        L = layers[l]
+        L.dispatch_prepare(X[l])
+        dist.all_to_all_single(L.recv.view(-1), L.send.view(-1))
+        evs[l][0].record(stream)
+        L.compute()
+        evs[l][1].record(stream)
+        dist.all_to_all_single(L.ret_back.view(-1), L.ret.view(-1))
+        L.finish(T, out[l])
+    torch.cuda.synchronize(dev)
+    experts_ms = sum(a.elapsed_time(b) for a, b in evs)
+    # unique local experts touched per layer on this rank
+    el = E // world
+    uniq = 0
+    rows_recv = 0
+    for l in range(NL):
+        L = layers[l]
+        cnt = L.recv[:, 0, :4].contiguous().view(torch.int32)[:, 0]
+        rows_recv += int(cnt.sum())
+        sel = torch.cat([L.recv[s, 1:1 + int(cnt[s])] for s in range(world)])
+        if sel.shape[0]:
+            from moe_fused_inference_b200.ep import row_offsets
+            _, _, so, _ = row_offsets(H, TOPK)
+            ids = sel[:, so:so + 4 * TOPK].contiguous().view(torch.int32)
+            uniq += int(torch.unique(ids[ids >= 0]).numel())
+    w_bytes = uniq * EXPERT_BYTES
+    peak, peak_kind = measured_peaks()
+    achieved = w_bytes / (experts_ms / 1e3) / 1e9
+    stats = torch.tensor([achieved, experts_ms, rows_recv / NL, uniq / NL], dtype=torch.float64,
+                         device=dev)
+    allstats = [torch.zeros_like(stats) for _ in range(world)]
+    dist.all_gather(allstats, stats)
+    allstats = torch.stack(allstats).cpu()
+
+    # ---- e2e: host activations in, host outputs back, plain launches ----
+    if graph is not None:
+        del graph
+    Xh = X.cpu().pin_memory()
+    Oh = torch.empty((NL, T, H), dtype=torch.float32).pin_memory()
+    Xd = torch.empty_like(X)
+
+    def e2e_step():
+        Xd.copy_(Xh, non_blocking=True)
+        for l in range(NL):
+            layers[l](Xd[l], out=out[l])
+        Oh.copy_(out, non_blocking=True)
+
+    e2e_ms, _ = timed_region(args, world, dev, stream, e2e_step)
+    e2e_value = tokens / (e2e_ms / 1e3)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    if rank != 0:
+        return
+    worst = int(torch.argmin(allstats[:, 0]))
+    line = {
+        "metric": "MXFP4 MoE layer tokens/s (decode)", "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "mxfp4 (e2m1 x e2m1, fp32 accumulate)",
+        "data": "synthetic (random-init weights N(0,0.02), activations N(0,1), seeded)",
+        "config": {"workload": f"decode MoE layer, T={T} tokens/GPU, H=2048, E=128, top-8, Mi=768",
+                   "step": f"T tokens per rank through {NL} expert-parallel MoE layers "
+                           "(route, pack, NCCL all-to-all dispatch, tcgen05 experts, "
+                           "all-to-all return, unpack), " + graph_note,
+                   "global_batch": T * world, "parallelism": f"ep{world} ({E // world} experts/GPU)",
+                   "l2": f"inputs larger than L2: {NL} distinct layer shards "
+                         f"({NL * (E // world) * EXPERT_BYTES / 1e9:.1f} GB/GPU) per step",
+                   "rows_received_per_layer": [float(v) for v in allstats[:, 2]],
+                   "unique_local_experts_per_layer": [float(v) for v in allstats[:, 3]]},
+        "gpu_launches": 9 * NL * args.steps,  # per layer: route, pack, header, mask, scatter,
+                                              # gate/up, down, combine, unpack (+ NCCL kernels)
+        "roofline": {"bound": "hbm", "kernel": "mfi_moe_experts (scatter, gate/up, down, combine)",
+                     "achieved": float(allstats[worst, 0]), "peak": peak, "unit": "GB/s",
+                     "frac": float(allstats[worst, 0]) / peak, "peak_kind": peak_kind,
+                     "rank": worst, "experts_ms_per_step": float(allstats[worst, 1]),
+                     "traffic": None},
+        "e2e": {"value": e2e_value, "unit": "tokens/s",
+                "h2d_bytes_per_step": int(Xh.numel() * Xh.element_size()),
+                "d2h_bytes_per_step": int(Oh.numel() * Oh.element_size())},
+        "clocks": clocks,
+    }
     print(json.dumps(line), flush=True)
 
 

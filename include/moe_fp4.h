@@ -192,13 +192,85 @@ int mfi_moe_layer(const mfi_moe_weights* w, const void* x_bf16, int T, float* ou
 
 /* As mfi_moe_layer, recording six caller-created cudaEvent_t (passed as void*)
  * on the stream at the stage boundaries, for per-kernel timing:
- * tensor-core shapes: [0] start, [1] after quantise + route, [2] after the
- * chunk gather, [3] after gate/up (+ SwiGLU requant), [4] after down,
- * [5] after the combine; other shapes: [2] after the gate/up GEMV, [3] after
- * SwiGLU requantisation, [4] after the down GEMV. */
+ * tensor-core shapes: [0] start, [1] after quantise + route (which also
+ * writes each token's row into its experts' regions), [2] = [1], [3] after
+ * gate/up (+ SwiGLU requant), [4] after down, [5] after the combine; other
+ * shapes: [2] after the gate/up GEMV, [3] after SwiGLU requantisation, [4]
+ * after the down GEMV. */
 int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float* out,
                      int32_t* topi, float* topw, float* logits, void* workspace,
                      size_t workspace_bytes, void* const* events, int n_events, void* stream);
+
+/* ------------------------------------------------------------------------
+ * The layer in two halves, for expert parallelism (no reference counterpart:
+ * the reference runs on one GPU; the halves are its route step
+ * runtime/model_runner_v2.py:183-194 and its expert step :195-208).
+ * ------------------------------------------------------------------------ */
+
+/* Quantise bf16 x (T, hidden) into xq (T, hidden/2) / xsc (T, hidden/32)
+ * (16- and 4-byte aligned) and route it with the router of `w`: topi int32
+ * (T, top_k), topw fp32 (T, top_k), logits fp32 (T, E) or NULL.  Bit-identical
+ * to the routing of mfi_moe_layer.  Only router_wp/router_sc, n_experts,
+ * hidden and top_k of `w` are read. */
+int mfi_moe_route(const mfi_moe_weights* w, const void* x_bf16, int T, uint8_t* xq, uint8_t* xsc,
+                  int32_t* topi, float* topw, float* logits, void* stream);
+
+/* Expert compute on R pre-quantised, pre-routed rows:
+ *   out[r] = sum over j < top_k with sel[r][j] >= 0, in slot order, of
+ *            selw[r][j] * down_e(swiglu(gate_e(x_r), up_e(x_r))),  e = sel[r][j]
+ * with each product and partial sum rounded to fp32 (the combine of
+ * mfi_moe_combine).  Row r of xq / xsc / sel / selw / out starts at r * *_ld
+ * (bytes for xq and xsc, elements otherwise); xq rows 16-byte aligned, xsc
+ * rows 4-byte aligned.  sel entries are expert ids of `w` (0..n_experts-1) or
+ * -1; an id must not repeat within a row (the device error flag then reads 5;
+ * an id >= n_experts reads 4 and is skipped).  Needs hidden and inter to be
+ * multiples of 256 and `w->prepared`; router fields are not read.
+ * R * top_k <= 16384.  Rows whose slots are all -1 get zeros. */
+size_t mfi_moe_experts_workspace_bytes(int R, int hidden, int inter, int n_experts, int top_k);
+int mfi_moe_experts(const mfi_moe_weights* w, const uint8_t* xq, long long xq_ld,
+                    const uint8_t* xsc, long long xsc_ld, const int32_t* sel, long long sel_ld,
+                    const float* selw, long long selw_ld, int R, float* out, long long out_ld,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Expert-parallel exchange (no reference counterpart).  N ranks each own
+ * experts_per_rank consecutive experts (global expert e lives on rank
+ * e / experts_per_rank).  A send buffer holds one block per destination rank
+ * of (capacity + 1) rows of mfi_ep_row_bytes() bytes: a header row whose
+ * first int32 is the block's row count, then one row per (token,
+ * destination) pair:
+ *   [0, hidden/2) packed nibbles | [hidden/2, +hidden/32) E8M0 codes |
+ *   int32 token, 3 pad | top_k int32 local expert ids (-1 = other rank) |
+ *   top_k fp32 routing weights | zero padding to a multiple of 16 bytes
+ * Exchanging the blocks with an equal-split all-to-all needs no host
+ * synchronisation; the receiver runs mfi_ep_mask_recv and then
+ * mfi_moe_experts over all n_ranks * (capacity + 1) rows (xq at row offset 0,
+ * xsc at hidden/2, sel and selw at the offsets above, all with stride
+ * row_bytes), returns the fp32 rows with a second all-to-all, and the source
+ * sums them with mfi_ep_unpack.
+ * ------------------------------------------------------------------------ */
+
+/* Row size in bytes (0 for invalid arguments: hidden % 128, top_k 1..32). */
+int mfi_ep_row_bytes(int hidden, int top_k);
+
+/* Pack routed tokens (xq/xsc/topi/topw of mfi_moe_route) into `send`.
+ * counts: int32 device scratch [n_ranks]; pack_pos: int32 (T, n_ranks)
+ * receives each pair's row in its destination block (-1: none).
+ * capacity >= T; n_ranks <= 64. */
+int mfi_ep_pack(const uint8_t* xq, const uint8_t* xsc, const int32_t* topi, const float* topw,
+                int T, int hidden, int top_k, int n_ranks, int experts_per_rank, int capacity,
+                int32_t* counts, uint8_t* send, int32_t* pack_pos, void* stream);
+
+/* Mark the header row and the unused rows of every received block as having
+ * no local expert (all ids -1), reading each block's count from its header. */
+int mfi_ep_mask_recv(uint8_t* recv, int n_ranks, int capacity, int hidden, int top_k,
+                     void* stream);
+
+/* out[t] (fp32, hidden) = sum over ranks d = 0..n_ranks-1 in order, where
+ * pack_pos[t][d] >= 0, of row 1 + pack_pos[t][d] of returned block d
+ * (ret: fp32 [n_ranks][capacity + 1][hidden]). */
+int mfi_ep_unpack(const float* ret, const int32_t* pack_pos, int T, int n_ranks, int capacity,
+                  int hidden, float* out, void* stream);
 
 #ifdef __cplusplus
 }

@@ -43,6 +43,14 @@ SIGNATURES = {
     "mfi_moe_layer_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
     "mfi_moe_layer": (_I, [_VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _SZ, _VP]),
     "mfi_moe_layer_ex": (_I, [_VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _SZ, _VP, _I, _VP]),
+    "mfi_moe_route": (_I, [_VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _VP]),
+    "mfi_moe_experts_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
+    "mfi_moe_experts": (_I, [_VP, _VP, _LL, _VP, _LL, _VP, _LL, _VP, _LL, _I, _VP, _LL, _VP, _SZ,
+                             _VP]),
+    "mfi_ep_row_bytes": (_I, [_I, _I]),
+    "mfi_ep_pack": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _I, _VP, _VP, _VP, _VP]),
+    "mfi_ep_mask_recv": (_I, [_VP, _I, _I, _I, _I, _VP]),
+    "mfi_ep_unpack": (_I, [_VP, _VP, _I, _I, _I, _I, _VP, _VP]),
 }
 
 MFI_F32, MFI_F16, MFI_BF16 = 0, 1, 2

@@ -63,7 +63,7 @@ extern "C" {
 
 const char* mfi_last_error(void) { return g_err.c_str(); }
 
-int mfi_version(void) { return 1; }
+int mfi_version(void) { return 2; }
 
 // ---------------------------------------------------------------------------
 int mfi_quantize_rows(const void* x, int dtype, long long ld_x, int half_roundtrip, uint8_t* xq,
@@ -465,6 +465,185 @@ int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float*
                    "moe_layer combine launch");
   if (rc != MFI_OK) return rc;
   return mark(5);
+}
+
+// ---------------------------------------------------------------------------
+// Routing alone and expert compute on pre-routed rows: the two halves of
+// mfi_moe_layer that expert parallelism puts a token exchange between.
+
+int mfi_moe_route(const mfi_moe_weights* w, const void* x_bf16, int T, uint8_t* xq, uint8_t* xsc,
+                  int32_t* topi, float* topw, float* logits, void* stream) {
+  if (!w) return fail(MFI_ERR_ARG, "null weights");
+  const int E = w->n_experts, H = w->hidden, k = w->top_k;
+  if (E <= 0 || E > mfi::kRouteMaxE) return fail(MFI_ERR_ARG, "n_experts must be in [1, 256]");
+  if (H <= 0 || H % 32 != 0 || H > 4096)
+    return fail(MFI_ERR_ARG, "hidden must be a positive multiple of 32, <= 4096");
+  if (k <= 0 || k > E || k > 32) return fail(MFI_ERR_ARG, "top_k must be in [1, min(E, 32)]");
+  if (T < 0) return fail(MFI_ERR_ARG, "T must be >= 0");
+  if (T == 0) return MFI_OK;
+  if (bad_ptr(x_bf16) || bad_ptr(xq) || bad_ptr(xsc) || bad_ptr(topi) || bad_ptr(topw) ||
+      bad_ptr(w->router_wp) || bad_ptr(w->router_sc))
+    return fail(MFI_ERR_ARG, "null pointer");
+  if ((reinterpret_cast<uintptr_t>(x_bf16) & 15) != 0 || (reinterpret_cast<uintptr_t>(xq) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(xsc) & 3) != 0)
+    return fail(MFI_ERR_ARG, "x and xq must be 16-byte aligned, xsc 4-byte aligned");
+  mfi::RouteArgs ra{};
+  ra.x = x_bf16; ra.xq = xq; ra.xsc = xsc; ra.wr = w->router_wp; ra.sr = w->router_sc;
+  ra.T = T; ra.H = H; ra.E = E; ra.k = k;
+  ra.logits = logits; ra.topi = topi; ra.topw = topw;
+  // no work lists, no expert regions: the kernel stops after the routing
+  return cuda_status(mfi::launch_route(ra, as_stream(stream)), "moe_route launch");
+}
+
+namespace {
+struct ExpertScratch {
+  int* cursor;
+  int* perm;
+  uint8_t* xp;
+  uint8_t* xp_atoms;
+  uint8_t* hp;
+  uint8_t* hp_atoms;
+  float* yd;
+  int T_pad;
+  size_t bytes;
+};
+
+ExpertScratch carve_experts(void* ws, int R, int H, int Mi, int E, int k) {
+  Carve c(ws);
+  ExpertScratch s;
+  s.T_pad = (R + 31) / 32 * 32;
+  const size_t rows = size_t(E) * s.T_pad;
+  s.cursor = c.take<int>(size_t(E));
+  s.perm = c.take<int>(rows);
+  s.xp = c.take<uint8_t>(rows * (H / 2));
+  s.xp_atoms = c.take<uint8_t>(rows / 32 * (H / 128) * 512);
+  s.hp = c.take<uint8_t>(rows * (Mi / 2));
+  s.hp_atoms = c.take<uint8_t>(rows / 32 * (Mi / 128) * 512);
+  s.yd = c.take<float>(size_t(R) * k * H);
+  s.bytes = c.used + 256;
+  return s;
+}
+}  // namespace
+
+size_t mfi_moe_experts_workspace_bytes(int R, int hidden, int inter, int n_experts, int top_k) {
+  if (R < 0 || hidden <= 0 || inter <= 0 || n_experts <= 0 || top_k <= 0) return 0;
+  return carve_experts(nullptr, R, hidden, inter, n_experts, top_k).bytes;
+}
+
+int mfi_moe_experts(const mfi_moe_weights* w, const uint8_t* xq, long long xq_ld,
+                    const uint8_t* xsc, long long xsc_ld, const int32_t* sel, long long sel_ld,
+                    const float* selw, long long selw_ld, int R, float* out, long long out_ld,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  if (!w) return fail(MFI_ERR_ARG, "null weights");
+  const int E = w->n_experts, H = w->hidden, Mi = w->inter, k = w->top_k;
+  if (E <= 0 || E > mfi::kRouteMaxE) return fail(MFI_ERR_ARG, "n_experts must be in [1, 256]");
+  if (!layer_uses_tc(H, Mi))
+    return fail(MFI_ERR_ARG, "moe_experts needs hidden and inter to be multiples of 256");
+  if (k <= 0 || k > 32) return fail(MFI_ERR_ARG, "top_k must be in [1, 32]");
+  if (R < 0 || (long long)R * k > 16384) return fail(MFI_ERR_ARG, "rows * top_k must be <= 16384");
+  if (R == 0) return MFI_OK;
+  if (bad_ptr(xq) || bad_ptr(xsc) || bad_ptr(sel) || bad_ptr(selw) || bad_ptr(out) ||
+      bad_ptr(workspace) || bad_ptr(w->prepared))
+    return fail(MFI_ERR_ARG, "null pointer (weights.prepared comes from mfi_moe_prepare)");
+  if (xq_ld < H / 2 || xsc_ld < H / 32 || sel_ld < k || selw_ld < k || out_ld < H)
+    return fail(MFI_ERR_ARG, "row strides must cover one row");
+  if ((reinterpret_cast<uintptr_t>(xq) & 15) != 0 || xq_ld % 16 != 0 ||
+      (reinterpret_cast<uintptr_t>(xsc) & 3) != 0 || xsc_ld % 4 != 0)
+    return fail(MFI_ERR_ARG, "xq rows must be 16-byte aligned, xsc rows 4-byte aligned");
+  if (workspace_bytes < mfi_moe_experts_workspace_bytes(R, H, Mi, E, k))
+    return fail(MFI_ERR_WORKSPACE, "workspace too small for moe_experts");
+  ExpertScratch s = carve_experts(workspace, R, H, Mi, E, k);
+  cudaStream_t st = as_stream(stream);
+  int rc = cuda_status(cudaMemsetAsync(s.cursor, 0, sizeof(int) * size_t(E), st),
+                       "moe_experts memset");
+  if (rc != MFI_OK) return rc;
+  rc = cuda_status(mfi::launch_scatter_sel(xq, xq_ld, xsc, xsc_ld, sel, sel_ld, R, k, H, E, s.T_pad,
+                                           s.cursor, s.perm, s.xp, s.xp_atoms,
+                                           mfi::device_error_flag(), st),
+                   "moe_experts scatter launch");
+  if (rc != MFI_OK) return rc;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  mfi::MoeTcLaunch L{};
+  L.E = E; L.H = H; L.Mi = Mi; L.grid = sms;
+  L.max_chunks = int((size_t(E) < size_t(R) * k ? size_t(E) : size_t(R) * k) +
+                     (size_t(R) * k + 31) / 32);
+  L.prepared = static_cast<const uint8_t*>(w->prepared);
+  L.counts = s.cursor; L.perm = s.perm;
+  L.rows = E * s.T_pad;
+  L.xp = s.xp; L.xp_atoms = s.xp_atoms; L.hp = s.hp; L.hp_atoms = s.hp_atoms; L.yd = s.yd;
+  L.err = mfi::device_error_flag();
+  L.gate_up = true;
+  rc = cuda_status(mfi::launch_moe_tc(L, st), "moe_experts gate/up launch");
+  if (rc != MFI_OK) return rc;
+  L.gate_up = false;
+  rc = cuda_status(mfi::launch_moe_tc(L, st), "moe_experts down launch");
+  if (rc != MFI_OK) return rc;
+  return cuda_status(mfi::launch_combine_sel(s.yd, sel, sel_ld, selw, selw_ld, R, k, E, H, out,
+                                             out_ld, st),
+                     "moe_experts combine launch");
+}
+
+// ---------------------------------------------------------------------------
+// Expert-parallel exchange buffers.
+
+int mfi_ep_row_bytes(int hidden, int top_k) {
+  if (hidden <= 0 || hidden % 128 != 0 || top_k <= 0 || top_k > 32) return 0;
+  return mfi::ep_row_bytes(hidden, top_k);
+}
+
+namespace {
+int ep_check(int T, int H, int k, int n_ranks, int C) {
+  if (H <= 0 || H % 128 != 0 || H > 4096)
+    return fail(MFI_ERR_ARG, "hidden must be a positive multiple of 128, <= 4096");
+  if (k <= 0 || k > 32) return fail(MFI_ERR_ARG, "top_k must be in [1, 32]");
+  if (n_ranks <= 0 || n_ranks > 64) return fail(MFI_ERR_ARG, "n_ranks must be in [1, 64]");
+  if (T < 0 || C < T) return fail(MFI_ERR_ARG, "capacity must be >= T >= 0");
+  return MFI_OK;
+}
+}  // namespace
+
+int mfi_ep_pack(const uint8_t* xq, const uint8_t* xsc, const int32_t* topi, const float* topw,
+                int T, int hidden, int top_k, int n_ranks, int experts_per_rank, int capacity,
+                int32_t* counts, uint8_t* send, int32_t* pack_pos, void* stream) {
+  int rc = ep_check(T, hidden, top_k, n_ranks, capacity);
+  if (rc != MFI_OK) return rc;
+  if (experts_per_rank <= 0) return fail(MFI_ERR_ARG, "experts_per_rank must be positive");
+  if (bad_ptr(counts) || bad_ptr(send) || (T > 0 && (bad_ptr(xq) || bad_ptr(xsc) ||
+                                                      bad_ptr(topi) || bad_ptr(topw) ||
+                                                      bad_ptr(pack_pos))))
+    return fail(MFI_ERR_ARG, "null pointer");
+  if ((reinterpret_cast<uintptr_t>(send) & 15) != 0 || (reinterpret_cast<uintptr_t>(xq) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(xsc) & 3) != 0)
+    return fail(MFI_ERR_ARG, "send and xq must be 16-byte aligned, xsc 4-byte aligned");
+  return cuda_status(mfi::launch_ep_pack(xq, xsc, topi, topw, T, hidden, top_k, n_ranks,
+                                         experts_per_rank, capacity, counts, send, pack_pos,
+                                         as_stream(stream)),
+                     "ep_pack launch");
+}
+
+int mfi_ep_mask_recv(uint8_t* recv, int n_ranks, int capacity, int hidden, int top_k,
+                     void* stream) {
+  int rc = ep_check(0, hidden, top_k, n_ranks, capacity);
+  if (rc != MFI_OK) return rc;
+  if (bad_ptr(recv)) return fail(MFI_ERR_ARG, "null pointer");
+  if ((reinterpret_cast<uintptr_t>(recv) & 15) != 0)
+    return fail(MFI_ERR_ARG, "recv must be 16-byte aligned");
+  return cuda_status(mfi::launch_ep_mask_recv(n_ranks, capacity, hidden, top_k, recv,
+                                              as_stream(stream)),
+                     "ep_mask_recv launch");
+}
+
+int mfi_ep_unpack(const float* ret, const int32_t* pack_pos, int T, int n_ranks, int capacity,
+                  int hidden, float* out, void* stream) {
+  int rc = ep_check(T, hidden, 1, n_ranks, capacity);
+  if (rc != MFI_OK) return rc;
+  if (T == 0) return MFI_OK;
+  if (bad_ptr(ret) || bad_ptr(pack_pos) || bad_ptr(out)) return fail(MFI_ERR_ARG, "null pointer");
+  return cuda_status(mfi::launch_ep_unpack(ret, pack_pos, T, n_ranks, capacity, hidden, out,
+                                           as_stream(stream)),
+                     "ep_unpack launch");
 }
 
 }  // extern "C"

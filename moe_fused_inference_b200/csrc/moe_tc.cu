@@ -62,7 +62,10 @@ constexpr uint32_t kTmemSFB = kTmemSFA + 8;
 constexpr int kChunk = 32;     // tokens per chunk (MMA N)
 
 constexpr int kMaxExperts = 256;
-constexpr int kMaxChunks = kMaxExperts + 4096 / kChunk;
+// pairs (token, expert) per launch: T * top_k <= 4096 from the fused layer,
+// rows * top_k <= 16384 from mfi_moe_experts
+constexpr int kMaxPairs = 16384;
+constexpr int kMaxChunks = kMaxExperts + kMaxPairs / kChunk;
 
 struct MoeTcArgs {
   const int* counts;           // tokens routed to each expert (route.cu cursors)
@@ -109,7 +112,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   __shared__ int s_cnt[kMaxExperts];
   __shared__ int s_chunk[kMaxChunks];
   __shared__ int s_nchunks;
-  for (int e = threadIdx.x; e < p.E; e += blockDim.x) s_cnt[e] = p.counts[e];
+  for (int e = threadIdx.x; e < p.E; e += blockDim.x) s_cnt[e] = min(p.counts[e], p.T_pad);
   __syncthreads();
   if (warp == 0) {
     int run = 0;
@@ -122,10 +125,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         const int v = __shfl_up_sync(0xffffffffu, inc, off);
         if (lane >= off) inc += v;
       }
-      for (int c = 0; c < nch; ++c) s_chunk[run + inc - nch + c] = e | (c << 16);
+      for (int c = 0; c < nch; ++c)
+        if (run + inc - nch + c < kMaxChunks) s_chunk[run + inc - nch + c] = e | (c << 16);
       run += __shfl_sync(0xffffffffu, inc, 31);
     }
-    if (lane == 0) s_nchunks = run;
+    if (lane == 0) s_nchunks = min(run, kMaxChunks);
   }
 
   if (threadIdx.x == 0) {

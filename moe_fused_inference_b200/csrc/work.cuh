@@ -124,6 +124,23 @@ cudaError_t launch_gather_chunks(const uint8_t* xq, const uint8_t* xsc, const in
                                  uint8_t* xp_atoms, cudaStream_t stream);
 cudaError_t launch_moe_tc(const MoeTcLaunch& L, cudaStream_t stream);
 
+// Expert parallelism and pre-routed rows (ep.cu).
+int ep_row_bytes(int H, int k);
+cudaError_t launch_ep_pack(const uint8_t* xq, const uint8_t* xsc, const int* topi,
+                           const float* topw, int T, int H, int k, int n_ranks, int e_local, int C,
+                           int* counts, uint8_t* send, int* pack_pos, cudaStream_t stream);
+cudaError_t launch_ep_mask_recv(int n_ranks, int C, int H, int k, uint8_t* recv,
+                                cudaStream_t stream);
+cudaError_t launch_ep_unpack(const float* ret, const int* pack_pos, int T, int n_ranks, int C,
+                             int H, float* out, cudaStream_t stream);
+cudaError_t launch_scatter_sel(const uint8_t* xq, long long xq_ld, const uint8_t* xsc,
+                               long long xsc_ld, const int* sel, long long sel_ld, int R, int k,
+                               int H, int E, int T_pad, int* cursor, int* perm, uint8_t* xp,
+                               uint8_t* xp_atoms, int* status, cudaStream_t stream);
+cudaError_t launch_combine_sel(const float* yd, const int* sel, long long sel_ld, const float* w,
+                               long long w_ld, int R, int k, int E, int H, float* out,
+                               long long out_ld, cudaStream_t stream);
+
 // Device-wide error flag written by kernels whose bounded waits time out.
 int* device_error_flag();
 

@@ -43,7 +43,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_workspace_queries_are_pure_host(lib):
-    assert lib.mfi_version() == 1
+    assert lib.mfi_version() == 2
     assert lib.mfi_moe_layer_workspace_bytes(64, 2048, 768, 128, 8) > 64 * 8 * 2048 * 4
     assert lib.mfi_moe_gateup_workspace_bytes(8, 1) >= 16 * (24 + 16)
     assert lib.mfi_linear_workspace_bytes(16, 256, 2048) >= 16 * (1024 + 64)
