@@ -385,6 +385,7 @@ def run_ours(args, world, rank, local):
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind,
                      "algorithmic_bytes_per_step": w_bytes,
+                     "algorithmic_bytes_per_layer_call": w_bytes / NL,
                      "traffic": (traffic or {}).get("bytes_per_layer_call"),
                      "traffic_source": (traffic or {}).get("source"),
                      "layer": {"achieved": layer_bytes / (ms_per_step / 1e3) / 1e9,
