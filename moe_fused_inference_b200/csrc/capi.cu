@@ -53,6 +53,21 @@ constexpr int kTcMinM = 64;
 
 bool bad_ptr(const void* p) { return p == nullptr; }
 
+// Speculative L2 prefetch of expert weights by the tensor-core expert launches
+// (issued while the kernel before them runs).  Only when routing is dense
+// enough that nearly every expert is active (pairs >= 2 x experts), so the
+// blocks fetched in storage order are the ones the launch reads first.
+#ifndef MFI_PF_GATEUP_MB
+#define MFI_PF_GATEUP_MB 64
+#endif
+#ifndef MFI_PF_DOWN_MB
+#define MFI_PF_DOWN_MB 32
+#endif
+size_t prefetch_bytes(long long pairs, int E, bool gate_up) {
+  if (pairs < 2LL * E) return 0;
+  return size_t(gate_up ? MFI_PF_GATEUP_MB : MFI_PF_DOWN_MB) << 20;
+}
+
 }  // namespace
 
 namespace mfi {
@@ -405,8 +420,9 @@ int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float*
   rc = cuda_status(cudaMemsetAsync(s.done, 0, sizeof(unsigned) * (1 + size_t(E)), st),
                    "moe_layer memset");
   if (rc != MFI_OK) return rc;
-  if ((reinterpret_cast<uintptr_t>(x_bf16) & 15) != 0)
-    return fail(MFI_ERR_ARG, "x must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(x_bf16) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(w->router_wp) & 15) != 0)
+    return fail(MFI_ERR_ARG, "x and router_wp must be 16-byte aligned");
   const bool tc = layer_uses_tc(H, Mi);
   mfi::RouteArgs ra{};
   ra.x = x_bf16;
@@ -424,6 +440,7 @@ int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float*
   ra.xp = tc ? s.xp : nullptr;
   ra.xp_atoms = tc ? s.xp_atoms : nullptr;
   ra.T_pad = s.T_pad;
+  ra.err = mfi::device_error_flag();
   rc = cuda_status(mfi::launch_route(ra, st), "moe_layer route launch");
   if (rc != MFI_OK || (rc = mark(1)) != MFI_OK) return rc;
   const int P = T * k;
@@ -440,10 +457,15 @@ int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float*
     L.rows = E * s.T_pad;
     L.xp = s.xp; L.xp_atoms = s.xp_atoms; L.hp = s.hp; L.hp_atoms = s.hp_atoms; L.yd = s.yd;
     L.err = mfi::device_error_flag();
+    // kernels overlap their prologue with the previous kernel's tail, except
+    // when stage events sit between them
+    L.pdl = events == nullptr;
     L.gate_up = true;
+    L.pf_bytes = prefetch_bytes(P, E, true);
     rc = cuda_status(mfi::launch_moe_tc(L, st), "moe_layer gate/up (tensor cores) launch");
     if (rc != MFI_OK || (rc = mark(3)) != MFI_OK) return rc;
     L.gate_up = false;
+    L.pf_bytes = prefetch_bytes(P, E, false);
     rc = cuda_status(mfi::launch_moe_tc(L, st), "moe_layer down (tensor cores) launch");
     if (rc != MFI_OK || (rc = mark(4)) != MFI_OK) return rc;
   } else {
@@ -461,7 +483,7 @@ int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float*
                      "moe_layer down launch");
     if (rc != MFI_OK || (rc = mark(4)) != MFI_OK) return rc;
   }
-  rc = cuda_status(mfi::launch_combine(s.yd, H, topw, k, k, out, T, H, st),
+  rc = cuda_status(mfi::launch_combine(s.yd, H, topw, k, k, out, T, H, st, tc && !events),
                    "moe_layer combine launch");
   if (rc != MFI_OK) return rc;
   return mark(5);
@@ -485,12 +507,14 @@ int mfi_moe_route(const mfi_moe_weights* w, const void* x_bf16, int T, uint8_t* 
       bad_ptr(w->router_wp) || bad_ptr(w->router_sc))
     return fail(MFI_ERR_ARG, "null pointer");
   if ((reinterpret_cast<uintptr_t>(x_bf16) & 15) != 0 || (reinterpret_cast<uintptr_t>(xq) & 15) != 0 ||
-      (reinterpret_cast<uintptr_t>(xsc) & 3) != 0)
-    return fail(MFI_ERR_ARG, "x and xq must be 16-byte aligned, xsc 4-byte aligned");
+      (reinterpret_cast<uintptr_t>(xsc) & 3) != 0 ||
+      (reinterpret_cast<uintptr_t>(w->router_wp) & 15) != 0)
+    return fail(MFI_ERR_ARG, "x, xq and router_wp must be 16-byte aligned, xsc 4-byte aligned");
   mfi::RouteArgs ra{};
   ra.x = x_bf16; ra.xq = xq; ra.xsc = xsc; ra.wr = w->router_wp; ra.sr = w->router_sc;
   ra.T = T; ra.H = H; ra.E = E; ra.k = k;
   ra.logits = logits; ra.topi = topi; ra.topw = topw;
+  ra.err = mfi::device_error_flag();
   // no work lists, no expert regions: the kernel stops after the routing
   return cuda_status(mfi::launch_route(ra, as_stream(stream)), "moe_route launch");
 }
@@ -574,10 +598,13 @@ int mfi_moe_experts(const mfi_moe_weights* w, const uint8_t* xq, long long xq_ld
   L.rows = E * s.T_pad;
   L.xp = s.xp; L.xp_atoms = s.xp_atoms; L.hp = s.hp; L.hp_atoms = s.hp_atoms; L.yd = s.yd;
   L.err = mfi::device_error_flag();
+  L.pdl = true;
   L.gate_up = true;
+  L.pf_bytes = prefetch_bytes((long long)R * k, E, true);
   rc = cuda_status(mfi::launch_moe_tc(L, st), "moe_experts gate/up launch");
   if (rc != MFI_OK) return rc;
   L.gate_up = false;
+  L.pf_bytes = prefetch_bytes((long long)R * k, E, false);
   rc = cuda_status(mfi::launch_moe_tc(L, st), "moe_experts down launch");
   if (rc != MFI_OK) return rc;
   return cuda_status(mfi::launch_combine_sel(s.yd, sel, sel_ld, selw, selw_ld, R, k, E, H, out,

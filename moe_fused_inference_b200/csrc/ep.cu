@@ -18,6 +18,7 @@
 //   k x int32 local expert id (-1 = none) | k x f32 weight | padding
 #include "mx_common.cuh"
 #include "work.cuh"
+#include "tc_ptx.cuh"
 
 namespace mfi {
 
@@ -118,6 +119,7 @@ __global__ void __launch_bounds__(128) scatter_sel_kernel(
     long long xsc_ld, const int* __restrict__ sel, long long sel_ld, int R, int k, int H, int E,
     int T_pad, int* __restrict__ cursor, int* __restrict__ perm, uint8_t* __restrict__ xp,
     uint8_t* __restrict__ xp_atoms, int* __restrict__ status) {
+  tc::grid_dep_launch();
   const int r = blockIdx.x;
   __shared__ int s_row[32];
   if (threadIdx.x < k) {
@@ -155,6 +157,7 @@ __global__ void __launch_bounds__(128) scatter_sel_kernel(
 __global__ void combine_sel_kernel(const float* __restrict__ yd, const int* __restrict__ sel,
                                    long long sel_ld, const float* __restrict__ w, long long w_ld,
                                    int k, int E, int H, float* __restrict__ out, long long out_ld) {
+  tc::grid_dep_wait();  // yd comes from the previous kernel
   const int m = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= H) return;
@@ -214,9 +217,17 @@ cudaError_t launch_combine_sel(const float* yd, const int* sel, long long sel_ld
                                long long w_ld, int R, int k, int E, int H, float* out,
                                long long out_ld, cudaStream_t stream) {
   if (R == 0) return cudaSuccess;
-  dim3 grid((H + 255) / 256, R);
-  combine_sel_kernel<<<grid, 256, 0, stream>>>(yd, sel, sel_ld, w, w_ld, k, E, H, out, out_ld);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((H + 255) / 256, R);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, combine_sel_kernel, yd, sel, sel_ld, w, w_ld, k, E, H, out,
+                            out_ld);
 }
 
 }  // namespace mfi

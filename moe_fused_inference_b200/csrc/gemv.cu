@@ -15,6 +15,7 @@
 // xor-butterfly across the warp.  The result is deterministic run to run.
 #include "mx_common.cuh"
 #include "work.cuh"
+#include "tc_ptx.cuh"
 
 namespace mfi {
 
@@ -287,6 +288,7 @@ cudaError_t launch_build_groups(const uint8_t* const* wp_tab, const uint8_t* con
 __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ yd, long ystride,
                                                       const float* __restrict__ w, int E, int E_sum,
                                                       float* __restrict__ out, int M, int N) {
+  tc::grid_dep_wait();  // yd comes from the previous kernel
   const int m = blockIdx.y;
   const int c4 = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (m >= M || c4 >= N) return;
@@ -313,11 +315,18 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
 }
 
 cudaError_t launch_combine(const float* yd, long ystride, const float* w, int E, int E_sum,
-                           float* out, int M, int N, cudaStream_t stream) {
+                           float* out, int M, int N, cudaStream_t stream, bool pdl) {
   if (M == 0 || N == 0) return cudaSuccess;
-  dim3 grid((N / 4 + 255) / 256 + 1, M);
-  combine_kernel<<<grid, 256, 0, stream>>>(yd, ystride, w, E, E_sum, out, M, N);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((N / 4 + 255) / 256 + 1, M);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, combine_kernel, yd, ystride, w, E, E_sum, out, M, N);
 }
 
 }  // namespace mfi

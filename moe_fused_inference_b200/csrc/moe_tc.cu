@@ -37,11 +37,13 @@ using namespace tc;
 
 namespace {
 
+// 2 CTAs per SM x 3 stages measured faster than 1 x 8 (two epilogues and two
+// load streams per SM; the ring depth is not the limit)
 #ifndef MFI_TC_STAGES
-#define MFI_TC_STAGES 8
+#define MFI_TC_STAGES 3
 #endif
 #ifndef MFI_TC_CTAS_PER_SM
-#define MFI_TC_CTAS_PER_SM 1
+#define MFI_TC_CTAS_PER_SM 2
 #endif
 constexpr int kStages = MFI_TC_STAGES;
 constexpr int kCtasPerSm = MFI_TC_CTAS_PER_SM;
@@ -84,6 +86,10 @@ struct MoeTcArgs {
   int hidden;
   float* yd;                   // (T*k, hidden)
   int* err;
+  // speculative L2 prefetch, issued before the wait on the upstream kernels:
+  // the first pf_bytes of this launch's weight blocks (storage order = item
+  // order when every expert has one chunk), split evenly over the CTAs
+  unsigned long long pf_bytes;
 };
 
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
@@ -106,6 +112,34 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int k_stages = p.K / 256;
+
+  // prologue independent of the upstream kernels: barriers, TMEM, tensor map
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < kAccBufs; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) prefetch_tmap(&tma_b);
+  if (warp == 0 && p.pf_bytes) {
+    // weights do not depend on the routing: stream the first blocks into L2
+    // while the router (or the previous expert launch) is still running
+    const unsigned long long per =
+        ((p.pf_bytes + gridDim.x - 1) / gridDim.x + 4095) & ~4095ull;
+    const unsigned long long lo = per * blockIdx.x;
+    const unsigned long long hi = min(lo + per, p.pf_bytes);
+    for (unsigned long long off = lo + lane * 32768ull; off < hi; off += 32 * 32768ull)
+      prefetch_l2(p.wblocks + off, uint32_t(min(32768ull, hi - off)));
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  // counts, rows and activations come from the kernels before this one
+  grid_dep_wait();
+  grid_dep_launch();
 
   // chunk table from the per-expert token counts: chunk -> (expert, c), expert
   // e's tokens fill rows [e*T_pad, e*T_pad + count) in chunks of 32
@@ -132,18 +166,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     if (lane == 0) s_nchunks = min(run, kMaxChunks);
   }
 
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    for (int b = 0; b < kAccBufs; ++b) {
-      mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
-    }
-    fence_mbar_init();
-  }
-  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -162,7 +184,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 
   if (warp == 0) {
     if (elect_one()) {
-      prefetch_tmap(&tma_b);
       uint32_t it = 0;
       bool ok = true;
       for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
@@ -452,6 +473,29 @@ static cudaError_t set_smem_once(const void* fn, bool* done) {
   return e;
 }
 
+static unsigned long long cap_prefetch(size_t want, size_t region) {
+  return (unsigned long long)(want < region ? want : region) & ~15ull;
+}
+
+// Launch with programmatic stream serialisation when `pdl`: the kernel may
+// start while the previous kernel in the stream drains (it waits with
+// grid_dep_wait before reading that kernel's outputs).
+template <class Kern>
+static cudaError_t launch_ex(Kern kern, int grid, bool pdl, cudaStream_t stream,
+                             const CUtensorMap& b, const MoeTcArgs& p) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = moe_tc_smem();
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, b, p);
+}
+
 cudaError_t launch_moe_tc(const MoeTcLaunch& L, cudaStream_t stream) {
   static bool smem_gu = false, smem_dn = false;
   const int E = L.E, H = L.H, Mi = L.Mi;
@@ -476,9 +520,11 @@ cudaError_t launch_moe_tc(const MoeTcLaunch& L, cudaStream_t stream) {
     p.K = H;
     p.tiles = Mi / 64;
     p.kc_pad = H / 128;
+    p.pf_bytes = cap_prefetch(L.pf_bytes, size_t(E) * (Mi / 64) * (H / 256) * kWBlock);
     cudaError_t e = set_smem_once(reinterpret_cast<const void*>(moe_tc_kernel<true>), &smem_gu);
     if (e != cudaSuccess) return e;
-    moe_tc_kernel<true><<<grid, kThreads, moe_tc_smem(), stream>>>(b, p);
+    e = launch_ex(moe_tc_kernel<true>, grid, L.pdl, stream, b, p);
+    if (e != cudaSuccess) return e;
   } else {
     if (!get_tmap(&b, L.hp, Mi / 2, uint64_t(L.rows), kChunk))
       return cudaErrorInvalidValue;
@@ -487,9 +533,11 @@ cudaError_t launch_moe_tc(const MoeTcLaunch& L, cudaStream_t stream) {
     p.K = Mi;
     p.tiles = H / 128;
     p.kc_pad = Mi / 128;
+    p.pf_bytes = cap_prefetch(L.pf_bytes, size_t(E) * (H / 128) * (Mi / 256) * kWBlock);
     cudaError_t e = set_smem_once(reinterpret_cast<const void*>(moe_tc_kernel<false>), &smem_dn);
     if (e != cudaSuccess) return e;
-    moe_tc_kernel<false><<<grid, kThreads, moe_tc_smem(), stream>>>(b, p);
+    e = launch_ex(moe_tc_kernel<false>, grid, L.pdl, stream, b, p);
+    if (e != cudaSuccess) return e;
   }
   return cudaGetLastError();
 }

@@ -15,6 +15,7 @@
 // logits go to the lower expert index.
 #include "mx_common.cuh"
 #include "work.cuh"
+#include "tc_ptx.cuh"
 
 namespace mfi {
 
@@ -31,6 +32,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   __shared__ unsigned s_last;
   __shared__ __align__(16) uint8_t s_xq[kMaxBlk * 32 * 16];
   __shared__ __align__(16) uint8_t s_xsc[kMaxBlk * 32];
+  // the expert kernels after this one may start their prologue now
+  tc::grid_dep_launch();
   const int t = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nwarp = kRouteThreads / 32;
@@ -312,14 +315,259 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Cluster router (no work lists): one thread-block cluster per token, CTA r
+// of the cluster owns experts [32r, 32r + 32).  Each CTA stages its 32 router
+// rows in shared memory with one bulk copy issued at entry (before the expert
+// launches that start under programmatic dependent launch begin streaming
+// their weights), quantises the token (redundantly: 4 KB of input), computes
+// its 32 logits with the same per-lane order and butterfly as route_kernel,
+// and stores them into the leader CTA's shared memory through distributed
+// shared memory.  The leader then runs top-k, the weights and the expert-row
+// claims.  Logits are bit-identical to route_kernel's.
+constexpr int kClusterThreads = 256;
+constexpr int kExpertsPerCta = 32;
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Store a float into CTA `rank`'s shared memory at the address of `local`.
+__device__ __forceinline__ void st_cluster_f32(const void* local, uint32_t rank, float v) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+               : "=r"(remote)
+               : "r"(tc::smem_u32(local)), "r"(rank));
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
+}
+
+template <int kMaxBlk>
+__global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArgs a, int n_split) {
+  tc::grid_dep_launch();
+  extern __shared__ __align__(128) uint8_t s_w[];  // [32][H/2] router rows of this CTA
+  __shared__ float s_logit[kMaxE];
+  __shared__ __align__(16) uint8_t s_xq[kMaxBlk * 32 * 16];
+  __shared__ __align__(16) uint8_t s_xsc[kMaxBlk * 32];
+  __shared__ uint8_t s_ws[kExpertsPerCta * kMaxBlk * 32];
+  __shared__ __align__(8) uint64_t s_bar;
+  const uint32_t crank = cluster_ctarank();
+  const int t = blockIdx.x / n_split;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nb = a.H >> 5;
+  const int e_begin = int(crank) * kExpertsPerCta;
+  const int n_e = min(kExpertsPerCta, a.E - e_begin);
+  const uint32_t w_bytes = uint32_t(n_e) * uint32_t(a.H >> 1);
+
+  // router rows first: their loads should not queue behind the weight
+  // prefetch of the expert kernels
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&s_bar, 1);
+    tc::fence_mbar_init();
+    if (n_e > 0) {
+      tc::mbar_expect_tx(&s_bar, w_bytes);
+      tc::bulk_load(s_w, a.wr + size_t(e_begin) * (a.H >> 1), w_bytes, &s_bar);
+    }
+  }
+  // the leader's logits start at 0 so that a failed peer leaves finite values
+  if (crank == 0)
+    for (int e = threadIdx.x; e < a.E; e += kClusterThreads) s_logit[e] = 0.0f;
+  cluster_arrive_release();  // every CTA of the cluster has started (and the init is ordered)
+  for (int i = threadIdx.x; i < n_e * nb; i += kClusterThreads)
+    s_ws[i] = a.sr[size_t(e_begin) * nb + i];
+
+  // ---- quantise token t ----------------------------------------------------
+  for (int base = warp * 32; base < (a.H >> 3); base += kClusterThreads) {
+    const int c8 = base + lane;
+    const bool live = c8 < (a.H >> 3);
+    float v[8];
+    if (live) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(
+          reinterpret_cast<const __nv_bfloat16*>(a.x) + long(t) * a.H + c8 * 8);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h2[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+    }
+    BlockScale bs;
+    const uint32_t word = quant_group8(v, bs);
+    if (live) {
+      reinterpret_cast<uint32_t*>(s_xq)[c8] = word;
+      if ((c8 & 3) == 0) s_xsc[c8 >> 2] = bs.code;
+    }
+  }
+  __syncthreads();
+  if (crank == 0) {
+    for (int i = threadIdx.x; i < (a.H >> 3); i += kClusterThreads)
+      reinterpret_cast<uint32_t*>(a.xq + long(t) * (a.H >> 1))[i] = reinterpret_cast<uint32_t*>(s_xq)[i];
+    for (int i = threadIdx.x; i < nb; i += kClusterThreads) a.xsc[long(t) * nb + i] = s_xsc[i];
+  }
+
+  // ---- 32 logits: warp w owns local experts w, w+8, w+16, w+24 --------------
+  const bool have_w = n_e > 0 && tc::mbar_wait(&s_bar, 0, a.err, 6);
+  uint32_t xa8[kMaxBlk][8];
+  int xs[kMaxBlk];
+#pragma unroll
+  for (int j = 0; j < kMaxBlk; ++j) {
+    const int b = lane + 32 * j;
+    if (b < nb) {
+      const uint4 q = reinterpret_cast<const uint4*>(s_xq)[b];
+      nib8_to_i8(q.x, xa8[j][0], xa8[j][1]);
+      nib8_to_i8(q.y, xa8[j][2], xa8[j][3]);
+      nib8_to_i8(q.z, xa8[j][4], xa8[j][5]);
+      nib8_to_i8(q.w, xa8[j][6], xa8[j][7]);
+      xs[j] = s_xsc[b];
+    }
+  }
+  constexpr int kU = 4;
+  constexpr int kWarps = kClusterThreads / 32;
+  double acc[kU];
+#pragma unroll
+  for (int u = 0; u < kU; ++u) {
+    const int el = warp + u * kWarps;
+    acc[u] = 0.0;
+#pragma unroll
+    for (int j = 0; j < kMaxBlk; ++j) {
+      const int b = lane + 32 * j;
+      if (have_w && el < n_e && b < nb) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(s_w + size_t(el) * (a.H >> 1) + b * 16);
+        const int sc = s_ws[el * nb + b];
+        const int sdot = block_dot_pre(wv, xa8[j]);
+        acc[u] += double(sdot) * exp2i_d(xs[j] + sc - 256);
+      }
+    }
+  }
+  // reduce-scatter butterfly (same pairwise sums as route_kernel)
+  int n = kU;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    if (n > 1) {
+      const bool upper = (lane & off) != 0;
+      const int h = n >> 1;
+#pragma unroll
+      for (int i = 0; i < kU / 2; ++i) {
+        if (i < h) {
+          const double send = upper ? acc[i] : acc[i + h];
+          const double keep = upper ? acc[i + h] : acc[i];
+          acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+      }
+      n = h;
+    } else {
+      acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], off);
+    }
+  }
+  cluster_wait_acquire();  // the leader has started (its shared memory exists)
+  if ((lane & 7) == 0) {
+    const int el = warp + (lane >> 3) * kWarps;
+    if (have_w && el < n_e) st_cluster_f32(&s_logit[e_begin + el], 0, float(acc[0]));
+  }
+  cluster_arrive_release();
+  cluster_wait_acquire();
+  if (crank != 0) return;
+
+  if (a.logits)
+    for (int e = threadIdx.x; e < a.E; e += kClusterThreads) a.logits[long(t) * a.E + e] = s_logit[e];
+
+  // ---- top-k, weights, expert-row claims (leader) ----------------------------
+  __shared__ int s_sel[32];
+  __shared__ float s_selv[32];
+  for (int e = threadIdx.x; e < a.E; e += kClusterThreads) {
+    const float v = s_logit[e];
+    int rank = 0;
+    for (int j = 0; j < a.E; ++j) rank += better(s_logit[j], j, v, e) ? 1 : 0;
+    if (rank < a.k) {
+      s_sel[rank] = e;
+      s_selv[rank] = v;
+    }
+  }
+  __syncthreads();
+  __shared__ int s_row[32];
+  if (warp == 0) {
+    const float mx = s_selv[0];
+    const float p = (lane < a.k) ? expf(s_selv[lane < a.k ? lane : 0] - mx) : 0.f;
+    float sum = 0.f;
+    for (int j = 0; j < a.k; ++j) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, p, j));
+    if (lane < a.k) {
+      a.topi[long(t) * a.k + lane] = s_sel[lane];
+      a.topw[long(t) * a.k + lane] = __fdiv_rn(p, sum);
+      if (a.xp) {
+        const int e = s_sel[lane];
+        const int pos = atomicAdd(a.cursor + e, 1);
+        const int row = e * a.T_pad + pos;
+        s_row[lane] = row;
+        a.perm[row] = t * a.k + lane;
+      }
+    }
+  }
+  if (a.xp) {
+    __syncthreads();
+    const int q16 = a.H >> 5;
+    for (int i = threadIdx.x; i < a.k * q16; i += kClusterThreads) {
+      const int j = i / q16, c = i % q16;
+      reinterpret_cast<uint4*>(a.xp + size_t(s_row[j]) * (a.H >> 1))[c] =
+          reinterpret_cast<const uint4*>(s_xq)[c];
+    }
+    const int kc = a.H >> 7;
+    for (int i = threadIdx.x; i < a.k * kc; i += kClusterThreads) {
+      const int j = i / kc, c = i % kc;
+      const int row = s_row[j];
+      *reinterpret_cast<uint32_t*>(a.xp_atoms + (size_t(row >> 5) * kc + c) * 512 + (row & 31) * 16) =
+          reinterpret_cast<const uint32_t*>(s_xsc)[c];
+    }
+  }
+}
+
+template <int kMaxBlk>
+static cudaError_t launch_route_cluster(const RouteArgs& a, cudaStream_t stream) {
+  static bool smem_set = false;
+  const int n_split = (a.E + kExpertsPerCta - 1) / kExpertsPerCta;  // <= 8
+  const size_t smem = size_t(kExpertsPerCta) * (a.H >> 1);
+  if (!smem_set) {
+    cudaError_t e = cudaFuncSetAttribute(route_cluster_kernel<kMaxBlk>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kExpertsPerCta * (kMaxBlk * 32 * 16));
+    if (e != cudaSuccess) return e;
+    smem_set = true;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(a.T * n_split);
+  cfg.blockDim = dim3(kClusterThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = n_split;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, route_cluster_kernel<kMaxBlk>, a, n_split);
+}
+
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t stream) {
   if (a.T <= 0) return cudaSuccess;
+  if (a.H > 4096) return cudaErrorInvalidValue;
+  if (!a.g_gu) {
+    // routing alone, or routing + expert regions for the tensor-core kernels
+    return a.H <= 2048 ? launch_route_cluster<2>(a, stream) : launch_route_cluster<4>(a, stream);
+  }
   if (a.H <= 2048)
     route_kernel<2><<<a.T, kRouteThreads, 0, stream>>>(a);
-  else if (a.H <= 4096)
-    route_kernel<4><<<a.T, kRouteThreads, 0, stream>>>(a);
   else
-    return cudaErrorInvalidValue;
+    route_kernel<4><<<a.T, kRouteThreads, 0, stream>>>(a);
   return cudaGetLastError();
 }
 

@@ -67,6 +67,7 @@ struct RouteArgs {
   uint8_t* xp;         // [E * T_pad][H/2] quantised rows per expert region
   uint8_t* xp_atoms;   // [E * T_pad / 32][H/128][512] their scale atoms
   int T_pad;
+  int* err;            // device error flag (bounded waits)
 };
 
 constexpr int kRouteMaxE = 256;
@@ -88,7 +89,7 @@ cudaError_t launch_build_groups(const uint8_t* const* wp_tab, const uint8_t* con
                                 int mode, int E, int N, GroupDesc* groups, int* n_groups,
                                 EntryDesc* entries, cudaStream_t stream);
 cudaError_t launch_combine(const float* yd, long ystride, const float* w, int E, int E_sum,
-                           float* out, int M, int N, cudaStream_t stream);
+                           float* out, int M, int N, cudaStream_t stream, bool pdl = false);
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t stream);
 
 // tcgen05 MXFP4 GEMM (tc_gemm.cu)
@@ -113,6 +114,8 @@ struct MoeTcLaunch {
   uint8_t* hp; uint8_t* hp_atoms;               // requantised h (gate/up output)
   float* yd;                                    // per-pair down output
   int* err;
+  bool pdl;                                     // programmatic dependent launch
+  size_t pf_bytes;                              // speculative L2 prefetch of weights
 };
 size_t moe_prepared_bytes(int E, int H, int Mi);
 cudaError_t launch_moe_prepare(const uint8_t* gate_wp, const uint8_t* gate_sc,
