@@ -441,6 +441,13 @@ int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float*
   ra.xp_atoms = tc ? s.xp_atoms : nullptr;
   ra.T_pad = s.T_pad;
   ra.err = mfi::device_error_flag();
+  if (tc && w->prepared && (reinterpret_cast<uintptr_t>(w->prepared) & 15) == 0) {
+    // the router issues the gate/up weight prefetch after its own loads
+    ra.pf_base = static_cast<const uint8_t*>(w->prepared);
+    ra.pf_bytes = prefetch_bytes((long long)T * k, E, true) & ~size_t(15);
+    const size_t gu_bytes = mfi::moe_prepared_bytes(E, H, Mi) / 3 * 2;
+    if (ra.pf_bytes > gu_bytes) ra.pf_bytes = gu_bytes & ~size_t(15);
+  }
   rc = cuda_status(mfi::launch_route(ra, st), "moe_layer route launch");
   if (rc != MFI_OK || (rc = mark(1)) != MFI_OK) return rc;
   const int P = T * k;
@@ -461,7 +468,7 @@ int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float*
     // when stage events sit between them
     L.pdl = events == nullptr;
     L.gate_up = true;
-    L.pf_bytes = prefetch_bytes(P, E, true);
+    L.pf_bytes = 0;  // issued by the router
     rc = cuda_status(mfi::launch_moe_tc(L, st), "moe_layer gate/up (tensor cores) launch");
     if (rc != MFI_OK || (rc = mark(3)) != MFI_OK) return rc;
     L.gate_up = false;

@@ -355,7 +355,7 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
   __shared__ float s_logit[kMaxE];
   __shared__ __align__(16) uint8_t s_xq[kMaxBlk * 32 * 16];
   __shared__ __align__(16) uint8_t s_xsc[kMaxBlk * 32];
-  __shared__ uint8_t s_ws[kExpertsPerCta * kMaxBlk * 32];
+  __shared__ __align__(16) uint8_t s_ws[kExpertsPerCta * kMaxBlk * 32];
   __shared__ __align__(8) uint64_t s_bar;
   const uint32_t crank = cluster_ctarank();
   const int t = blockIdx.x / n_split;
@@ -367,20 +367,24 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
 
   // router rows first: their loads should not queue behind the weight
   // prefetch of the expert kernels
+  const uint32_t sc_bytes = uint32_t(n_e) * uint32_t(nb);
+  const uint8_t* sc_src = a.sr + size_t(e_begin) * nb;
+  const bool sc_bulk = (sc_bytes % 16) == 0 && (reinterpret_cast<uintptr_t>(sc_src) % 16) == 0;
   if (threadIdx.x == 0) {
     tc::mbar_init(&s_bar, 1);
     tc::fence_mbar_init();
     if (n_e > 0) {
-      tc::mbar_expect_tx(&s_bar, w_bytes);
+      tc::mbar_expect_tx(&s_bar, w_bytes + (sc_bulk ? sc_bytes : 0u));
       tc::bulk_load(s_w, a.wr + size_t(e_begin) * (a.H >> 1), w_bytes, &s_bar);
+      if (sc_bulk) tc::bulk_load(s_ws, sc_src, sc_bytes, &s_bar);
     }
   }
+  if (!sc_bulk)
+    for (int i = threadIdx.x; i < n_e * nb; i += kClusterThreads) s_ws[i] = sc_src[i];
   // the leader's logits start at 0 so that a failed peer leaves finite values
   if (crank == 0)
     for (int e = threadIdx.x; e < a.E; e += kClusterThreads) s_logit[e] = 0.0f;
   cluster_arrive_release();  // every CTA of the cluster has started (and the init is ordered)
-  for (int i = threadIdx.x; i < n_e * nb; i += kClusterThreads)
-    s_ws[i] = a.sr[size_t(e_begin) * nb + i];
 
   // ---- quantise token t ----------------------------------------------------
   for (int base = warp * 32; base < (a.H >> 3); base += kClusterThreads) {
@@ -417,6 +421,15 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
 
   // ---- 32 logits: warp w owns local experts w, w+8, w+16, w+24 --------------
   const bool have_w = n_e > 0 && tc::mbar_wait(&s_bar, 0, a.err, 6);
+  if (warp == 0 && a.pf_bytes) {
+    // this token's inputs are in: start streaming the expert weights that the
+    // next kernel reads first into L2 (speculative: the routing is not known)
+    const unsigned long long per = ((a.pf_bytes + gridDim.x - 1) / gridDim.x + 4095) & ~4095ull;
+    const unsigned long long lo = per * blockIdx.x;
+    const unsigned long long hi = min(lo + per, a.pf_bytes);
+    for (unsigned long long off = lo + lane * 32768ull; off < hi; off += 32 * 32768ull)
+      tc::prefetch_l2(a.pf_base + off, uint32_t(min(32768ull, hi - off)));
+  }
   uint32_t xa8[kMaxBlk][8];
   int xs[kMaxBlk];
 #pragma unroll

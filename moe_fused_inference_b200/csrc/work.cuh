@@ -68,6 +68,10 @@ struct RouteArgs {
   uint8_t* xp_atoms;   // [E * T_pad / 32][H/128][512] their scale atoms
   int T_pad;
   int* err;            // device error flag (bounded waits)
+  // speculative L2 prefetch of the first pf_bytes at pf_base (expert weights
+  // in the order the next kernel reads them), issued once the inputs are in
+  const uint8_t* pf_base;
+  unsigned long long pf_bytes;
 };
 
 constexpr int kRouteMaxE = 256;
