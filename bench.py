@@ -380,8 +380,8 @@ def run_ours(args, world, rank, local):
                    "l2": f"inputs larger than L2: {NL} distinct layer weight sets "
                          f"({NL * E * EXPERT_BYTES / 1e9:.1f} GB) per step",
                    "unique_experts_per_layer": uniq / NL},
-        "gpu_launches": 4 * NL * args.steps,  # route (+quantise), gate/up, down, combine
-        "roofline": {"bound": "hbm", "kernel": "moe_tc_kernel (gate/up + down launches)",
+        "gpu_launches": 3 * NL * args.steps,  # route (+quantise), experts (gate/up + down), combine
+        "roofline": {"bound": "hbm", "kernel": "moe_experts_kernel (gate/up + down, one launch)",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind,
                      "algorithmic_bytes_per_step": w_bytes,
@@ -390,8 +390,9 @@ def run_ours(args, world, rank, local):
                      "traffic_source": (traffic or {}).get("source"),
                      "layer": {"achieved": layer_bytes / (ms_per_step / 1e3) / 1e9,
                                "frac": layer_bytes / (ms_per_step / 1e3) / 1e9 / peak,
-                               "stage_ms_per_step": {"route": stage[0], "gate_up": stage[2],
-                                                     "down": stage[3], "combine": stage[4]}}},
+                               "stage_ms_per_step": {"route": stage[0],
+                                                     "experts": stage[2] + stage[3],
+                                                     "combine": stage[4]}}},
         "e2e": {"value": e2e_value, "unit": "tokens/s",
                 "h2d_bytes_per_step": int(Xh.numel() * Xh.element_size()),
                 "d2h_bytes_per_step": int(Oh.numel() * Oh.element_size())},
@@ -523,8 +524,8 @@ def run_ep(args, world, rank, local):
                          f"({NL * (E // world) * EXPERT_BYTES / 1e9:.1f} GB/GPU) per step",
                    "rows_received_per_layer": [float(v) for v in allstats[:, 2]],
                    "unique_local_experts_per_layer": [float(v) for v in allstats[:, 3]]},
-        "gpu_launches": 9 * NL * args.steps,  # per layer: route, pack, header, mask, scatter,
-                                              # gate/up, down, combine, unpack (+ NCCL kernels)
+        "gpu_launches": 8 * NL * args.steps,  # per layer: route, pack, header, mask, scatter,
+                                              # experts, combine, unpack (+ NCCL kernels)
         "roofline": {"bound": "hbm", "kernel": "mfi_moe_experts (scatter, gate/up, down, combine)",
                      "achieved": float(allstats[worst, 0]), "peak": peak, "unit": "GB/s",
                      "frac": float(allstats[worst, 0]) / peak, "peak_kind": peak_kind,

@@ -193,8 +193,9 @@ int mfi_moe_layer(const mfi_moe_weights* w, const void* x_bf16, int T, float* ou
 /* As mfi_moe_layer, recording six caller-created cudaEvent_t (passed as void*)
  * on the stream at the stage boundaries, for per-kernel timing:
  * tensor-core shapes: [0] start, [1] after quantise + route (which also
- * writes each token's row into its experts' regions), [2] = [1], [3] after
- * gate/up (+ SwiGLU requant), [4] after down, [5] after the combine; other
+ * writes each token's row into its experts' regions), [2] = [1], [3] = [4]
+ * after the expert GEMMs (gate/up, SwiGLU requant and down run as one
+ * persistent launch), [5] after the combine; other
  * shapes: [2] after the gate/up GEMV, [3] after SwiGLU requantisation, [4]
  * after the down GEMV. */
 int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float* out,

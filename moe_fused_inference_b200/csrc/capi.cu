@@ -277,8 +277,15 @@ int mfi_moe_combine(const float* yd, int ystride, const float* w, int E, float* 
 
 // ---------------------------------------------------------------------------
 namespace {
+// completion counter, per-expert cursors, the expert launch's work-item
+// counter and per-chunk readiness counters
+inline size_t layer_zero_words(int E, int max_chunks) { return 1 + size_t(E) + 1 + size_t(max_chunks); }
+
 struct LayerScratch {
   unsigned* done;
+  int* queue;
+  unsigned* ready;
+  size_t zero_words;
   int* n_gu;
   int* n_dn;
   int* n_active;
@@ -317,9 +324,12 @@ LayerScratch carve_layer(void* ws, int T, int H, int Mi, int E, int k) {
   s.max_chunks = int((size_t(E) < P ? size_t(E) : P) + (P + 31) / 32);
   s.T_pad = (T + 31) / 32 * 32;
   const size_t rows = size_t(E) * s.T_pad;  // per-expert regions of T_pad rows
-  // completion counter and per-expert cursors: one region, zeroed per call
-  s.done = c.take<unsigned>(1 + size_t(E));
+  // counters of the call, one region zeroed by one memset per call
+  s.zero_words = layer_zero_words(E, s.max_chunks);
+  s.done = c.take<unsigned>(s.zero_words);
   s.cursor = reinterpret_cast<int*>(s.done + 1);
+  s.queue = s.cursor + E;
+  s.ready = s.done + 1 + E + 1;
   s.n_gu = c.take<int>(1);
   s.n_dn = c.take<int>(1);
   s.n_active = c.take<int>(1);
@@ -417,7 +427,7 @@ int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float*
   };
   int rc = mark(0);
   if (rc != MFI_OK) return rc;
-  rc = cuda_status(cudaMemsetAsync(s.done, 0, sizeof(unsigned) * (1 + size_t(E)), st),
+  rc = cuda_status(cudaMemsetAsync(s.done, 0, sizeof(unsigned) * s.zero_words, st),
                    "moe_layer memset");
   if (rc != MFI_OK) return rc;
   if ((reinterpret_cast<uintptr_t>(x_bf16) & 15) != 0 ||
@@ -467,14 +477,11 @@ int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float*
     // kernels overlap their prologue with the previous kernel's tail, except
     // when stage events sit between them
     L.pdl = events == nullptr;
-    L.gate_up = true;
     L.pf_bytes = 0;  // issued by the router
-    rc = cuda_status(mfi::launch_moe_tc(L, st), "moe_layer gate/up (tensor cores) launch");
-    if (rc != MFI_OK || (rc = mark(3)) != MFI_OK) return rc;
-    L.gate_up = false;
-    L.pf_bytes = prefetch_bytes(P, E, false);
-    rc = cuda_status(mfi::launch_moe_tc(L, st), "moe_layer down (tensor cores) launch");
-    if (rc != MFI_OK || (rc = mark(4)) != MFI_OK) return rc;
+    L.queue = s.queue;
+    L.ready = s.ready;
+    rc = cuda_status(mfi::launch_moe_tc(L, st), "moe_layer experts (tensor cores) launch");
+    if (rc != MFI_OK || (rc = mark(3)) != MFI_OK || (rc = mark(4)) != MFI_OK) return rc;
   } else {
     const int max_groups = E < P ? E : P;
     rc = cuda_status(mfi::launch_grouped_gemv(s.g_gu, s.n_gu, 2 * max_groups, s.e_gu, s.xq, s.xsc,
@@ -529,6 +536,8 @@ int mfi_moe_route(const mfi_moe_weights* w, const void* x_bf16, int T, uint8_t* 
 namespace {
 struct ExpertScratch {
   int* cursor;
+  int max_chunks;
+  size_t zero_words;
   int* perm;
   uint8_t* xp;
   uint8_t* xp_atoms;
@@ -544,7 +553,11 @@ ExpertScratch carve_experts(void* ws, int R, int H, int Mi, int E, int k) {
   ExpertScratch s;
   s.T_pad = (R + 31) / 32 * 32;
   const size_t rows = size_t(E) * s.T_pad;
-  s.cursor = c.take<int>(size_t(E));
+  s.max_chunks = int((size_t(E) < size_t(R) * k ? size_t(E) : size_t(R) * k) +
+                     (size_t(R) * k + 31) / 32);
+  // per-expert cursors, the work-item counter, per-chunk readiness: zeroed per call
+  s.zero_words = size_t(E) + 1 + size_t(s.max_chunks);
+  s.cursor = c.take<int>(s.zero_words);
   s.perm = c.take<int>(rows);
   s.xp = c.take<uint8_t>(rows * (H / 2));
   s.xp_atoms = c.take<uint8_t>(rows / 32 * (H / 128) * 512);
@@ -585,7 +598,7 @@ int mfi_moe_experts(const mfi_moe_weights* w, const uint8_t* xq, long long xq_ld
     return fail(MFI_ERR_WORKSPACE, "workspace too small for moe_experts");
   ExpertScratch s = carve_experts(workspace, R, H, Mi, E, k);
   cudaStream_t st = as_stream(stream);
-  int rc = cuda_status(cudaMemsetAsync(s.cursor, 0, sizeof(int) * size_t(E), st),
+  int rc = cuda_status(cudaMemsetAsync(s.cursor, 0, sizeof(int) * s.zero_words, st),
                        "moe_experts memset");
   if (rc != MFI_OK) return rc;
   rc = cuda_status(mfi::launch_scatter_sel(xq, xq_ld, xsc, xsc_ld, sel, sel_ld, R, k, H, E, s.T_pad,
@@ -598,21 +611,17 @@ int mfi_moe_experts(const mfi_moe_weights* w, const uint8_t* xq, long long xq_ld
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   mfi::MoeTcLaunch L{};
   L.E = E; L.H = H; L.Mi = Mi; L.grid = sms;
-  L.max_chunks = int((size_t(E) < size_t(R) * k ? size_t(E) : size_t(R) * k) +
-                     (size_t(R) * k + 31) / 32);
+  L.max_chunks = s.max_chunks;
   L.prepared = static_cast<const uint8_t*>(w->prepared);
   L.counts = s.cursor; L.perm = s.perm;
   L.rows = E * s.T_pad;
   L.xp = s.xp; L.xp_atoms = s.xp_atoms; L.hp = s.hp; L.hp_atoms = s.hp_atoms; L.yd = s.yd;
   L.err = mfi::device_error_flag();
   L.pdl = true;
-  L.gate_up = true;
   L.pf_bytes = prefetch_bytes((long long)R * k, E, true);
-  rc = cuda_status(mfi::launch_moe_tc(L, st), "moe_experts gate/up launch");
-  if (rc != MFI_OK) return rc;
-  L.gate_up = false;
-  L.pf_bytes = prefetch_bytes((long long)R * k, E, false);
-  rc = cuda_status(mfi::launch_moe_tc(L, st), "moe_experts down launch");
+  L.queue = s.cursor + E;
+  L.ready = reinterpret_cast<unsigned*>(s.cursor + E + 1);
+  rc = cuda_status(mfi::launch_moe_tc(L, st), "moe_experts launch");
   if (rc != MFI_OK) return rc;
   return cuda_status(mfi::launch_combine_sel(s.yd, sel, sel_ld, selw, selw_ld, R, k, E, H, out,
                                              out_ld, st),

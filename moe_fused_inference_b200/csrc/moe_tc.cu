@@ -9,23 +9,26 @@
 //   D^T (128 weight rows x 32 tokens) += W_tile (128 x 256 K) . X_chunk^T,
 //   tcgen05.mma.kind::mxf4.block_scale, M = 128, N = 32, K = 64 per instruction.
 //
-// Tokens routed to one expert are packed in chunks of up to 32 rows
-// (route.cu builds the chunk table; gather_chunks_kernel packs the rows and
-// their scale atoms).  A persistent CTA per SM walks work items
-// (chunk, weight tile) with
-//   warp 0     TMA loads of the weight tile (A), the chunk tile (B) and bulk
-//              copies of both scale-factor atoms into an 8-stage ring,
+// The router (route.cu) writes each token's quantised row into per-expert
+// regions; tokens of one expert form chunks of up to 32 rows.  One persistent
+// launch (2 CTAs per SM) runs gate/up and down: work items (chunk, weight
+// tile) come from a global counter in order — all gate/up items first, then
+// the down items, each of which waits (bounded) until the gate/up items of
+// its chunk have published the chunk's requantised h rows.  Per CTA
+//   warp 0     bulk copies of the pre-swizzled weight block (A + its scale
+//              atoms, one contiguous copy per stage), TMA of the chunk's rows
+//              (B) and a bulk copy of their scale atoms into a 3-stage ring,
 //   warp 1     tcgen05.cp of the scales into TMEM + 4 MMAs per stage into one
-//              of two TMEM accumulators (32 fp32 columns each),
-//   warps 2-5  epilogue of the previous item while the next one streams.
+//              of four TMEM accumulators (32 fp32 columns each),
+//   warps 2-5  epilogue of earlier items while the next ones stream.
 //
 // gate/up items take 64 gate rows and the same 64 up rows as one 128-row A
-// tile (two TMA boxes), so the epilogue has g and u for the same outputs: it
-// computes h = g / (1 + exp(-g)) * u in fp32 (src/ext/mxfp4_decode.cu:258),
-// requantises each 32-element block of h with the library's quantiser and
-// writes the packed h rows plus their scale atoms — the B operand of the down
-// items.  down items write per-(token, slot) rows of y for the deterministic
-// combine.  Every wait is bounded (see tc_ptx.cuh).
+// tile, so the epilogue has g and u for the same outputs: it computes
+// h = g / (1 + exp(-g)) * u in fp32 (src/ext/mxfp4_decode.cu:258), requantises
+// each 32-element block of h with the library's quantiser and writes the
+// packed h rows plus their scale atoms — the B operand of the down items.
+// down items write per-(token, slot) rows of y for the deterministic combine.
+// Every wait is bounded (see tc_ptx.cuh).
 #include "mx_common.cuh"
 #include "tc_ptx.cuh"
 #include "tmap.cuh"
@@ -73,32 +76,49 @@ struct MoeTcArgs {
   const int* counts;           // tokens routed to each expert (route.cu cursors)
   int E, T_pad;
   const int* perm;             // row -> (token * k + slot) for the rows of each expert region
-  const uint8_t* wblocks;      // prepared weight blocks [expert][tile][k-stage][kWBlock]
-  const uint8_t* sfb;          // chunk scale atoms [chunk][kc_pad][512]
-  int K;                       // reduction length (hidden or inter), multiple of 256
-  int tiles;                   // weight tiles per chunk
-  int kc_pad;                  // atoms per 128-row block along K (= K / 128)
-  // gate/up
-  int inter;
-  uint8_t* hp;                 // (rows, inter/2)
-  uint8_t* hp_atoms;           // [chunk][inter/128][512]
-  // down
-  int hidden;
-  float* yd;                   // (T*k, hidden)
+  const uint8_t* w_gu;         // prepared gate/up blocks [expert][Mi/64][H/256][kWBlock]
+  const uint8_t* w_dn;         // prepared down blocks [expert][H/128][Mi/256][kWBlock]
+  const uint8_t* sfb_x;        // token-row scale atoms [chunk][H/128][512]
+  uint8_t* hp;                 // requantised h rows (rows, inter/2)
+  uint8_t* hp_atoms;           // their scale atoms [chunk][inter/128][512]
+  int hidden, inter;
+  float* yd;                   // (pairs, hidden) per-(token, slot) down outputs
   int* err;
+  int* queue;                  // work-item counter, zero before the launch
+  unsigned* ready;             // per chunk: finished gate/up items, zero before the launch
   // speculative L2 prefetch, issued before the wait on the upstream kernels:
-  // the first pf_bytes of this launch's weight blocks (storage order = item
-  // order when every expert has one chunk), split evenly over the CTAs
+  // the first pf_bytes of the gate/up blocks (storage order = item order when
+  // every expert has one chunk), split evenly over the CTAs
   unsigned long long pf_bytes;
 };
 
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
+// Order this thread's generic-proxy global accesses with its async-proxy
+// (TMA / bulk copy) accesses.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
-template <bool kGateUp>
+// One persistent launch runs both expert GEMMs of the layer.  Work items,
+// handed out in order by a global counter:
+//   [0, n_gu)          gate/up items (chunk, 64-row gate+up tile), K = hidden
+//   [n_gu, n_items)    down items (chunk, 128-row output tile), K = inter
+// A down item's B operand (the chunk's requantised h rows) is complete once
+// all inter/64 gate/up items of its chunk have published it: their epilogues
+// bump ready[chunk] (release), the down producer polls it (acquire, bounded)
+// and then reads h through the async proxy.  Items are only ever taken by
+// running CTAs and every down item follows all gate/up items in the queue, so
+// the wait always ends (no assumption that the grid is co-resident).
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
-    moe_tc_kernel(const __grid_constant__ CUtensorMap tma_b, MoeTcArgs p) {
+    moe_experts_kernel(const __grid_constant__ CUtensorMap tma_x,
+                       const __grid_constant__ CUtensorMap tma_h, MoeTcArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -108,12 +128,17 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   uint64_t* empty = full + kStages;
   uint64_t* acc_full = empty + kStages;
   uint64_t* acc_empty = acc_full + kAccBufs;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + kAccBufs);
+  uint64_t* item_full = acc_empty + kAccBufs;
+  uint64_t* item_empty = item_full + kAccBufs;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_empty + kAccBufs);
+  __shared__ int s_item[kAccBufs];  // work item of each accumulator slot (-1: no more work)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int k_stages = p.K / 256;
+  const int tiles_gu = p.inter / 64, tiles_dn = p.hidden / 128;
+  const int ks_gu = p.hidden / 256, ks_dn = p.inter / 256;
+  const int kc_gu = p.hidden / 128, kc_dn = p.inter / 128;
 
-  // prologue independent of the upstream kernels: barriers, TMEM, tensor map
+  // prologue independent of the upstream kernels: barriers, TMEM, tensor maps
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
@@ -122,21 +147,30 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     for (int b = 0; b < kAccBufs; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 4);
+      mbar_init(&item_full[b], 1);
+      mbar_init(&item_empty[b], 5);  // the MMA thread + the 4 epilogue warps
     }
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) prefetch_tmap(&tma_b);
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tma_x);
+    prefetch_tmap(&tma_h);
+  }
   if (warp == 0 && p.pf_bytes) {
     // weights do not depend on the routing: stream the first blocks into L2
-    // while the router (or the previous expert launch) is still running
+    // while the router is still running
     const unsigned long long per =
         ((p.pf_bytes + gridDim.x - 1) / gridDim.x + 4095) & ~4095ull;
     const unsigned long long lo = per * blockIdx.x;
     const unsigned long long hi = min(lo + per, p.pf_bytes);
     for (unsigned long long off = lo + lane * 32768ull; off < hi; off += 32 * 32768ull)
-      prefetch_l2(p.wblocks + off, uint32_t(min(32768ull, hi - off)));
+      prefetch_l2(p.w_gu + off, uint32_t(min(32768ull, hi - off)));
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  // the counter was zeroed before the kernel ahead of this one started, so
+  // the first claim may overlap the wait
+  int first_item = 0;
+  if (warp == 0 && lane == 0) first_item = atomicAdd(p.queue, 1);
   // counts, rows and activations come from the kernels before this one
   grid_dep_wait();
   grid_dep_launch();
@@ -170,7 +204,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int n_items = s_nchunks * p.tiles;
+  const int n_gu = s_nchunks * tiles_gu;
+  const int n_items = n_gu + s_nchunks * tiles_dn;
   auto chunk_desc = [&](int chunk) {
     ChunkDesc cd;
     const int v = s_chunk[chunk];
@@ -181,38 +216,94 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     cd.pad = 0;
     return cd;
   };
+  // item -> (gate/up?, chunk, tile)
+  auto decode = [&](int item, bool& gu, int& chunk, int& tile) {
+    gu = item < n_gu;
+    const int i = gu ? item : item - n_gu;
+    const int tiles = gu ? tiles_gu : tiles_dn;
+    chunk = i / tiles;
+    tile = i % tiles;
+  };
 
   if (warp == 0) {
+    first_item = __shfl_sync(0xffffffffu, first_item, 0);
     if (elect_one()) {
       uint32_t it = 0;
       bool ok = true;
-      for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
-        const int tile = item % p.tiles;
-        const ChunkDesc cd = chunk_desc(item / p.tiles);
-        const int e = cd.expert;
-        for (int ks = 0; ks < k_stages; ++ks, ++it) {
+      int item = first_item;
+      for (uint32_t qi = 0; ok; ++qi) {
+        const uint32_t slot = qi % kAccBufs;
+        if (!mbar_wait(&item_empty[slot], ((qi / kAccBufs) & 1) ^ 1, p.err, 1)) break;
+        if (item >= n_items) item = -1;
+        s_item[slot] = item;
+        mbar_arrive(&item_full[slot]);
+        if (item < 0) break;
+        // claim the next item now; its value is needed only after this
+        // item's loads are issued
+        const int next = atomicAdd(p.queue, 1);
+        bool gu;
+        int chunk, tile;
+        decode(item, gu, chunk, tile);
+        const ChunkDesc cd = chunk_desc(chunk);
+        const uint8_t* wb;
+        if (gu) {
+          wb = p.w_gu + (size_t(cd.expert) * tiles_gu + tile) * ks_gu * size_t(kWBlock);
+        } else {
+          wb = p.w_dn + (size_t(cd.expert) * tiles_dn + tile) * ks_dn * size_t(kWBlock);
+          // the chunk's h rows: published by its tiles_gu gate/up items
+          if (ld_acquire_u32(p.ready + chunk) < unsigned(tiles_gu)) {
+            const uint64_t t0 = globaltimer_ns();
+            for (uint32_t i = 1;; ++i) {
+              __nanosleep(64);
+              if (ld_acquire_u32(p.ready + chunk) >= unsigned(tiles_gu)) break;
+              if ((i & 255u) == 0) {
+                if (*reinterpret_cast<volatile int*>(p.err) != 0 ||
+                    globaltimer_ns() - t0 > kWaitLimitNs) {
+                  atomicCAS(p.err, 0, 4);
+                  ok = false;
+                  break;
+                }
+              }
+            }
+            if (!ok) break;
+          }
+          fence_proxy_async_global();
+        }
+        const int ksn = gu ? ks_gu : ks_dn;
+        const int kc = gu ? kc_gu : kc_dn;
+        const uint8_t* sfb = gu ? p.sfb_x : p.hp_atoms;
+        const CUtensorMap* tb = gu ? &tma_x : &tma_h;
+        for (int ks = 0; ks < ksn; ++ks, ++it) {
           const int s = it % kStages;
           if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, p.err, 1)) { ok = false; break; }
           uint8_t* st = ring + s * kStageBytes;
           mbar_expect_tx(&full[s], kStageBytes);
-          const size_t blk = (size_t(e) * p.tiles + tile) * k_stages + ks;
-          bulk_load(st, p.wblocks + blk * kWBlock, kWBlock, &full[s]);
-          tma_load_2d(st + kOffB, &tma_b, ks * 128, cd.row0, &full[s]);
-          bulk_load(st + kOffSFB, p.sfb + (size_t(cd.row0 / kChunk) * p.kc_pad + 2 * ks) * 512, kSF,
+          bulk_load(st, wb + size_t(ks) * kWBlock, kWBlock, &full[s]);
+          tma_load_2d(st + kOffB, tb, ks * 128, cd.row0, &full[s]);
+          bulk_load(st + kOffSFB, sfb + (size_t(cd.row0 / kChunk) * kc + 2 * ks) * 512, kSF,
                     &full[s]);
         }
+        item = next;
       }
     }
   } else if (warp == 1) {
     if (elect_one()) {
-      uint32_t it = 0, acc_it = 0;
+      uint32_t it = 0;
       bool ok = true;
-      for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x, ++acc_it) {
+      for (uint32_t acc_it = 0; ok; ++acc_it) {
         const uint32_t buf = acc_it % kAccBufs;
+        if (!mbar_wait(&item_full[buf], (acc_it / kAccBufs) & 1, p.err, 2)) break;
+        const int item = s_item[buf];
+        mbar_arrive(&item_empty[buf]);
         if (!mbar_wait(&acc_empty[buf], ((acc_it / kAccBufs) & 1) ^ 1, p.err, 2)) { ok = false; break; }
+        if (item < 0) {
+          mbar_arrive(&acc_full[buf]);  // tells the epilogue there is no more work
+          break;
+        }
+        const int ksn = item < n_gu ? ks_gu : ks_dn;
         tc_fence_after();
         const uint32_t d = tmem + buf * 32;
-        for (int ks = 0; ks < k_stages; ++ks, ++it) {
+        for (int ks = 0; ks < ksn; ++ks, ++it) {
           const int s = it % kStages;
           if (!mbar_wait(&full[s], (it / kStages) & 1, p.err, 2)) { ok = false; break; }
           tc_fence_after();
@@ -239,15 +330,25 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   } else {
     const int lane_base = (warp & 3) * 32;
     const int et = threadIdx.x - 64;  // 0..127
-    uint32_t acc_it = 0;
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++acc_it) {
+    for (uint32_t acc_it = 0;; ++acc_it) {
       const uint32_t buf = acc_it % kAccBufs;
-      const int chunk = item / p.tiles, tile = item % p.tiles;
+      if (!mbar_wait(&item_full[buf], (acc_it / kAccBufs) & 1, p.err, 3)) break;
+      const int item = s_item[buf];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[buf]);
+      if (item < 0) {
+        // consume the final acc_full phase so the barrier is left in order
+        mbar_wait(&acc_full[buf], (acc_it / kAccBufs) & 1, p.err, 3);
+        break;
+      }
+      bool gu;
+      int chunk, tile;
+      decode(item, gu, chunk, tile);
       // metadata loads issued before the wait so their latency overlaps it
       const ChunkDesc cd = chunk_desc(chunk);
       const int count = cd.count;
       const int row0 = cd.row0;
-      const int my_pair = kGateUp ? 0 : p.perm[row0 + lane];
+      const int my_pair = gu ? 0 : p.perm[row0 + lane];
       if (!mbar_wait(&acc_full[buf], (acc_it / kAccBufs) & 1, p.err, 3)) break;
       tc_fence_after();
       uint32_t r[32];
@@ -256,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
-      if (kGateUp) {
+      if (gu) {
         // rows 0-63 of the accumulator are gate outputs, rows 64-127 the up
         // outputs of the same 64 columns; columns are the chunk's tokens
         float* sg = s_gu + (acc_it & 1) * (128 * 33);
@@ -312,9 +413,17 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           else if ((sub & 1) == 0) *dst = uint8_t(w0 | (nb_other << 4));
           if (sub == 0) {
             const int kb = tile * 2 + b;
-            p.hp_atoms[(size_t(row0 / kChunk) * (p.inter / 128) + kb / 4) * 512 + n * 16 + (kb & 3)] =
+            p.hp_atoms[(size_t(row0 / kChunk) * kc_dn + kb / 4) * 512 + n * 16 + (kb & 3)] =
                 bs.code;
           }
+        }
+        // publish this tile of the chunk's h rows to the down items (the
+        // barrier also frees s_gu for reuse)
+        named_bar_sync(1, 128);
+        if (et == 0) {
+          fence_proxy_async_global();
+          __threadfence();
+          atomicAdd(p.ready + chunk, 1u);
         }
       } else {
         const int o = tile * 128 + lane_base + lane;
@@ -337,36 +446,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 }
 
 size_t moe_tc_smem() {
-  return 1024 + size_t(kStages) * kStageBytes + 2 * 128 * 33 * 4 + 8 * (2 * kStages + 2 * kAccBufs) +
+  return 1024 + size_t(kStages) * kStageBytes + 2 * 128 * 33 * 4 + 8 * (2 * kStages + 4 * kAccBufs) +
          16;
-}
-
-// ---------------------------------------------------------------------------
-// Pack each chunk's token rows (packed activations) and scale atoms.
-// One warp per chunk row: 16 bytes per lane per pass.
-__global__ void __launch_bounds__(256) gather_chunks_kernel(const uint8_t* __restrict__ xq,
-                                                            const uint8_t* __restrict__ xsc,
-                                                            const int* __restrict__ perm,
-                                                            const int* __restrict__ n_chunks,
-                                                            int k, int H, uint8_t* __restrict__ xp,
-                                                            uint8_t* __restrict__ xp_atoms) {
-  const int rows = *n_chunks * kChunk;
-  const int lane = threadIdx.x & 31;
-  const int nb = H / 32, kc = H / 128;
-  for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows;
-       r += (gridDim.x * blockDim.x) >> 5) {
-    const int pair = perm[r];
-    const int tok = pair >= 0 ? pair / k : -1;
-    uint4* dst = reinterpret_cast<uint4*>(xp + size_t(r) * (H / 2));
-    const uint4* src = reinterpret_cast<const uint4*>(xq + size_t(tok < 0 ? 0 : tok) * (H / 2));
-    for (int i = lane; i < H / 32; i += 32) dst[i] = tok >= 0 ? src[i] : make_uint4(0, 0, 0, 0);
-    const int chunk = r / kChunk, i = r % kChunk;
-    for (int a = lane; a < kc; a += 32) {
-      uint32_t v = 0x7f7f7f7fu;
-      if (tok >= 0) v = *reinterpret_cast<const uint32_t*>(xsc + size_t(tok) * nb + 4 * a);
-      *reinterpret_cast<uint32_t*>(xp_atoms + (size_t(chunk) * kc + a) * 512 + i * 16) = v;
-    }
-  }
 }
 
 // Prepared weight blocks.  Block (e, tile, ks) holds rows r = 0..127 of the
@@ -454,37 +535,47 @@ cudaError_t launch_moe_prepare(const uint8_t* gate_wp, const uint8_t* gate_sc,
   return cudaGetLastError();
 }
 
-cudaError_t launch_gather_chunks(const uint8_t* xq, const uint8_t* xsc, const int* perm,
-                                 const int* n_chunks, int max_chunks, int k, int H, uint8_t* xp,
-                                 uint8_t* xp_atoms, cudaStream_t stream) {
-  const int rows = max_chunks * kChunk;
-  int blocks = (rows * 32 + 255) / 256;
-  if (blocks > 148 * 8) blocks = 148 * 8;
-  if (blocks < 1) blocks = 1;
-  gather_chunks_kernel<<<blocks, 256, 0, stream>>>(xq, xsc, perm, n_chunks, k, H, xp, xp_atoms);
-  return cudaGetLastError();
-}
-
-static cudaError_t set_smem_once(const void* fn, bool* done) {
-  if (*done) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       int(moe_tc_smem()));
-  if (e == cudaSuccess) *done = true;
-  return e;
-}
-
 static unsigned long long cap_prefetch(size_t want, size_t region) {
   return (unsigned long long)(want < region ? want : region) & ~15ull;
 }
 
-// Launch with programmatic stream serialisation when `pdl`: the kernel may
-// start while the previous kernel in the stream drains (it waits with
-// grid_dep_wait before reading that kernel's outputs).
-template <class Kern>
-static cudaError_t launch_ex(Kern kern, int grid, bool pdl, cudaStream_t stream,
-                             const CUtensorMap& b, const MoeTcArgs& p) {
+cudaError_t launch_moe_tc(const MoeTcLaunch& L, cudaStream_t stream) {
+  if (L.queue == nullptr || L.ready == nullptr) return cudaErrorInvalidValue;
+  static bool smem_set = false;
+  if (!smem_set) {
+    cudaError_t e = cudaFuncSetAttribute(moe_experts_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(moe_tc_smem()));
+    if (e != cudaSuccess) return e;
+    smem_set = true;
+  }
+  const int E = L.E, H = L.H, Mi = L.Mi;
+  CUtensorMap tx, th;
+  if (!get_tmap(&tx, L.xp, H / 2, uint64_t(L.rows), kChunk) ||
+      !get_tmap(&th, L.hp, Mi / 2, uint64_t(L.rows), kChunk))
+    return cudaErrorInvalidValue;
+  MoeTcArgs p{};
+  p.counts = L.counts;
+  p.E = E;
+  p.T_pad = L.rows / E;
+  p.perm = L.perm;
+  p.w_gu = L.prepared;
+  p.w_dn = L.prepared + size_t(E) * (Mi / 64) * (H / 256) * kWBlock;
+  p.sfb_x = L.xp_atoms;
+  p.hp = L.hp;
+  p.hp_atoms = L.hp_atoms;
+  p.hidden = H;
+  p.inter = Mi;
+  p.yd = L.yd;
+  p.err = L.err;
+  p.queue = L.queue;
+  p.ready = L.ready;
+  p.pf_bytes = cap_prefetch(L.pf_bytes, size_t(E) * (Mi / 64) * (H / 256) * kWBlock);
+  // programmatic stream serialisation when `pdl`: the kernel may start while
+  // the previous kernel in the stream drains (it waits with grid_dep_wait
+  // before reading that kernel's outputs)
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = dim3(L.grid * kCtasPerSm);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = moe_tc_smem();
   cfg.stream = stream;
@@ -492,54 +583,8 @@ static cudaError_t launch_ex(Kern kern, int grid, bool pdl, cudaStream_t stream,
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kern, b, p);
-}
-
-cudaError_t launch_moe_tc(const MoeTcLaunch& L, cudaStream_t stream) {
-  static bool smem_gu = false, smem_dn = false;
-  const int E = L.E, H = L.H, Mi = L.Mi;
-  CUtensorMap b;
-  MoeTcArgs p{};
-  p.counts = L.counts;
-  p.E = L.E;
-  p.T_pad = L.rows / L.E;
-  p.perm = L.perm;
-  p.inter = Mi;
-  p.hidden = H;
-  p.hp = L.hp;
-  p.hp_atoms = L.hp_atoms;
-  p.yd = L.yd;
-  p.err = L.err;
-  const int grid = L.grid * kCtasPerSm;
-  if (L.gate_up) {
-    if (!get_tmap(&b, L.xp, H / 2, uint64_t(L.rows), kChunk))
-      return cudaErrorInvalidValue;
-    p.wblocks = L.prepared;
-    p.sfb = L.xp_atoms;
-    p.K = H;
-    p.tiles = Mi / 64;
-    p.kc_pad = H / 128;
-    p.pf_bytes = cap_prefetch(L.pf_bytes, size_t(E) * (Mi / 64) * (H / 256) * kWBlock);
-    cudaError_t e = set_smem_once(reinterpret_cast<const void*>(moe_tc_kernel<true>), &smem_gu);
-    if (e != cudaSuccess) return e;
-    e = launch_ex(moe_tc_kernel<true>, grid, L.pdl, stream, b, p);
-    if (e != cudaSuccess) return e;
-  } else {
-    if (!get_tmap(&b, L.hp, Mi / 2, uint64_t(L.rows), kChunk))
-      return cudaErrorInvalidValue;
-    p.wblocks = L.prepared + size_t(E) * (Mi / 64) * (H / 256) * kWBlock;
-    p.sfb = L.hp_atoms;
-    p.K = Mi;
-    p.tiles = H / 128;
-    p.kc_pad = Mi / 128;
-    p.pf_bytes = cap_prefetch(L.pf_bytes, size_t(E) * (H / 128) * (Mi / 256) * kWBlock);
-    cudaError_t e = set_smem_once(reinterpret_cast<const void*>(moe_tc_kernel<false>), &smem_dn);
-    if (e != cudaSuccess) return e;
-    e = launch_ex(moe_tc_kernel<false>, grid, L.pdl, stream, b, p);
-    if (e != cudaSuccess) return e;
-  }
-  return cudaGetLastError();
+  cfg.numAttrs = L.pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, moe_experts_kernel, tx, th, p);
 }
 
 }  // namespace mfi

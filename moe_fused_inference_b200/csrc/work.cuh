@@ -106,9 +106,9 @@ cudaError_t launch_tc_gemm(const uint8_t* a, const uint8_t* sfa_atoms, const uin
                            const uint8_t* sfb_atoms, float* y, long long ldy, int M, int N, int Kp,
                            int* err, cudaStream_t stream);
 
-// Decode expert GEMMs on tensor cores (moe_tc.cu).
+// Decode expert GEMMs on tensor cores (moe_tc.cu): gate/up and down in one
+// persistent launch.
 struct MoeTcLaunch {
-  bool gate_up;
   int E, H, Mi, max_chunks, grid;
   const uint8_t* prepared;           // weight blocks from launch_moe_prepare
   const int* counts;                            // tokens per expert (route cursors)
@@ -120,15 +120,14 @@ struct MoeTcLaunch {
   int* err;
   bool pdl;                                     // programmatic dependent launch
   size_t pf_bytes;                              // speculative L2 prefetch of weights
+  int* queue;                                   // work-item counter, zeroed before the launch
+  unsigned* ready;                              // [max_chunks], zeroed before the launch
 };
 size_t moe_prepared_bytes(int E, int H, int Mi);
 cudaError_t launch_moe_prepare(const uint8_t* gate_wp, const uint8_t* gate_sc,
                                const uint8_t* up_wp, const uint8_t* up_sc,
                                const uint8_t* down_wp, const uint8_t* down_sc, int E, int H, int Mi,
                                uint8_t* prepared, cudaStream_t stream);
-cudaError_t launch_gather_chunks(const uint8_t* xq, const uint8_t* xsc, const int* perm,
-                                 const int* n_chunks, int max_chunks, int k, int H, uint8_t* xp,
-                                 uint8_t* xp_atoms, cudaStream_t stream);
 cudaError_t launch_moe_tc(const MoeTcLaunch& L, cudaStream_t stream);
 
 // Expert parallelism and pre-routed rows (ep.cu).
