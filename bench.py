@@ -56,6 +56,9 @@ def parse():
     ap.add_argument("--tokens", type=int, default=64, help="decode tokens per GPU (T)")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="distinct MoE layers per step (48 = the model; fewer for profiling)")
+    ap.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
+                    help="multi-GPU token exchange: peer-memory stores fused into the kernels "
+                         "(p2p) or two NCCL all_to_all_single calls (nccl)")
     ap.add_argument("--no-graph", action="store_true",
                     help="time plain launches instead of a captured CUDA graph")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
@@ -404,12 +407,14 @@ def run_ours(args, world, rank, local):
 
 
 def run_ep(args, world, rank, local):
-    """Expert-parallel step over the torchrun ranks (NCCL all-to-all)."""
+    """Expert-parallel step over the torchrun ranks (peer-memory exchange fused
+    into the kernels, or NCCL all-to-all with --ep-transport nccl)."""
     from moe_fused_inference_b200.ep import EPMoELayer, random_shard
 
     dev = torch.device("cuda", local)
     T, NL = args.tokens, args.layers
-    layers = [EPMoELayer(random_shard(E, world, rank, H, MI, 0.02, seed=l, device=dev), TOPK, T)
+    layers = [EPMoELayer(random_shard(E, world, rank, H, MI, 0.02, seed=l, device=dev), TOPK, T,
+                         transport=args.ep_transport)
               for l in range(NL)]
     g = torch.Generator(device=dev).manual_seed(7 + rank)
     X = torch.randn((NL, T, H), generator=g, device=dev).bfloat16()
@@ -455,26 +460,38 @@ def run_ep(args, world, rank, local):
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(NL)]
     import torch.distributed as dist
+    from moe_fused_inference_b200.ep import ep_row_bytes
+    recvs = []
     for l in range(NL):
         L = layers[l]
-        L.dispatch_prepare(X[l])
-        dist.all_to_all_single(L.recv.view(-1), L.send.view(-1))
-        evs[l][0].record(stream)
-        L.compute()
-        evs[l][1].record(stream)
-        dist.all_to_all_single(L.ret_back.view(-1), L.ret.view(-1))
-        L.finish(T, out[l])
+        if L.transport == "p2p":
+            L.p2p_dispatch(X[l])
+            evs[l][0].record(stream)
+            L.p2p_experts()  # includes the wait for the peers' dispatch
+            evs[l][1].record(stream)
+            L.p2p_finish(T, out[l])
+            rv = torch.empty((world, T + 1, ep_row_bytes(H, TOPK)), dtype=torch.uint8, device=dev)
+            L.xch.copy_recv_to(rv)
+            recvs.append(rv)
+        else:
+            L.dispatch_prepare(X[l])
+            dist.all_to_all_single(L.recv.view(-1), L.send.view(-1))
+            evs[l][0].record(stream)
+            L.compute()
+            evs[l][1].record(stream)
+            dist.all_to_all_single(L.ret_back.view(-1), L.ret.view(-1))
+            L.finish(T, out[l])
+            recvs.append(L.recv)
     torch.cuda.synchronize(dev)
     experts_ms = sum(a.elapsed_time(b) for a, b in evs)
     # unique local experts touched per layer on this rank
-    el = E // world
     uniq = 0
     rows_recv = 0
     for l in range(NL):
-        L = layers[l]
-        cnt = L.recv[:, 0, :4].contiguous().view(torch.int32)[:, 0]
+        rv = recvs[l]
+        cnt = rv[:, 0, :4].contiguous().view(torch.int32)[:, 0]
         rows_recv += int(cnt.sum())
-        sel = torch.cat([L.recv[s, 1:1 + int(cnt[s])] for s in range(world)])
+        sel = torch.cat([rv[s, 1:1 + int(cnt[s])] for s in range(world)])
         if sel.shape[0]:
             from moe_fused_inference_b200.ep import row_offsets
             _, _, so, _ = row_offsets(H, TOPK)
@@ -492,6 +509,7 @@ def run_ep(args, world, rank, local):
     # ---- e2e: host activations in, host outputs back, plain launches ----
     if graph is not None:
         del graph
+    del recvs
     Xh = X.cpu().pin_memory()
     Oh = torch.empty((NL, T, H), dtype=torch.float32).pin_memory()
     Xd = torch.empty_like(X)
@@ -506,6 +524,9 @@ def run_ep(args, world, rank, local):
     e2e_value = tokens / (e2e_ms / 1e3)
     torch.cuda.synchronize(dev)
     barrier(world)
+    for L in layers:
+        L.close()  # unmap the peers' memory before the process group goes away
+    barrier(world)
     if rank != 0:
         return
     worst = int(torch.argmin(allstats[:, 0]))
@@ -516,16 +537,21 @@ def run_ep(args, world, rank, local):
         "dtype": "mxfp4 (e2m1 x e2m1, fp32 accumulate)",
         "data": "synthetic (random-init weights N(0,0.02), activations N(0,1), seeded)",
         "config": {"workload": f"decode MoE layer, T={T} tokens/GPU, H=2048, E=128, top-8, Mi=768",
-                   "step": f"T tokens per rank through {NL} expert-parallel MoE layers "
-                           "(route, pack, NCCL all-to-all dispatch, tcgen05 experts, "
-                           "all-to-all return, unpack), " + graph_note,
+                   "step": f"T tokens per rank through {NL} expert-parallel MoE layers, " + (
+                       "router storing rows into the owners' receive buffers over NVLink, "
+                       "tcgen05 experts storing weighted sums back, rank-ordered unpack"
+                       if args.ep_transport == "p2p" else
+                       "route, pack, NCCL all-to-all dispatch, tcgen05 experts, all-to-all "
+                       "return, unpack") + ", " + graph_note,
+                   "ep_transport": args.ep_transport,
                    "global_batch": T * world, "parallelism": f"ep{world} ({E // world} experts/GPU)",
                    "l2": f"inputs larger than L2: {NL} distinct layer shards "
                          f"({NL * (E // world) * EXPERT_BYTES / 1e9:.1f} GB/GPU) per step",
                    "rows_received_per_layer": [float(v) for v in allstats[:, 2]],
                    "unique_local_experts_per_layer": [float(v) for v in allstats[:, 3]]},
-        "gpu_launches": 8 * NL * args.steps,  # per layer: route, pack, header, mask, scatter,
-                                              # experts, combine, unpack (+ NCCL kernels)
+        # per layer: p2p route+dispatch, scatter, experts, combine+return, unpack;
+        # nccl: route, pack, header, mask, scatter, experts, combine, unpack (+ NCCL's own)
+        "gpu_launches": (5 if args.ep_transport == "p2p" else 8) * NL * args.steps,
         "roofline": {"bound": "hbm", "kernel": "mfi_moe_experts (scatter, gate/up, down, combine)",
                      "achieved": float(allstats[worst, 0]), "peak": peak, "unit": "GB/s",
                      "frac": float(allstats[worst, 0]) / peak, "peak_kind": peak_kind,

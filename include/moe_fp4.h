@@ -221,8 +221,8 @@ int mfi_moe_route(const mfi_moe_weights* w, const void* x_bf16, int T, uint8_t* 
  *            selw[r][j] * down_e(swiglu(gate_e(x_r), up_e(x_r))),  e = sel[r][j]
  * with each product and partial sum rounded to fp32 (the combine of
  * mfi_moe_combine).  Row r of xq / xsc / sel / selw / out starts at r * *_ld
- * (bytes for xq and xsc, elements otherwise); xq rows 16-byte aligned, xsc
- * rows 4-byte aligned.  sel entries are expert ids of `w` (0..n_experts-1) or
+ * (bytes for xq and xsc, elements otherwise); xq and out rows 16-byte
+ * aligned, xsc rows 4-byte aligned.  sel entries are expert ids of `w` (0..n_experts-1) or
  * -1; an id must not repeat within a row (the device error flag then reads 5;
  * an id >= n_experts reads 4 and is skipped).  Needs hidden and inter to be
  * multiples of 256 and `w->prepared`; router fields are not read.
@@ -272,6 +272,72 @@ int mfi_ep_mask_recv(uint8_t* recv, int n_ranks, int capacity, int hidden, int t
  * (ret: fp32 [n_ranks][capacity + 1][hidden]). */
 int mfi_ep_unpack(const float* ret, const int32_t* pack_pos, int T, int n_ranks, int capacity,
                   int hidden, float* out, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Expert parallelism over peer memory (no reference counterpart).  Instead of
+ * two all-to-alls, the router stores each token's row straight into the
+ * receive buffer of every rank that owns one of its experts (NVLink stores
+ * through CUDA IPC mappings) and raises a flag there; the expert side answers
+ * with the weighted sums of its slots stored straight into the source's
+ * return buffer.  Flags carry a call id (the rank's completed-call epoch + 1,
+ * kept in its flag area), so no flag is ever reset and the whole exchange can
+ * be captured in a CUDA graph.  Every wait is bounded (2 s; the device error
+ * flag then reads 7 for a missing dispatch, 8 for a missing return).
+ *
+ * Per rank, in memory the peers map (e.g. one mfi_ipc_alloc block):
+ *   recv   mfi_ep_recv_bytes()  block s = rows from rank s, same row layout
+ *                               as the all-to-all exchange above
+ *   ret    mfi_ep_ret_bytes()   block d = fp32 rows returned by rank d
+ *   flags  mfi_ep_flag_bytes()  zero before the first call
+ * Each rank calls, in order on one stream, for every layer call:
+ *   mfi_ep_route_dispatch, mfi_ep_experts_return, mfi_ep_unpack_wait.
+ * All ranks must make the same sequence of calls with the same capacity.
+ * ------------------------------------------------------------------------ */
+
+/* Device memory for peer mapping: cudaMalloc'd and zeroed (synchronous).
+ * These, with mfi_ep_table_set, are the only calls that allocate or copy
+ * synchronously; they are meant for setup. */
+int mfi_ipc_alloc(size_t bytes, void** ptr);
+int mfi_ipc_free(void* ptr);
+/* 64-byte CUDA IPC handle of an mfi_ipc_alloc block / open a peer's handle. */
+int mfi_ipc_handle(const void* ptr, void* handle);
+int mfi_ipc_open(const void* handle, void** ptr);
+int mfi_ipc_close(void* ptr);
+/* Stream-ordered copy between device (or host) buffers (cudaMemcpyDefault),
+ * for inspecting exchange buffers that have no torch tensor. */
+int mfi_copy_async(void* dst, const void* src, size_t bytes, void* stream);
+
+size_t mfi_ep_flag_bytes(void);
+size_t mfi_ep_recv_bytes(int n_ranks, int capacity, int hidden, int top_k);
+size_t mfi_ep_ret_bytes(int n_ranks, int capacity, int hidden);
+/* Peer table: device buffer of mfi_ep_table_bytes() holding, for d < n_ranks,
+ * rank d's recv, ret and flags addresses as seen from this rank (this rank's
+ * own at d = rank).  Written synchronously. */
+size_t mfi_ep_table_bytes(void);
+int mfi_ep_table_set(void* table, int n_ranks, void* const* recv, void* const* ret,
+                     void* const* flags);
+
+/* Route T <= capacity tokens (x bf16 (T, hidden)) with the router of `w`
+ * (n_experts divisible by n_ranks; rank d owns experts [d*E/n, (d+1)*E/n))
+ * and send them: topi/topw as mfi_moe_route, pack_pos int32 (T, n_ranks) =
+ * each token's row in its block at rank d, or -1. */
+int mfi_ep_route_dispatch(const mfi_moe_weights* w, const void* x_bf16, int T, int rank,
+                          int n_ranks, int capacity, const void* table, void* flags,
+                          int32_t* topi, float* topw, int32_t* pack_pos, void* stream);
+
+/* Wait for every rank's dispatch, run the local experts (`w`: this rank's
+ * E/n experts, prepared) on the received rows and send each row's weighted
+ * slot sum back to its source.  n_ranks * (capacity + 1) * top_k <= 16384. */
+size_t mfi_ep_experts_workspace_bytes(int n_ranks, int capacity, int hidden, int inter,
+                                      int local_experts, int top_k);
+int mfi_ep_experts_return(const mfi_moe_weights* w, int rank, int n_ranks, int capacity,
+                          const void* table, void* flags, uint8_t* recv, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/* Wait for every rank's return and sum, in rank order, out[t] (fp32
+ * (T, hidden)) from this rank's ret buffer; closes the call. */
+int mfi_ep_unpack_wait(int n_ranks, int capacity, int hidden, int T, void* flags, const float* ret,
+                       const int32_t* pack_pos, float* out, void* stream);
 
 #ifdef __cplusplus
 }

@@ -51,6 +51,21 @@ SIGNATURES = {
     "mfi_ep_pack": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _I, _VP, _VP, _VP, _VP]),
     "mfi_ep_mask_recv": (_I, [_VP, _I, _I, _I, _I, _VP]),
     "mfi_ep_unpack": (_I, [_VP, _VP, _I, _I, _I, _I, _VP, _VP]),
+    "mfi_ipc_alloc": (_I, [_SZ, ctypes.POINTER(_VP)]),
+    "mfi_ipc_free": (_I, [_VP]),
+    "mfi_ipc_handle": (_I, [_VP, _VP]),
+    "mfi_ipc_open": (_I, [_VP, ctypes.POINTER(_VP)]),
+    "mfi_ipc_close": (_I, [_VP]),
+    "mfi_copy_async": (_I, [_VP, _VP, _SZ, _VP]),
+    "mfi_ep_flag_bytes": (_SZ, []),
+    "mfi_ep_recv_bytes": (_SZ, [_I, _I, _I, _I]),
+    "mfi_ep_ret_bytes": (_SZ, [_I, _I, _I]),
+    "mfi_ep_table_bytes": (_SZ, []),
+    "mfi_ep_table_set": (_I, [_VP, _I, _VP, _VP, _VP]),
+    "mfi_ep_route_dispatch": (_I, [_VP, _VP, _I, _I, _I, _I, _VP, _VP, _VP, _VP, _VP, _VP]),
+    "mfi_ep_experts_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I, _I]),
+    "mfi_ep_experts_return": (_I, [_VP, _I, _I, _I, _VP, _VP, _VP, _VP, _SZ, _VP]),
+    "mfi_ep_unpack_wait": (_I, [_I, _I, _I, _I, _VP, _VP, _VP, _VP, _VP]),
 }
 
 MFI_F32, MFI_F16, MFI_BF16 = 0, 1, 2

@@ -592,8 +592,10 @@ int mfi_moe_experts(const mfi_moe_weights* w, const uint8_t* xq, long long xq_ld
   if (xq_ld < H / 2 || xsc_ld < H / 32 || sel_ld < k || selw_ld < k || out_ld < H)
     return fail(MFI_ERR_ARG, "row strides must cover one row");
   if ((reinterpret_cast<uintptr_t>(xq) & 15) != 0 || xq_ld % 16 != 0 ||
-      (reinterpret_cast<uintptr_t>(xsc) & 3) != 0 || xsc_ld % 4 != 0)
-    return fail(MFI_ERR_ARG, "xq rows must be 16-byte aligned, xsc rows 4-byte aligned");
+      (reinterpret_cast<uintptr_t>(xsc) & 3) != 0 || xsc_ld % 4 != 0 ||
+      (reinterpret_cast<uintptr_t>(out) & 15) != 0 || out_ld % 4 != 0)
+    return fail(MFI_ERR_ARG,
+                "xq and out rows must be 16-byte aligned, xsc rows 4-byte aligned");
   if (workspace_bytes < mfi_moe_experts_workspace_bytes(R, H, Mi, E, k))
     return fail(MFI_ERR_WORKSPACE, "workspace too small for moe_experts");
   ExpertScratch s = carve_experts(workspace, R, H, Mi, E, k);
@@ -684,9 +686,212 @@ int mfi_ep_unpack(const float* ret, const int32_t* pack_pos, int T, int n_ranks,
   if (rc != MFI_OK) return rc;
   if (T == 0) return MFI_OK;
   if (bad_ptr(ret) || bad_ptr(pack_pos) || bad_ptr(out)) return fail(MFI_ERR_ARG, "null pointer");
+  if ((reinterpret_cast<uintptr_t>(ret) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
+    return fail(MFI_ERR_ARG, "ret and out must be 16-byte aligned");
   return cuda_status(mfi::launch_ep_unpack(ret, pack_pos, T, n_ranks, capacity, hidden, out,
                                            as_stream(stream)),
                      "ep_unpack launch");
+}
+
+// ---------------------------------------------------------------------------
+// Expert parallelism over peer memory (CUDA IPC + NVLink stores).
+
+int mfi_ipc_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return fail(MFI_ERR_ARG, "ipc_alloc: null out pointer or zero size");
+  *ptr = nullptr;
+  void* p = nullptr;
+  int rc = cuda_status(cudaMalloc(&p, bytes), "ipc_alloc cudaMalloc");
+  if (rc != MFI_OK) return rc;
+  rc = cuda_status(cudaMemset(p, 0, bytes), "ipc_alloc cudaMemset");
+  if (rc != MFI_OK) {
+    cudaFree(p);
+    return rc;
+  }
+  *ptr = p;
+  return MFI_OK;
+}
+
+int mfi_ipc_free(void* ptr) {
+  if (!ptr) return MFI_OK;
+  return cuda_status(cudaFree(ptr), "ipc_free");
+}
+
+int mfi_ipc_handle(const void* ptr, void* handle) {
+  if (!ptr || !handle) return fail(MFI_ERR_ARG, "null pointer");
+  cudaIpcMemHandle_t h;
+  int rc = cuda_status(cudaIpcGetMemHandle(&h, const_cast<void*>(ptr)), "cudaIpcGetMemHandle");
+  if (rc == MFI_OK) memcpy(handle, &h, sizeof(h));
+  return rc;
+}
+
+int mfi_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return fail(MFI_ERR_ARG, "null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return cuda_status(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess),
+                     "cudaIpcOpenMemHandle");
+}
+
+int mfi_ipc_close(void* ptr) {
+  if (!ptr) return MFI_OK;
+  return cuda_status(cudaIpcCloseMemHandle(ptr), "cudaIpcCloseMemHandle");
+}
+
+int mfi_copy_async(void* dst, const void* src, size_t bytes, void* stream) {
+  if (bytes == 0) return MFI_OK;
+  if (!dst || !src) return fail(MFI_ERR_ARG, "null pointer");
+  return cuda_status(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, as_stream(stream)),
+                     "copy_async");
+}
+
+size_t mfi_ep_flag_bytes(void) { return sizeof(unsigned) * mfi::kFlagWords; }
+
+size_t mfi_ep_recv_bytes(int n_ranks, int capacity, int hidden, int top_k) {
+  if (n_ranks <= 0 || capacity < 0 || hidden <= 0 || hidden % 128 || top_k <= 0 || top_k > 32)
+    return 0;
+  return size_t(n_ranks) * (capacity + 1) * mfi::ep_row_bytes(hidden, top_k);
+}
+
+size_t mfi_ep_ret_bytes(int n_ranks, int capacity, int hidden) {
+  if (n_ranks <= 0 || capacity < 0 || hidden <= 0) return 0;
+  return size_t(n_ranks) * (capacity + 1) * hidden * sizeof(float);
+}
+
+size_t mfi_ep_table_bytes(void) { return sizeof(mfi::EpTable); }
+
+int mfi_ep_table_set(void* table, int n_ranks, void* const* recv, void* const* ret,
+                     void* const* flags) {
+  if (!table || !recv || !ret || !flags) return fail(MFI_ERR_ARG, "null pointer");
+  if (n_ranks <= 0 || n_ranks > mfi::kEpMaxRanks) return fail(MFI_ERR_ARG, "n_ranks must be in [1, 64]");
+  mfi::EpTable t{};
+  for (int d = 0; d < n_ranks; ++d) {
+    if (!recv[d] || !ret[d] || !flags[d]) return fail(MFI_ERR_ARG, "null peer pointer");
+    if ((reinterpret_cast<uintptr_t>(recv[d]) & 15) || (reinterpret_cast<uintptr_t>(ret[d]) & 15) ||
+        (reinterpret_cast<uintptr_t>(flags[d]) & 15))
+      return fail(MFI_ERR_ARG, "peer buffers must be 16-byte aligned");
+    t.recv[d] = static_cast<uint8_t*>(recv[d]);
+    t.ret[d] = static_cast<float*>(ret[d]);
+    t.flags[d] = static_cast<unsigned*>(flags[d]);
+  }
+  return cuda_status(cudaMemcpy(table, &t, sizeof(t), cudaMemcpyHostToDevice), "ep_table_set");
+}
+
+namespace {
+int ep_p2p_check(int rank, int n, int C, int H, int k) {
+  if (n <= 0 || n > mfi::kEpMaxRanks) return fail(MFI_ERR_ARG, "n_ranks must be in [1, 64]");
+  if (rank < 0 || rank >= n) return fail(MFI_ERR_ARG, "rank out of range");
+  if (C < 0) return fail(MFI_ERR_ARG, "capacity must be >= 0");
+  if (H <= 0 || H % 256 != 0 || H > 4096)
+    return fail(MFI_ERR_ARG, "hidden must be a positive multiple of 256, <= 4096");
+  if (k <= 0 || k > 32) return fail(MFI_ERR_ARG, "top_k must be in [1, 32]");
+  return MFI_OK;
+}
+}  // namespace
+
+int mfi_ep_route_dispatch(const mfi_moe_weights* w, const void* x_bf16, int T, int rank,
+                          int n_ranks, int capacity, const void* table, void* flags,
+                          int32_t* topi, float* topw, int32_t* pack_pos, void* stream) {
+  if (!w) return fail(MFI_ERR_ARG, "null weights");
+  const int E = w->n_experts, H = w->hidden, k = w->top_k;
+  int rc = ep_p2p_check(rank, n_ranks, capacity, H, k);
+  if (rc != MFI_OK) return rc;
+  if (E <= 0 || E > mfi::kRouteMaxE || E % n_ranks != 0)
+    return fail(MFI_ERR_ARG, "n_experts must be in [1, 256] and divisible by n_ranks");
+  if (k > E) return fail(MFI_ERR_ARG, "top_k must be <= n_experts");
+  if (T < 0 || T > capacity) return fail(MFI_ERR_ARG, "T must be in [0, capacity]");
+  if (bad_ptr(table) || bad_ptr(flags) || bad_ptr(w->router_wp) || bad_ptr(w->router_sc) ||
+      (T > 0 && (bad_ptr(x_bf16) || bad_ptr(topi) || bad_ptr(topw) || bad_ptr(pack_pos))))
+    return fail(MFI_ERR_ARG, "null pointer");
+  if ((reinterpret_cast<uintptr_t>(x_bf16) & 15) || (reinterpret_cast<uintptr_t>(w->router_wp) & 15))
+    return fail(MFI_ERR_ARG, "x and router_wp must be 16-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  unsigned* fl = static_cast<unsigned*>(flags);
+  rc = cuda_status(cudaMemsetAsync(fl + mfi::kFlagZeroFirst, 0,
+                                   sizeof(unsigned) * (mfi::kFlagWords - mfi::kFlagZeroFirst), st),
+                   "ep_route_dispatch memset");
+  if (rc != MFI_OK) return rc;
+  mfi::RouteArgs ra{};
+  ra.x = x_bf16; ra.wr = w->router_wp; ra.sr = w->router_sc;
+  ra.T = T; ra.H = H; ra.E = E; ra.k = k;
+  ra.topi = topi; ra.topw = topw;
+  ra.err = mfi::device_error_flag();
+  ra.ep.table = static_cast<const mfi::EpTable*>(table);
+  ra.ep.flags = fl;
+  ra.ep.pack_pos = pack_pos;
+  ra.ep.rank = rank; ra.ep.n = n_ranks; ra.ep.C = capacity; ra.ep.el = E / n_ranks; ra.ep.T = T;
+  return cuda_status(mfi::launch_route(ra, st), "ep_route_dispatch launch");
+}
+
+size_t mfi_ep_experts_workspace_bytes(int n_ranks, int capacity, int hidden, int inter,
+                                      int local_experts, int top_k) {
+  if (n_ranks <= 0 || capacity < 0) return 0;
+  return mfi_moe_experts_workspace_bytes(n_ranks * (capacity + 1), hidden, inter, local_experts,
+                                         top_k);
+}
+
+int mfi_ep_experts_return(const mfi_moe_weights* w, int rank, int n_ranks, int capacity,
+                          const void* table, void* flags, uint8_t* recv, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  if (!w) return fail(MFI_ERR_ARG, "null weights");
+  const int E = w->n_experts, H = w->hidden, Mi = w->inter, k = w->top_k;
+  int rc = ep_p2p_check(rank, n_ranks, capacity, H, k);
+  if (rc != MFI_OK) return rc;
+  if (E <= 0 || E > mfi::kRouteMaxE) return fail(MFI_ERR_ARG, "n_experts must be in [1, 256]");
+  if (!layer_uses_tc(H, Mi)) return fail(MFI_ERR_ARG, "hidden and inter must be multiples of 256");
+  const int R = n_ranks * (capacity + 1);
+  if ((long long)R * k > 16384) return fail(MFI_ERR_ARG, "n_ranks * (capacity + 1) * top_k must be <= 16384");
+  if (bad_ptr(table) || bad_ptr(flags) || bad_ptr(recv) || bad_ptr(workspace) || bad_ptr(w->prepared))
+    return fail(MFI_ERR_ARG, "null pointer (weights.prepared comes from mfi_moe_prepare)");
+  if (reinterpret_cast<uintptr_t>(recv) & 15) return fail(MFI_ERR_ARG, "recv must be 16-byte aligned");
+  if (workspace_bytes < mfi_moe_experts_workspace_bytes(R, H, Mi, E, k))
+    return fail(MFI_ERR_WORKSPACE, "workspace too small for ep_experts_return");
+  ExpertScratch s = carve_experts(workspace, R, H, Mi, E, k);
+  cudaStream_t st = as_stream(stream);
+  const mfi::EpTable* tb = static_cast<const mfi::EpTable*>(table);
+  unsigned* fl = static_cast<unsigned*>(flags);
+  rc = cuda_status(cudaMemsetAsync(s.cursor, 0, sizeof(int) * s.zero_words, st),
+                   "ep_experts_return memset");
+  if (rc != MFI_OK) return rc;
+  rc = cuda_status(mfi::launch_ep_scatter_wait(tb, fl, recv, rank, n_ranks, capacity, H, k, E,
+                                               s.T_pad, s.cursor, s.perm, s.xp, s.xp_atoms,
+                                               mfi::device_error_flag(), st),
+                   "ep_experts_return scatter launch");
+  if (rc != MFI_OK) return rc;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  mfi::MoeTcLaunch L{};
+  L.E = E; L.H = H; L.Mi = Mi; L.grid = sms;
+  L.max_chunks = s.max_chunks;
+  L.prepared = static_cast<const uint8_t*>(w->prepared);
+  L.counts = s.cursor; L.perm = s.perm;
+  L.rows = E * s.T_pad;
+  L.xp = s.xp; L.xp_atoms = s.xp_atoms; L.hp = s.hp; L.hp_atoms = s.hp_atoms; L.yd = s.yd;
+  L.err = mfi::device_error_flag();
+  L.pdl = true;
+  L.pf_bytes = prefetch_bytes((long long)R * k, E, true);
+  L.queue = s.cursor + E;
+  L.ready = reinterpret_cast<unsigned*>(s.cursor + E + 1);
+  rc = cuda_status(mfi::launch_moe_tc(L, st), "ep_experts_return experts launch");
+  if (rc != MFI_OK) return rc;
+  return cuda_status(mfi::launch_ep_combine_return(tb, fl, s.yd, recv, rank, n_ranks, capacity, H,
+                                                   k, E, mfi::device_error_flag(), st),
+                     "ep_experts_return combine launch");
+}
+
+int mfi_ep_unpack_wait(int n_ranks, int capacity, int hidden, int T, void* flags, const float* ret,
+                       const int32_t* pack_pos, float* out, void* stream) {
+  if (n_ranks <= 0 || n_ranks > mfi::kEpMaxRanks) return fail(MFI_ERR_ARG, "n_ranks must be in [1, 64]");
+  if (capacity < 0 || T < 0 || T > capacity) return fail(MFI_ERR_ARG, "T must be in [0, capacity]");
+  if (hidden <= 0) return fail(MFI_ERR_ARG, "hidden must be positive");
+  if (bad_ptr(flags) || bad_ptr(ret) || (T > 0 && (bad_ptr(pack_pos) || bad_ptr(out))))
+    return fail(MFI_ERR_ARG, "null pointer");
+  if (hidden % 4 || (reinterpret_cast<uintptr_t>(ret) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
+    return fail(MFI_ERR_ARG, "ret and out must be 16-byte aligned, hidden a multiple of 4");
+  return cuda_status(mfi::launch_ep_unpack_wait(static_cast<unsigned*>(flags), ret, pack_pos, T,
+                                                n_ranks, capacity, hidden, out,
+                                                mfi::device_error_flag(), as_stream(stream)),
+                     "ep_unpack_wait launch");
 }
 
 }  // extern "C"

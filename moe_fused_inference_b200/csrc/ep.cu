@@ -37,6 +37,42 @@ struct RowLayout {
   __host__ __device__ int w_off() const { return sel_off() + 4 * k; }
 };
 
+// sum over i < m, in order, of w[i] * rows[i][off .. off+3] (w == null: the
+// plain sum) with unfused fp32 multiply and add.  All loads of a group of 8
+// rows are issued before the first add, so the sum is latency-bound once per
+// group, not once per row.  kCg: load through L2 only (rows a peer wrote).
+template <bool kCg>
+__device__ __forceinline__ float4 ordered_sum4(const float* const* rows, const float* w, int m,
+                                               size_t off) {
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int i0 = 0; i0 < m; i0 += 8) {
+    float4 v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i0 + i < m) {
+        const float4* src = reinterpret_cast<const float4*>(rows[i0 + i] + off);
+        v[i] = kCg ? __ldcg(src) : *src;
+      }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i0 + i < m) {
+        if (w) {
+          const float wi = w[i0 + i];
+          acc.x = __fadd_rn(acc.x, __fmul_rn(wi, v[i].x));
+          acc.y = __fadd_rn(acc.y, __fmul_rn(wi, v[i].y));
+          acc.z = __fadd_rn(acc.z, __fmul_rn(wi, v[i].z));
+          acc.w = __fadd_rn(acc.w, __fmul_rn(wi, v[i].w));
+        } else {
+          acc.x = __fadd_rn(acc.x, v[i].x);
+          acc.y = __fadd_rn(acc.y, v[i].y);
+          acc.z = __fadd_rn(acc.z, v[i].z);
+          acc.w = __fadd_rn(acc.w, v[i].w);
+        }
+      }
+  }
+  return acc;
+}
+
 // One CTA per token: for each destination rank that owns one of the token's
 // experts, claim a row in that rank's block and write row + metadata.
 __global__ void __launch_bounds__(128) ep_pack_kernel(const uint8_t* __restrict__ xq,
@@ -99,17 +135,30 @@ __global__ void ep_mask_recv_kernel(int n_ranks, int C, RowLayout L, uint8_t* __
 }
 
 // out[t] = sum over ranks d (in rank order) of the row returned for (t, d).
-__global__ void ep_unpack_kernel(const float* __restrict__ ret, const int* __restrict__ pack_pos,
-                                 int T, int n_ranks, int C, int H, float* __restrict__ out) {
-  const int t = blockIdx.y;
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= H) return;
-  float acc = 0.0f;
-  for (int d = 0; d < n_ranks; ++d) {
-    const int pos = pack_pos[t * n_ranks + d];
-    if (pos >= 0) acc = __fadd_rn(acc, ret[(size_t(d) * (C + 1) + 1 + pos) * H + c]);
+// One CTA per token, 4 columns per thread.
+__global__ void __launch_bounds__(128) ep_unpack_kernel(const float* __restrict__ ret,
+                                                        const int* __restrict__ pack_pos, int T,
+                                                        int n_ranks, int C, int H,
+                                                        float* __restrict__ out) {
+  const int t = blockIdx.x;
+  __shared__ const float* s_rows[kEpMaxRanks];
+  __shared__ int s_m;
+  if (threadIdx.x < 32) {
+    // lanes look at ranks d, d+32 (n <= 64); rows compacted in rank order
+    int base = 0;
+    for (int d0 = 0; d0 < n_ranks; d0 += 32) {
+      const int d = d0 + threadIdx.x;
+      const int pos = d < n_ranks ? pack_pos[t * n_ranks + d] : -1;
+      const unsigned mask = __ballot_sync(0xffffffffu, pos >= 0);
+      if (pos >= 0)
+        s_rows[base + __popc(mask & ((1u << threadIdx.x) - 1u))] = ret + (size_t(d) * (C + 1) + 1 + pos) * H;
+      base += __popc(mask);
+    }
+    if (threadIdx.x == 0) s_m = base;
   }
-  out[size_t(t) * H + c] = acc;
+  __syncthreads();
+  for (int c4 = threadIdx.x * 4; c4 < H; c4 += blockDim.x * 4)
+    *reinterpret_cast<float4*>(out + size_t(t) * H + c4) = ordered_sum4<false>(s_rows, nullptr, s_m, c4);
 }
 
 // Expert-region scatter for pre-routed rows: row r's expert list sel[r][j]
@@ -153,22 +202,241 @@ __global__ void __launch_bounds__(128) scatter_sel_kernel(
 }
 
 // Combine with a slot mask: out[m] = sum over slots j with 0 <= sel < E of
-// w[m][j] * yd[m*k + j], sequential in j (unfused multiply and add).
-__global__ void combine_sel_kernel(const float* __restrict__ yd, const int* __restrict__ sel,
-                                   long long sel_ld, const float* __restrict__ w, long long w_ld,
-                                   int k, int E, int H, float* __restrict__ out, long long out_ld) {
+// w[m][j] * yd[m*k + j], sequential in j (unfused multiply and add).  One CTA
+// per row, 4 columns per thread.
+__global__ void __launch_bounds__(128) combine_sel_kernel(
+    const float* __restrict__ yd, const int* __restrict__ sel, long long sel_ld,
+    const float* __restrict__ w, long long w_ld, int k, int E, int H, float* __restrict__ out,
+    long long out_ld) {
   tc::grid_dep_wait();  // yd comes from the previous kernel
-  const int m = blockIdx.y;
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= H) return;
-  float acc = 0.0f;
-  for (int j = 0; j < k; ++j)
-    if (unsigned(sel[size_t(m) * sel_ld + j]) < unsigned(E))
-      acc = __fadd_rn(acc, __fmul_rn(w[size_t(m) * w_ld + j], yd[(size_t(m) * k + j) * H + c]));
-  out[size_t(m) * out_ld + c] = acc;
+  const int m = blockIdx.x;
+  __shared__ const float* s_rows[32];
+  __shared__ float s_w[32];
+  __shared__ int s_m;
+  if (threadIdx.x < 32) {
+    // lane j looks at slot j; valid slots are compacted in slot order
+    const int j = threadIdx.x;
+    const bool valid = j < k && unsigned(sel[size_t(m) * sel_ld + j]) < unsigned(E);
+    const unsigned mask = __ballot_sync(0xffffffffu, valid);
+    if (valid) {
+      const int pos = __popc(mask & ((1u << j) - 1u));
+      s_rows[pos] = yd + (size_t(m) * k + j) * H;
+      s_w[pos] = w[size_t(m) * w_ld + j];
+    }
+    if (j == 0) s_m = __popc(mask);
+  }
+  __syncthreads();
+  for (int c4 = threadIdx.x * 4; c4 < H; c4 += blockDim.x * 4)
+    *reinterpret_cast<float4*>(out + size_t(m) * out_ld + c4) = ordered_sum4<false>(s_rows, s_w, s_m, c4);
+}
+
+// ---------------------------------------------------------------------------
+// Peer-memory exchange: the router writes rows straight into the owning
+// ranks' receive buffers and raises a per-source flag to the call id
+// (route.cu); the kernels below consume and answer them.  Every wait polls a
+// flag in this rank's own memory with acquire semantics at system scope and
+// gives up after kWaitLimitNs (error flag, the block is then treated as
+// empty), so no launch can hang on a peer that never writes.
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Spin (one thread) until every flag[i], i < count, is >= call; each poll is
+// an acquire load at system scope.  Bounded: returns false after the limit.
+__device__ bool wait_flags(const unsigned* flag, int count, unsigned call, int* err, int code) {
+  int i = 0;
+  const uint64_t t0 = tc::globaltimer_ns();
+  for (uint32_t spins = 0; i < count; ++spins) {
+    if (ld_acquire_sys(flag + i) >= call) {
+      ++i;
+      continue;
+    }
+    __nanosleep(64);
+    if ((spins & 255u) == 255u && tc::globaltimer_ns() - t0 > tc::kWaitLimitNs) {
+      atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ unsigned current_call(const unsigned* flags) {
+  return *reinterpret_cast<const volatile unsigned*>(flags + kFlagEpoch) + 1u;
+}
+
+// One CTA per received row: wait for the source block's dispatch flag, then
+// either mask the row (header / past the block's count: all ids -1) or claim
+// its rows in the local experts' regions (scatter_sel_kernel's work).
+__global__ void __launch_bounds__(128) ep_scatter_wait_kernel(
+    unsigned* __restrict__ flags, uint8_t* __restrict__ recv, int n, int C, RowLayout L, int E,
+    int T_pad, int* __restrict__ cursor, int* __restrict__ perm, uint8_t* __restrict__ xp,
+    uint8_t* __restrict__ xp_atoms, int* __restrict__ err) {
+  tc::grid_dep_launch();
+  const int r = blockIdx.x;
+  const int src = r / (C + 1), rr = r % (C + 1);
+  __shared__ int s_valid;
+  __shared__ int s_row[32];
+  const unsigned call = current_call(flags);
+  if (threadIdx.x == 0) {
+    const bool ok = wait_flags(flags + kFlagDispatch + src, 1, call, err, 7);
+    const int count =
+        ok ? *reinterpret_cast<const volatile int*>(recv + size_t(src) * (C + 1) * L.rb) : 0;
+    s_valid = rr >= 1 && rr - 1 < count;
+  }
+  __syncthreads();
+  uint8_t* row = recv + size_t(r) * L.rb;
+  int* sel = reinterpret_cast<int*>(row + L.sel_off());
+  if (!s_valid) {
+    if (threadIdx.x < L.k) sel[threadIdx.x] = -1;
+    return;
+  }
+  if (threadIdx.x < L.k) {
+    const int e = sel[threadIdx.x];
+    int dst = -1;
+    if (e >= E) {
+      atomicCAS(err, 0, 4);
+    } else if (e >= 0) {
+      const int pos = atomicAdd(cursor + e, 1);
+      if (pos < T_pad) {
+        dst = e * T_pad + pos;
+        perm[dst] = r * L.k + threadIdx.x;
+      } else {
+        atomicCAS(err, 0, 5);
+      }
+    }
+    s_row[threadIdx.x] = dst;
+  }
+  __syncthreads();
+  const int q16 = L.H / 32, kc = L.H / 128;
+  for (int j = 0; j < L.k; ++j) {
+    const int dst = s_row[j];
+    if (dst < 0) continue;
+    for (int i = threadIdx.x; i < q16; i += blockDim.x)
+      reinterpret_cast<uint4*>(xp + size_t(dst) * (L.H / 2))[i] = reinterpret_cast<const uint4*>(row)[i];
+    for (int i = threadIdx.x; i < kc; i += blockDim.x)
+      *reinterpret_cast<uint32_t*>(xp_atoms + (size_t(dst >> 5) * kc + i) * 512 + (dst & 31) * 16) =
+          reinterpret_cast<const uint32_t*>(row + L.sc_off())[i];
+  }
+}
+
+// Weighted sum of each valid received row's local slots (combine_sel_kernel's
+// arithmetic) written straight into the source rank's return buffer; the
+// last CTA raises this rank's return flag at every source.
+__global__ void __launch_bounds__(128) ep_combine_return_kernel(
+    const EpTable* __restrict__ table, unsigned* __restrict__ flags, const float* __restrict__ yd,
+    const uint8_t* __restrict__ recv, int rank, int n, int C, RowLayout L, int E,
+    int* __restrict__ err) {
+  tc::grid_dep_wait();  // yd comes from the expert kernel
+  const unsigned call = current_call(flags);
+  const int R = n * (C + 1);
+  __shared__ const float* s_rows[32];
+  __shared__ float s_w[32];
+  __shared__ int s_m;
+  for (int r = blockIdx.x; r < R; r += gridDim.x) {
+    if (threadIdx.x < 32) {
+      const uint8_t* row = recv + size_t(r) * L.rb;
+      const int j = threadIdx.x;
+      const bool valid =
+          j < L.k && unsigned(reinterpret_cast<const int*>(row + L.sel_off())[j]) < unsigned(E);
+      const unsigned mask = __ballot_sync(0xffffffffu, valid);
+      if (valid) {
+        const int pos = __popc(mask & ((1u << j) - 1u));
+        s_rows[pos] = yd + (size_t(r) * L.k + j) * L.H;
+        s_w[pos] = reinterpret_cast<const float*>(row + L.w_off())[j];
+      }
+      if (j == 0) s_m = __popc(mask);
+    }
+    __syncthreads();
+    const int m = s_m;
+    if (m > 0) {  // header, unused or not-for-us rows send nothing
+      const int src = r / (C + 1), rr = r % (C + 1);
+      float* dst = table->ret[src] + (size_t(rank) * (C + 1) + rr) * L.H;
+      for (int c4 = threadIdx.x * 4; c4 < L.H; c4 += blockDim.x * 4)
+        *reinterpret_cast<float4*>(dst + c4) = ordered_sum4<false>(s_rows, s_w, m, c4);
+    }
+    __syncthreads();
+  }
+  // release: every thread's stores precede thread 0's system fence
+  if (threadIdx.x != 0) return;
+  __threadfence_system();
+  if (atomicAdd(flags + kFlagDone + 1, 1u) != gridDim.x - 1) return;
+  __threadfence_system();
+  for (int d = 0; d < n; ++d) tc::st_relaxed_sys(table->flags[d] + kFlagReturn + rank, call);
+}
+
+// out[t] = sum over ranks d (ascending) of the row that rank d returned for
+// token t; waits for every rank's return flag first.  The last CTA closes the
+// call: epoch + 1.
+__global__ void __launch_bounds__(128) ep_unpack_wait_kernel(
+    unsigned* __restrict__ flags, const float* __restrict__ ret, const int* __restrict__ pack_pos,
+    int T, int n, int C, int H, float* __restrict__ out, int* __restrict__ err) {
+  const unsigned call = current_call(flags);
+  __shared__ const float* s_rows[kEpMaxRanks];
+  __shared__ int s_m;
+  const int t = blockIdx.x;
+  // thread d waits for rank d's return (in parallel), then lanes compact rows
+  const bool ok = __syncthreads_and(
+      threadIdx.x >= n || wait_flags(flags + kFlagReturn + threadIdx.x, 1, call, err, 8));
+  if (threadIdx.x < 32) {
+    int base = 0;
+    for (int d0 = 0; d0 < n; d0 += 32) {
+      const int d = d0 + threadIdx.x;
+      const int pos = (ok && t < T && d < n) ? pack_pos[t * n + d] : -1;
+      const unsigned mask = __ballot_sync(0xffffffffu, pos >= 0);
+      if (pos >= 0)
+        s_rows[base + __popc(mask & ((1u << threadIdx.x) - 1u))] = ret + (size_t(d) * (C + 1) + 1 + pos) * H;
+      base += __popc(mask);
+    }
+    if (threadIdx.x == 0) s_m = base;
+  }
+  __syncthreads();
+  if (t < T)
+    for (int c4 = threadIdx.x * 4; c4 < H; c4 += blockDim.x * 4)
+      *reinterpret_cast<float4*>(out + size_t(t) * H + c4) = ordered_sum4<true>(s_rows, nullptr, s_m, c4);
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(flags + kFlagDone + 2, 1u) == gridDim.x - 1)
+    atomicAdd(flags + kFlagEpoch, 1u);
 }
 
 }  // namespace
+
+cudaError_t launch_ep_scatter_wait(const EpTable* table, unsigned* flags, uint8_t* recv, int rank,
+                                   int n, int C, int H, int k, int E, int T_pad, int* cursor,
+                                   int* perm, uint8_t* xp, uint8_t* xp_atoms, int* err,
+                                   cudaStream_t stream) {
+  (void)table;
+  (void)rank;
+  RowLayout L{H, k, ep_row_bytes(H, k)};
+  ep_scatter_wait_kernel<<<n * (C + 1), 128, 0, stream>>>(flags, recv, n, C, L, E, T_pad, cursor,
+                                                          perm, xp, xp_atoms, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_combine_return(const EpTable* table, unsigned* flags, const float* yd,
+                                     const uint8_t* recv, int rank, int n, int C, int H, int k,
+                                     int E, int* err, cudaStream_t stream) {
+  RowLayout L{H, k, ep_row_bytes(H, k)};
+  const int R = n * (C + 1);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(R < 296 ? R : 296);
+  cfg.blockDim = dim3(128);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, ep_combine_return_kernel, table, flags, yd, recv, rank, n, C, L,
+                            E, err);
+}
+
+cudaError_t launch_ep_unpack_wait(unsigned* flags, const float* ret, const int* pack_pos, int T,
+                                  int n, int C, int H, float* out, int* err, cudaStream_t stream) {
+  ep_unpack_wait_kernel<<<T > 0 ? T : 1, 128, 0, stream>>>(flags, ret, pack_pos, T, n, C, H, out,
+                                                           err);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_ep_pack(const uint8_t* xq, const uint8_t* xsc, const int* topi,
                            const float* topw, int T, int H, int k, int n_ranks, int e_local, int C,
@@ -198,8 +466,7 @@ cudaError_t launch_ep_mask_recv(int n_ranks, int C, int H, int k, uint8_t* recv,
 cudaError_t launch_ep_unpack(const float* ret, const int* pack_pos, int T, int n_ranks, int C,
                              int H, float* out, cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
-  dim3 grid((H + 255) / 256, T);
-  ep_unpack_kernel<<<grid, 256, 0, stream>>>(ret, pack_pos, T, n_ranks, C, H, out);
+  ep_unpack_kernel<<<T, 128, 0, stream>>>(ret, pack_pos, T, n_ranks, C, H, out);
   return cudaGetLastError();
 }
 
@@ -218,8 +485,8 @@ cudaError_t launch_combine_sel(const float* yd, const int* sel, long long sel_ld
                                long long out_ld, cudaStream_t stream) {
   if (R == 0) return cudaSuccess;
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3((H + 255) / 256, R);
-  cfg.blockDim = dim3(256);
+  cfg.gridDim = dim3(R);
+  cfg.blockDim = dim3(128);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -348,6 +348,39 @@ __device__ __forceinline__ void st_cluster_f32(const void* local, uint32_t rank,
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
 }
 
+__device__ __forceinline__ int ep_row_bytes_dev(int H, int k) {
+  return (H / 2 + H / 32 + 16 + 8 * k + 15) / 16 * 16;
+}
+
+// Completion of an expert-parallel dispatch, run by every thread of each
+// cluster leader after its rows are written: the last leader writes each
+// destination block's header (row count) and raises this rank's dispatch
+// flag at every destination to the call id.
+__device__ void ep_finish_dispatch(const EpDispatch& ep, int H, int k, int n_leaders,
+                                   unsigned call) {
+  __shared__ int s_last;
+  __syncthreads();  // every thread's row stores precede thread 0's fence
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    s_last = atomicAdd(ep.flags + kFlagDone + 0, 1u) == unsigned(n_leaders - 1);
+    if (s_last) __threadfence_system();  // the other leaders' rows and counts
+  }
+  __syncthreads();
+  if (!s_last) return;
+  if (threadIdx.x < ep.n) {
+    const int d = threadIdx.x;
+    const int rb = ep_row_bytes_dev(H, k);
+    const int cnt = int(*reinterpret_cast<volatile unsigned*>(ep.flags + kFlagCounts + d));
+    *reinterpret_cast<volatile int*>(ep.table->recv[d] + size_t(ep.rank) * (ep.C + 1) * rb) = cnt;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();  // headers (all threads) before the flags
+    for (int d = 0; d < ep.n; ++d)
+      tc::st_relaxed_sys(ep.table->flags[d] + kFlagDispatch + ep.rank, call);
+  }
+}
+
 template <int kMaxBlk>
 __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArgs a, int n_split) {
   tc::grid_dep_launch();
@@ -360,6 +393,15 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
   const uint32_t crank = cluster_ctarank();
   const int t = blockIdx.x / n_split;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // expert parallelism: the call id this dispatch belongs to (the epoch only
+  // moves at the end of the call); a launch for T = 0 tokens has one cluster
+  // that only joins the completion
+  const unsigned ep_call =
+      a.ep.table ? *reinterpret_cast<volatile unsigned*>(a.ep.flags + kFlagEpoch) + 1u : 0u;
+  if (a.ep.table && t >= a.ep.T) {
+    if (crank == 0) ep_finish_dispatch(a.ep, a.H, a.k, int(gridDim.x) / n_split, ep_call);
+    return;
+  }
   const int nb = a.H >> 5;
   const int e_begin = int(crank) * kExpertsPerCta;
   const int n_e = min(kExpertsPerCta, a.E - e_begin);
@@ -413,7 +455,7 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
     }
   }
   __syncthreads();
-  if (crank == 0) {
+  if (crank == 0 && a.xq) {
     for (int i = threadIdx.x; i < (a.H >> 3); i += kClusterThreads)
       reinterpret_cast<uint32_t*>(a.xq + long(t) * (a.H >> 1))[i] = reinterpret_cast<uint32_t*>(s_xq)[i];
     for (int i = threadIdx.x; i < nb; i += kClusterThreads) a.xsc[long(t) * nb + i] = s_xsc[i];
@@ -508,14 +550,17 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
   }
   __syncthreads();
   __shared__ int s_row[32];
+  __shared__ float s_tw[32];
   if (warp == 0) {
     const float mx = s_selv[0];
     const float p = (lane < a.k) ? expf(s_selv[lane < a.k ? lane : 0] - mx) : 0.f;
     float sum = 0.f;
     for (int j = 0; j < a.k; ++j) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, p, j));
     if (lane < a.k) {
+      const float wgt = __fdiv_rn(p, sum);
       a.topi[long(t) * a.k + lane] = s_sel[lane];
-      a.topw[long(t) * a.k + lane] = __fdiv_rn(p, sum);
+      a.topw[long(t) * a.k + lane] = wgt;
+      s_tw[lane] = wgt;
       if (a.xp) {
         const int e = s_sel[lane];
         const int pos = atomicAdd(a.cursor + e, 1);
@@ -524,6 +569,41 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
         a.perm[row] = t * a.k + lane;
       }
     }
+  }
+  if (a.ep.table) {
+    // ---- expert parallelism: send the token to every rank owning one of its
+    // experts, straight into that rank's receive buffer (peer memory) --------
+    const EpDispatch& ep = a.ep;
+    __shared__ int s_dpos[kEpMaxRanks];
+    __syncthreads();
+    if (threadIdx.x < ep.n) {
+      const int d = threadIdx.x;
+      bool any = false;
+      for (int j = 0; j < a.k; ++j) any |= (s_sel[j] / ep.el) == d;
+      const int pos = any ? int(atomicAdd(ep.flags + kFlagCounts + d, 1u)) : -1;
+      s_dpos[d] = pos;
+      ep.pack_pos[long(t) * ep.n + d] = pos;
+    }
+    __syncthreads();
+    const int rb = ep_row_bytes_dev(a.H, a.k);
+    const int meta = (a.H >> 1) + nb;
+    for (int d = 0; d < ep.n; ++d) {
+      const int pos = s_dpos[d];
+      if (pos < 0) continue;
+      uint8_t* row = ep.table->recv[d] + (size_t(ep.rank) * (ep.C + 1) + 1 + pos) * rb;
+      for (int i = threadIdx.x; i < (a.H >> 5); i += kClusterThreads)
+        reinterpret_cast<uint4*>(row)[i] = reinterpret_cast<const uint4*>(s_xq)[i];
+      for (int i = threadIdx.x; i < (a.H >> 7); i += kClusterThreads)
+        reinterpret_cast<uint32_t*>(row + (a.H >> 1))[i] = reinterpret_cast<const uint32_t*>(s_xsc)[i];
+      if (threadIdx.x == 0) reinterpret_cast<int*>(row + meta)[0] = t;
+      if (threadIdx.x < a.k) {
+        const int e = s_sel[threadIdx.x];
+        reinterpret_cast<int*>(row + meta + 16)[threadIdx.x] = (e / ep.el) == d ? e % ep.el : -1;
+        reinterpret_cast<float*>(row + meta + 16 + 4 * a.k)[threadIdx.x] = s_tw[threadIdx.x];
+      }
+    }
+    ep_finish_dispatch(ep, a.H, a.k, int(gridDim.x) / n_split, ep_call);
+    return;
   }
   if (a.xp) {
     __syncthreads();
@@ -556,7 +636,8 @@ static cudaError_t launch_route_cluster(const RouteArgs& a, cudaStream_t stream)
     smem_set = true;
   }
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(a.T * n_split);
+  const int clusters = a.ep.table ? (a.T > 0 ? a.T : 1) : a.T;
+  cfg.gridDim = dim3(clusters * n_split);
   cfg.blockDim = dim3(kClusterThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -571,7 +652,7 @@ static cudaError_t launch_route_cluster(const RouteArgs& a, cudaStream_t stream)
 }
 
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t stream) {
-  if (a.T <= 0) return cudaSuccess;
+  if (a.T < 0 || (a.T == 0 && !a.ep.table)) return cudaSuccess;
   if (a.H > 4096) return cudaErrorInvalidValue;
   if (!a.g_gu) {
     // routing alone, or routing + expert regions for the tensor-core kernels

@@ -185,6 +185,25 @@ __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// ---------------------------------------------------------------- peer flags
+// System-scope flag traffic between GPUs.  A fence at system scope is costly
+// (microseconds), so each CTA issues it once, from one thread, around relaxed
+// flag accesses: a writer stores its data (all threads), bar.sync, then one
+// thread fences and stores the flag (release pattern); a reader polls the
+// flag with relaxed loads, fences once, then bar.sync before the data reads
+// (acquire pattern).
+__device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_sys(unsigned* p, unsigned v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
 // Programmatic dependent launch.  grid_dep_wait() returns once every grid
 // this one depends on has completed and its memory is visible (immediately
 // for a launch without the programmatic-serialisation attribute), so a kernel

@@ -39,6 +39,32 @@ struct ChunkDesc {
   int pad;
 };
 
+// ---- expert parallelism over peer memory (ep.cu, route.cu) -----------------
+// Per-rank flag area (32-bit words), in memory every peer maps:
+constexpr int kEpMaxRanks = 64;
+constexpr int kFlagDispatch = 0;    // [s]: call id of the last dispatch received from rank s
+constexpr int kFlagReturn = 64;     // [d]: call id of the last return received from rank d
+constexpr int kFlagEpoch = 128;     // calls completed by this rank
+constexpr int kFlagCounts = 160;    // [d]: rows sent to rank d in this call (zeroed per call)
+constexpr int kFlagDone = 224;      // completion counters of this call's launches (zeroed per call)
+constexpr int kFlagWords = 256;
+constexpr int kFlagZeroFirst = kFlagCounts;  // per-call zeroed range [kFlagCounts, kFlagWords)
+
+// Peer pointers of one exchange, as seen from this rank (device copy).
+struct EpTable {
+  uint8_t* recv[kEpMaxRanks];   // rank d's receive buffer [n][C+1][row bytes]
+  float* ret[kEpMaxRanks];      // rank d's return buffer [n][C+1][hidden]
+  unsigned* flags[kEpMaxRanks]; // rank d's flag area
+};
+
+struct EpDispatch {            // route_cluster_kernel: send each routed token to its ranks
+  const EpTable* table;
+  unsigned* flags;             // this rank's flag area
+  int* pack_pos;               // (T, n): row of token t in its block at rank d, or -1
+  int rank, n, C, el;          // rank, ranks, capacity, experts per rank
+  int T;                       // real tokens (clusters past T only join the completion)
+};
+
 struct RouteArgs {
   const void* x;       // bf16 (T, H): quantised inside the kernel into xq/xsc
   uint8_t* xq;         // (T, H/2)
@@ -72,6 +98,7 @@ struct RouteArgs {
   // in the order the next kernel reads them), issued once the inputs are in
   const uint8_t* pf_base;
   unsigned long long pf_bytes;
+  EpDispatch ep;       // ep.table == null: no expert-parallel dispatch
 };
 
 constexpr int kRouteMaxE = 256;
@@ -146,6 +173,17 @@ cudaError_t launch_scatter_sel(const uint8_t* xq, long long xq_ld, const uint8_t
 cudaError_t launch_combine_sel(const float* yd, const int* sel, long long sel_ld, const float* w,
                                long long w_ld, int R, int k, int E, int H, float* out,
                                long long out_ld, cudaStream_t stream);
+
+// Peer-memory exchange (ep.cu).
+cudaError_t launch_ep_scatter_wait(const EpTable* table, unsigned* flags, uint8_t* recv, int rank,
+                                   int n, int C, int H, int k, int E, int T_pad, int* cursor,
+                                   int* perm, uint8_t* xp, uint8_t* xp_atoms, int* err,
+                                   cudaStream_t stream);
+cudaError_t launch_ep_combine_return(const EpTable* table, unsigned* flags, const float* yd,
+                                     const uint8_t* recv, int rank, int n, int C, int H, int k,
+                                     int E, int* err, cudaStream_t stream);
+cudaError_t launch_ep_unpack_wait(unsigned* flags, const float* ret, const int* pack_pos, int T,
+                                  int n, int C, int H, float* out, int* err, cudaStream_t stream);
 
 // Device-wide error flag written by kernels whose bounded waits time out.
 int* device_error_flag();

@@ -3,7 +3,21 @@ combine as NCCL all-to-all over NVLink.
 
 The reference runs the MoE block on one GPU (runtime/model_runner_v2.py:183-208,
 :266-290) and has no collective anywhere; this module is the multi-GPU form of
-the same block.  Per layer and rank, with no host synchronisation:
+the same block.  Two transports move the same rows:
+
+``transport="p2p"`` (default on GPUs): the exchange is fused into the kernels.
+The router stores each token's row straight into the receive buffer of every
+rank that owns one of its experts (NVLink stores through CUDA IPC mappings,
+mfi_ep_route_dispatch); the expert side waits on per-source flags, runs the
+local experts and stores each row's weighted slot sum straight back into the
+source's return buffer (mfi_ep_experts_return); the source waits for every
+rank's return and sums in rank order (mfi_ep_unpack_wait).  Only the rows that
+exist cross NVLink, no collective library runs on the data path and flags
+carry call ids, so a whole decode step can be captured in one CUDA graph.
+
+``transport="nccl"``: the same rows in fixed-capacity blocks exchanged with
+two ``all_to_all_single`` calls.  Per layer and rank, with no host
+synchronisation:
 
   route     mfi_moe_route: quantise the rank's tokens, router GEMM, top-k
             (full router on every rank, so the routing is the single-GPU one)
@@ -188,6 +202,106 @@ class CudaEPOps:
                                           self.C, self.H, out.data_ptr(), _stream(out.device)),
                    "ep_unpack")
 
+    # ---- peer-memory transport ----
+    def p2p_dispatch(self, x, topi, topw, pack_pos, xch, C):
+        rank = xch.rank
+        _lib.check(self.lib.mfi_ep_route_dispatch(
+            ctypes.byref(self._route_w), x.data_ptr(), x.shape[0], rank, self.world, C,
+            xch.table.data_ptr(), xch.flags, topi.data_ptr(), topw.data_ptr(),
+            pack_pos.data_ptr(), _stream(x.device)), "ep_route_dispatch")
+
+    def p2p_experts(self, xch, C):
+        dev = self.ws.device
+        _lib.check(self.lib.mfi_ep_experts_return(
+            ctypes.byref(self._exp_w), xch.rank, self.world, C, xch.table.data_ptr(), xch.flags,
+            xch.recv, self.ws.data_ptr(), self.ws.numel(), _stream(dev)), "ep_experts_return")
+
+    def p2p_finish(self, T, out, pack_pos, xch, C):
+        _lib.check(self.lib.mfi_ep_unpack_wait(
+            self.world, C, self.H, T, xch.flags, xch.ret, pack_pos.data_ptr(), out.data_ptr(),
+            _stream(out.device)), "ep_unpack_wait")
+
+
+class P2PExchange:
+    """This rank's exchange memory — receive buffer, return buffer and flag
+    area in one block that the peers map through CUDA IPC — and the device
+    table of every rank's addresses as seen from this rank."""
+
+    def __init__(self, world: int, rank: int, capacity: int, hidden: int, top_k: int, device):
+        lib = _lib.load()
+        self.lib = lib
+        self.world, self.rank = world, rank
+        self.recv_bytes = int(lib.mfi_ep_recv_bytes(world, capacity, hidden, top_k))
+        self.ret_bytes = int(lib.mfi_ep_ret_bytes(world, capacity, hidden))
+        self.flag_bytes = int(lib.mfi_ep_flag_bytes())
+        if not (self.recv_bytes and self.ret_bytes and self.flag_bytes):
+            raise RuntimeError("invalid exchange shape")
+        up = lambda v: (v + 255) // 256 * 256
+        self.off_ret = up(self.recv_bytes)
+        self.off_flags = self.off_ret + up(self.ret_bytes)
+        self.total = self.off_flags + up(self.flag_bytes)
+        ptr = ctypes.c_void_p()
+        _lib.check(lib.mfi_ipc_alloc(self.total, ctypes.byref(ptr)), "ipc_alloc")
+        self.base = int(ptr.value)
+        self.table = torch.empty(int(lib.mfi_ep_table_bytes()), dtype=torch.uint8, device=device)
+        self._opened: list[int] = []
+
+    @property
+    def recv(self) -> int:
+        return self.base
+
+    @property
+    def ret(self) -> int:
+        return self.base + self.off_ret
+
+    @property
+    def flags(self) -> int:
+        return self.base + self.off_flags
+
+    def copy_recv_to(self, dst: torch.Tensor) -> None:
+        """Copy this rank's receive buffer into a cuda tensor (inspection)."""
+        if dst.numel() * dst.element_size() < self.recv_bytes or not dst.is_contiguous():
+            raise RuntimeError("destination too small")
+        _lib.check(self.lib.mfi_copy_async(dst.data_ptr(), self.recv, self.recv_bytes,
+                                           _stream(dst.device)), "copy")
+
+    def handle(self) -> bytes:
+        h = ctypes.create_string_buffer(64)
+        _lib.check(self.lib.mfi_ipc_handle(self.base, h), "ipc_handle")
+        return h.raw
+
+    def connect(self, bases) -> None:
+        """bases[d]: rank d's block address as seen from this rank."""
+        n = self.world
+        if len(bases) != n:
+            raise RuntimeError("one base address per rank")
+        arr = lambda off: (ctypes.c_void_p * n)(*[b + off for b in bases])
+        _lib.check(self.lib.mfi_ep_table_set(self.table.data_ptr(), n, arr(0), arr(self.off_ret),
+                                             arr(self.off_flags)), "ep_table_set")
+
+    def connect_group(self, group=None) -> None:
+        """Exchange IPC handles over the process group and map every peer."""
+        handles = [None] * self.world
+        dist.all_gather_object(handles, self.handle(), group=group)
+        bases = []
+        for d, h in enumerate(handles):
+            if d == self.rank:
+                bases.append(self.base)
+                continue
+            ptr = ctypes.c_void_p()
+            _lib.check(self.lib.mfi_ipc_open(h, ctypes.byref(ptr)), "ipc_open")
+            self._opened.append(int(ptr.value))
+            bases.append(int(ptr.value))
+        self.connect(bases)
+
+    def close(self) -> None:
+        for p in self._opened:
+            self.lib.mfi_ipc_close(p)
+        self._opened = []
+        if self.base:
+            self.lib.mfi_ipc_free(self.base)
+            self.base = 0
+
 
 class EPMoELayer:
     """One MoE layer sharded over the ranks of ``group`` (expert parallelism).
@@ -197,7 +311,8 @@ class EPMoELayer:
     are collective)."""
 
     def __init__(self, shard: EPShard, top_k: int, capacity: int, group=None, ops=None,
-                 device=None, world: int | None = None, rank: int | None = None):
+                 device=None, world: int | None = None, rank: int | None = None,
+                 transport: str | None = None, connect: bool = True):
         self.group = group
         # world / rank may be given to drive the steps without a process group
         # (all ranks of a test in one process, the exchange done by copies)
@@ -220,10 +335,29 @@ class EPMoELayer:
         self.topw = torch.empty((C, top_k), dtype=torch.float32, device=dev)
         self.counts = torch.zeros(n, dtype=torch.int32, device=dev)
         self.pack_pos = torch.empty((C, n), dtype=torch.int32, device=dev)
-        self.send = torch.zeros((n, C + 1, rb), dtype=torch.uint8, device=dev)
-        self.recv = torch.zeros_like(self.send)
-        self.ret = torch.empty((n, C + 1, H), dtype=torch.float32, device=dev)
-        self.ret_back = torch.empty_like(self.ret)
+        if transport is None:
+            transport = "nccl" if ops is not None or not torch.device(dev).type == "cuda" else "p2p"
+        if transport not in ("p2p", "nccl"):
+            raise RuntimeError("transport must be 'p2p' or 'nccl'")
+        self.transport = transport
+        self.xch = None
+        if transport == "p2p":
+            if not isinstance(self.ops, CudaEPOps):
+                raise RuntimeError("the p2p transport runs on the GPU library only")
+            self.xch = P2PExchange(n, self.rank, C, H, top_k, dev)
+            if connect:
+                self.xch.connect_group(group)
+        else:
+            self.send = torch.zeros((n, C + 1, rb), dtype=torch.uint8, device=dev)
+            self.recv = torch.zeros_like(self.send)
+            self.ret = torch.empty((n, C + 1, H), dtype=torch.float32, device=dev)
+            self.ret_back = torch.empty_like(self.ret)
+
+    def close(self) -> None:
+        """Release the peer mappings (p2p transport)."""
+        if self.xch is not None:
+            self.xch.close()
+            self.xch = None
 
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None):
         """x bf16 (T, hidden), T <= capacity -> fp32 (T, hidden); also leaves the
@@ -235,6 +369,11 @@ class EPMoELayer:
             raise RuntimeError(f"x must have {self.shard.hidden} columns")
         if out is None:
             out = torch.empty((T, H), dtype=torch.float32, device=x.device)
+        if self.transport == "p2p":
+            self.p2p_dispatch(x)
+            self.p2p_experts()
+            self.p2p_finish(T, out)
+            return out
         self.dispatch_prepare(x)
         dist.all_to_all_single(self.recv.view(-1), self.send.view(-1), group=self.group)
         self.compute()
@@ -259,5 +398,16 @@ class EPMoELayer:
     def finish(self, T: int, out: torch.Tensor) -> None:
         """Sum the returned rows of ``self.ret_back`` into out (T, hidden)."""
         self.ops.unpack(self.ret_back, self.pack_pos, T, out)
+
+    # p2p transport: the three launches groups of a forward, in order
+    def p2p_dispatch(self, x: torch.Tensor) -> None:
+        x = x.contiguous()
+        self.ops.p2p_dispatch(x, self.topi, self.topw, self.pack_pos, self.xch, self.C)
+
+    def p2p_experts(self) -> None:
+        self.ops.p2p_experts(self.xch, self.C)
+
+    def p2p_finish(self, T: int, out: torch.Tensor) -> None:
+        self.ops.p2p_finish(T, out, self.pack_pos, self.xch, self.C)
 
     __call__ = forward

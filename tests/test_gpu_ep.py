@@ -40,9 +40,11 @@ def _x(T, H, seed):
 
 
 def _emulate(w, xs, world, k, capacity):
-    """Run an EP layer over `world` virtual ranks in this process."""
+    """Run an EP layer (all-to-all transport) over `world` virtual ranks in
+    this process, the all-to-alls done by copies."""
     from moe_fused_inference_b200.ep import EPMoELayer, EPShard
-    layers = [EPMoELayer(EPShard.from_layer(w, r, world), k, capacity, world=world, rank=r)
+    layers = [EPMoELayer(EPShard.from_layer(w, r, world), k, capacity, world=world, rank=r,
+                         transport="nccl")
               for r in range(world)]
     for L, x in zip(layers, xs):
         L.dispatch_prepare(x)
@@ -85,6 +87,57 @@ def test_ep_emulated_matches_single_gpu(world, counts):
         assert cosine(a, b) >= 0.999999
 
 
+def _emulate_p2p(w, xs, world, k, capacity, calls=1):
+    """The peer-memory transport over `world` virtual ranks on one GPU: every
+    rank's block is an allocation of this process, so the peer table holds
+    plain device addresses.  Launch order keeps every wait already satisfied
+    when it runs: all dispatches, then all expert steps, then all unpacks."""
+    from moe_fused_inference_b200.ep import EPMoELayer, EPShard
+    layers = [EPMoELayer(EPShard.from_layer(w, r, world), k, capacity, world=world, rank=r,
+                         transport="p2p", connect=False)
+              for r in range(world)]
+    bases = [L.xch.base for L in layers]
+    for L in layers:
+        L.xch.connect(bases)
+    outs = []
+    for _ in range(calls):
+        for L, x in zip(layers, xs):
+            L.p2p_dispatch(x)
+        for L in layers:
+            L.p2p_experts()
+        outs = []
+        for L, x in zip(layers, xs):
+            out = torch.full((x.shape[0], w.hidden), float("nan"), dtype=torch.float32,
+                             device="cuda")
+            L.p2p_finish(x.shape[0], out)
+            outs.append(out)
+        torch.cuda.synchronize()
+    return layers, outs
+
+
+@pytest.mark.parametrize("world,counts", [(2, [64, 64]), (4, [64, 17, 0, 33]),
+                                          (8, [1, 0, 5, 64, 2, 31, 8, 3])])
+def test_ep_p2p_emulated_matches_all_to_all(world, counts):
+    """Peer-memory transport: same routing, bit-identical outputs to the
+    all-to-all transport (same rows, same sums, same order), over three
+    consecutive calls (call ids advance, buffers are reused)."""
+    E, H, Mi, k = 128, 2048, 768, 8
+    w = _layer_w(E, H, Mi, seed=21)
+    xs = [_x(t, H, 90 + r) for r, t in enumerate(counts)]
+    ref_layers, ref = _emulate(w, xs, world, k, max(counts))
+    layers, outs = _emulate_p2p(w, xs, world, k, max(counts), calls=3)
+    try:
+        lib = _lib().load()
+        assert lib.mfi_device_error(1) == 0
+        for r, x in enumerate(xs):
+            T = x.shape[0]
+            assert torch.equal(layers[r].topi[:T], ref_layers[r].topi[:T])
+            assert torch.equal(outs[r], ref[r])
+    finally:
+        for L in layers:
+            L.close()
+
+
 def test_ep_pack_rows_match_restatement():
     """The packed rows (keyed by token: row order inside a block follows
     atomics) equal the CPU restatement byte for byte."""
@@ -92,7 +145,7 @@ def test_ep_pack_rows_match_restatement():
     E, H, Mi, k, world, T = 32, 512, 256, 4, 4, 23
     w = _layer_w(E, H, Mi, seed=11)
     x = _x(T, H, 5)
-    L = EPMoELayer(EPShard.from_layer(w, 1, world), k, T, world=world, rank=1)
+    L = EPMoELayer(EPShard.from_layer(w, 1, world), k, T, world=world, rank=1, transport="nccl")
     L.dispatch_prepare(x)
     torch.cuda.synchronize()
     W = mx.MoELayerWeights(*(t.cpu().numpy() for t in (w.gate_wp, w.gate_sc, w.up_wp, w.up_sc,
@@ -238,7 +291,7 @@ def _free_port():
     return p
 
 
-def _nccl_worker(rank, world, port, outdir):
+def _nccl_worker(rank, world, port, outdir, transport):
     import torch.distributed as dist
     from datetime import timedelta
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -252,10 +305,12 @@ def _nccl_worker(rank, world, port, outdir):
         w = _layer_w(128, 2048, 768)
         counts = [64, 40]
         x = _x(counts[rank], 2048, 70 + rank)
-        ep = EPMoELayer(EPShard.from_layer(w, rank, world), 8, 64)
+        ep = EPMoELayer(EPShard.from_layer(w, rank, world), 8, 64, transport=transport)
         out = ep(x)
+        out = ep(x)  # a second call: the call ids advance
         ref, topi, _ = MoELayer(w, top_k=8)(x)
         torch.cuda.synchronize()
+        ep.close()
         np.save(os.path.join(outdir, f"nccl{rank}.npy"),
                 np.array([max_rel_err(out.cpu().numpy(), ref.cpu().numpy()),
                           float(torch.equal(ep.topi[: counts[rank]], topi))]))
@@ -266,10 +321,11 @@ def _nccl_worker(rank, world, port, outdir):
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs 2 GPUs")
-def test_ep_nccl_two_ranks(tmp_path):
+@pytest.mark.parametrize("transport", ["p2p", "nccl"])
+def test_ep_nccl_two_ranks(tmp_path, transport):
     import torch.multiprocessing as mp
-    mp.start_processes(_nccl_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
-                       start_method="spawn")
+    mp.start_processes(_nccl_worker, args=(2, _free_port(), str(tmp_path), transport), nprocs=2,
+                       join=True, start_method="spawn")
     for r in range(2):
         rel, same = np.load(os.path.join(tmp_path, f"nccl{r}.npy"))
         assert same == 1.0 and rel <= 1e-5
