@@ -168,7 +168,9 @@ typedef struct mfi_moe_weights {
   int hidden;               /* multiple of 32, <= 4096                */
   int inter;                /* multiple of 32                         */
   int top_k;                /* 1..min(E, 32)                          */
-  const void* prepared;     /* scale atoms from mfi_moe_prepare, or NULL */
+  const void* prepared;     /* blocks from mfi_moe_prepare, or NULL       */
+  const float* logit_bias;  /* [E] fp32 added to the router logits before
+                               top-k (e.g. a synthetic load skew), or NULL */
 } mfi_moe_weights;
 
 /* Tensor-core form of the layer's expert weights.  When hidden and inter are
@@ -183,8 +185,12 @@ size_t mfi_moe_prepared_bytes(int n_experts, int hidden, int inter);
 int mfi_moe_prepare(const mfi_moe_weights* w, void* prepared, size_t prepared_bytes, void* stream);
 
 /* x: bf16 (T, hidden) -> out fp32 (T, hidden); topi int32 (T, top_k) and
- * topw fp32 (T, top_k) receive the routing; logits fp32 (T, E) may be NULL.
- * T <= 4096 / top_k. */
+ * topw fp32 (T, top_k) receive the routing; logits fp32 (T, E) may be NULL
+ * (with logit_bias set they hold the biased logits top-k ranked).
+ * Decode sizes (T * top_k <= 4096) run the decode kernels; larger T, up to
+ * T * top_k <= 262144, runs the prefill path of mfi_moe_layer_prefill
+ * (needs hidden and inter multiples of 256).  The decode combine is
+ * bit-reproducible; the prefill one sums a token's slots in arrival order. */
 size_t mfi_moe_layer_workspace_bytes(int T, int hidden, int inter, int n_experts, int top_k);
 int mfi_moe_layer(const mfi_moe_weights* w, const void* x_bf16, int T, float* out, int32_t* topi,
                   float* topw, float* logits, void* workspace, size_t workspace_bytes,
@@ -201,6 +207,17 @@ int mfi_moe_layer(const mfi_moe_weights* w, const void* x_bf16, int T, float* ou
 int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float* out,
                      int32_t* topi, float* topw, float* logits, void* workspace,
                      size_t workspace_bytes, void* const* events, int n_events, void* stream);
+
+/* Prefill path for any T >= 1 (T * top_k <= 262144): router with count-based
+ * compact placement (per-expert rows rounded up to 128-token tiles), then one
+ * persistent tcgen05 launch of 128-token x 128-row tiles: gate/up with the
+ * SwiGLU requantisation in the epilogue, down scaled by the routing weight
+ * and added into out (fp32 vector reductions).  Needs `prepared`. */
+size_t mfi_moe_layer_prefill_workspace_bytes(int T, int hidden, int inter, int n_experts,
+                                             int top_k);
+int mfi_moe_layer_prefill(const mfi_moe_weights* w, const void* x_bf16, int T, float* out,
+                          int32_t* topi, float* topw, float* logits, void* workspace,
+                          size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
  * The layer in two halves, for expert parallelism (no reference counterpart:

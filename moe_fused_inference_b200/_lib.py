@@ -44,6 +44,8 @@ SIGNATURES = {
     "mfi_moe_layer": (_I, [_VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _SZ, _VP]),
     "mfi_moe_layer_ex": (_I, [_VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _SZ, _VP, _I, _VP]),
     "mfi_moe_route": (_I, [_VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _VP]),
+    "mfi_moe_layer_prefill_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
+    "mfi_moe_layer_prefill": (_I, [_VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _SZ, _VP]),
     "mfi_moe_experts_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
     "mfi_moe_experts": (_I, [_VP, _VP, _LL, _VP, _LL, _VP, _LL, _VP, _LL, _I, _VP, _LL, _VP, _SZ,
                              _VP]),
@@ -78,7 +80,7 @@ class MoEWeights(ctypes.Structure):
         ("gate_wp", _VP), ("gate_sc", _VP), ("up_wp", _VP), ("up_sc", _VP),
         ("down_wp", _VP), ("down_sc", _VP), ("router_wp", _VP), ("router_sc", _VP),
         ("n_experts", _I), ("hidden", _I), ("inter", _I), ("top_k", _I),
-        ("prepared", _VP),
+        ("prepared", _VP), ("logit_bias", _VP),
     ]
 
 

@@ -362,6 +362,132 @@ LayerScratch carve_layer(void* ws, int T, int H, int Mi, int E, int k) {
 }
 }  // namespace
 
+namespace {
+// Prefill workspace: per-call counters (zeroed), routing scratch, compact
+// expert rows of the quantised tokens and of h with their 128-row atoms.
+struct PrefillScratch {
+  int* counts;          // [E] tokens per expert (router cursors)
+  int* queue;           // work-item counter
+  unsigned* ready;      // [max tiles]
+  size_t zero_words;
+  int* slot_pos;        // [T*k]
+  uint8_t* xq; uint8_t* xsc;
+  int* perm;
+  uint8_t* xp; uint8_t* xa; uint8_t* hp; uint8_t* ha;
+  int rows;
+  size_t bytes;
+};
+
+PrefillScratch carve_prefill(void* ws, int T, int H, int Mi, int E, int k) {
+  Carve c(ws);
+  PrefillScratch s;
+  const int P = T * k;
+  const size_t max_tiles = size_t(E) + size_t(P) / 128 + 1;
+  s.zero_words = size_t(E) + 1 + max_tiles;
+  s.counts = c.take<int>(s.zero_words);
+  s.queue = s.counts + E;
+  s.ready = reinterpret_cast<unsigned*>(s.counts + E + 1);
+  s.slot_pos = c.take<int>(size_t(P));
+  s.xq = c.take<uint8_t>(size_t(T) * (H / 2));
+  s.xsc = c.take<uint8_t>(size_t(T) * (H / 32));
+  s.rows = int(mfi::prefill_rows(P, E));
+  s.perm = c.take<int>(size_t(s.rows));
+  s.xp = c.take<uint8_t>(size_t(s.rows) * (H / 2));
+  s.xa = c.take<uint8_t>(size_t(s.rows) / 128 * (H / 128) * 512);
+  s.hp = c.take<uint8_t>(size_t(s.rows) * (Mi / 2));
+  s.ha = c.take<uint8_t>(size_t(s.rows) / 128 * (Mi / 128) * 512);
+  s.bytes = c.used + 256;
+  return s;
+}
+
+// Decode kernels up to this many (token, slot) pairs, prefill beyond.
+constexpr long long kDecodeMaxPairs = 4096;
+
+bool use_prefill(int T, int H, int Mi, int k) {
+  return layer_uses_tc(H, Mi) && (long long)T * k > kDecodeMaxPairs;
+}
+
+int run_prefill(const mfi_moe_weights* w, const void* x_bf16, int T, float* out, int32_t* topi,
+                float* topw, float* logits, void* workspace, size_t workspace_bytes,
+                cudaStream_t st) {
+  const int E = w->n_experts, H = w->hidden, Mi = w->inter, k = w->top_k;
+  if (!layer_uses_tc(H, Mi))
+    return fail(MFI_ERR_ARG, "the prefill path needs hidden and inter to be multiples of 256");
+  if ((long long)T * k > mfi::kPrefillMaxPairs) return fail(MFI_ERR_ARG, "T * top_k must be <= 262144");
+  if (bad_ptr(w->prepared)) return fail(MFI_ERR_ARG, "weights.prepared is null (mfi_moe_prepare)");
+  if ((reinterpret_cast<uintptr_t>(out) & 15) != 0) return fail(MFI_ERR_ARG, "out must be 16-byte aligned");
+  PrefillScratch s = carve_prefill(workspace, T, H, Mi, E, k);
+  if (workspace_bytes < s.bytes) return fail(MFI_ERR_WORKSPACE, "workspace too small for the prefill layer");
+  int rc = cuda_status(cudaMemsetAsync(s.counts, 0, sizeof(int) * s.zero_words, st),
+                       "moe_layer prefill memset");
+  if (rc != MFI_OK) return rc;
+  mfi::RouteArgs ra{};
+  ra.x = x_bf16; ra.xq = s.xq; ra.xsc = s.xsc; ra.wr = w->router_wp; ra.sr = w->router_sc;
+  ra.T = T; ra.H = H; ra.E = E; ra.k = k;
+  ra.logits = logits; ra.topi = topi; ra.topw = topw;
+  ra.cursor = s.counts; ra.slot_pos = s.slot_pos; ra.out_zero = out;
+  ra.logit_bias = w->logit_bias;
+  ra.err = mfi::device_error_flag();
+  rc = cuda_status(mfi::launch_route(ra, st), "moe_layer prefill route launch");
+  if (rc != MFI_OK) return rc;
+  rc = cuda_status(mfi::launch_prefill_scatter(s.xq, s.xsc, topi, s.slot_pos, s.counts, T, E, k, H,
+                                               s.perm, s.xp, s.xa, st),
+                   "moe_layer prefill scatter launch");
+  if (rc != MFI_OK) return rc;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  mfi::PrefillLaunch L{};
+  L.E = E; L.H = H; L.Mi = Mi; L.top_k = k; L.grid = sms;
+  L.prepared = static_cast<const uint8_t*>(w->prepared);
+  L.counts = s.counts; L.perm = s.perm; L.rows = s.rows;
+  L.xp = s.xp; L.xa = s.xa; L.hp = s.hp; L.ha = s.ha;
+  L.topw = topw; L.out = out;
+  L.err = mfi::device_error_flag(); L.queue = s.queue; L.ready = s.ready;
+  L.pdl = true;
+  return cuda_status(mfi::launch_moe_prefill(L, st), "moe_layer prefill experts launch");
+}
+
+int layer_common_checks(const mfi_moe_weights* w, int T) {
+  if (!w) return fail(MFI_ERR_ARG, "null weights");
+  const int E = w->n_experts, H = w->hidden, Mi = w->inter, k = w->top_k;
+  if (E <= 0 || E > mfi::kRouteMaxE) return fail(MFI_ERR_ARG, "n_experts must be in [1, 256]");
+  if (H <= 0 || H % 32 != 0 || Mi <= 0 || Mi % 32 != 0 || H > 4096)
+    return fail(MFI_ERR_ARG, "hidden and inter must be positive multiples of 32, hidden <= 4096");
+  if (k <= 0 || k > E || k > 32) return fail(MFI_ERR_ARG, "top_k must be in [1, min(E, 32)]");
+  if (T < 0) return fail(MFI_ERR_ARG, "T must be >= 0");
+  return MFI_OK;
+}
+
+bool layer_ptrs_bad(const mfi_moe_weights* w, const void* x, const float* out, const int32_t* topi,
+                    const float* topw, const void* ws) {
+  return bad_ptr(x) || bad_ptr(out) || bad_ptr(topi) || bad_ptr(topw) || bad_ptr(ws) ||
+         bad_ptr(w->gate_wp) || bad_ptr(w->gate_sc) || bad_ptr(w->up_wp) || bad_ptr(w->up_sc) ||
+         bad_ptr(w->down_wp) || bad_ptr(w->down_sc) || bad_ptr(w->router_wp) ||
+         bad_ptr(w->router_sc);
+}
+}  // namespace
+
+size_t mfi_moe_layer_prefill_workspace_bytes(int T, int hidden, int inter, int n_experts,
+                                             int top_k) {
+  if (T <= 0 || hidden <= 0 || inter <= 0 || n_experts <= 0 || top_k <= 0) return 0;
+  return carve_prefill(nullptr, T, hidden, inter, n_experts, top_k).bytes;
+}
+
+int mfi_moe_layer_prefill(const mfi_moe_weights* w, const void* x_bf16, int T, float* out,
+                          int32_t* topi, float* topw, float* logits, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  int rc = layer_common_checks(w, T);
+  if (rc != MFI_OK) return rc;
+  if (T == 0) return MFI_OK;
+  if (layer_ptrs_bad(w, x_bf16, out, topi, topw, workspace)) return fail(MFI_ERR_ARG, "null pointer");
+  if ((reinterpret_cast<uintptr_t>(x_bf16) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(w->router_wp) & 15) != 0)
+    return fail(MFI_ERR_ARG, "x and router_wp must be 16-byte aligned");
+  return run_prefill(w, x_bf16, T, out, topi, topw, logits, workspace, workspace_bytes,
+                     as_stream(stream));
+}
+
 size_t mfi_moe_prepared_bytes(int n_experts, int hidden, int inter) {
   if (!layer_uses_tc(hidden, inter)) return 0;
   return mfi::moe_prepared_bytes(n_experts, hidden, inter);
@@ -384,6 +510,8 @@ int mfi_moe_prepare(const mfi_moe_weights* w, void* prepared, size_t prepared_by
 }
 
 size_t mfi_moe_layer_workspace_bytes(int T, int hidden, int inter, int n_experts, int top_k) {
+  if (use_prefill(T, hidden, inter, top_k))
+    return mfi_moe_layer_prefill_workspace_bytes(T, hidden, inter, n_experts, top_k);
   return carve_layer(nullptr, T, hidden, inter, n_experts, top_k).bytes;
 }
 
@@ -398,19 +526,33 @@ int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float*
                      int32_t* topi, float* topw, float* logits, void* workspace,
                      size_t workspace_bytes, void* const* events, int n_events, void* stream) {
   if (events && n_events < 6) return fail(MFI_ERR_ARG, "events must hold 6 cudaEvent_t handles");
-  if (!w) return fail(MFI_ERR_ARG, "null weights");
+  int rc0 = layer_common_checks(w, T);
+  if (rc0 != MFI_OK) return rc0;
   const int E = w->n_experts, H = w->hidden, Mi = w->inter, k = w->top_k;
-  if (E <= 0 || E > mfi::kRouteMaxE) return fail(MFI_ERR_ARG, "n_experts must be in [1, 256]");
-  if (H <= 0 || H % 32 != 0 || Mi <= 0 || Mi % 32 != 0 || H > 4096)
-    return fail(MFI_ERR_ARG, "hidden and inter must be positive multiples of 32, hidden <= 4096");
-  if (k <= 0 || k > E || k > 32) return fail(MFI_ERR_ARG, "top_k must be in [1, min(E, 32)]");
-  if (T < 0 || (long long)T * k > mfi::kRouteMaxPairs)
-    return fail(MFI_ERR_ARG, "T * top_k must be <= 4096");
+  const bool prefill = use_prefill(T, H, Mi, k);
+  if (!prefill && (long long)T * k > mfi::kRouteMaxPairs)
+    return fail(MFI_ERR_ARG, "T * top_k must be <= 4096 unless hidden and inter are multiples of 256");
   if (T == 0) return MFI_OK;
-  if (bad_ptr(x_bf16) || bad_ptr(out) || bad_ptr(topi) || bad_ptr(topw) || bad_ptr(workspace) ||
-      bad_ptr(w->gate_wp) || bad_ptr(w->gate_sc) || bad_ptr(w->up_wp) || bad_ptr(w->up_sc) ||
-      bad_ptr(w->down_wp) || bad_ptr(w->down_sc) || bad_ptr(w->router_wp) || bad_ptr(w->router_sc))
-    return fail(MFI_ERR_ARG, "null pointer");
+  if (layer_ptrs_bad(w, x_bf16, out, topi, topw, workspace)) return fail(MFI_ERR_ARG, "null pointer");
+  if (prefill) {
+    if ((reinterpret_cast<uintptr_t>(x_bf16) & 15) != 0 ||
+        (reinterpret_cast<uintptr_t>(w->router_wp) & 15) != 0)
+      return fail(MFI_ERR_ARG, "x and router_wp must be 16-byte aligned");
+    cudaStream_t stp = as_stream(stream);
+    auto rec = [&](int i) -> int {
+      if (!events) return MFI_OK;
+      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+      cudaStreamIsCapturing(stp, &cs);
+      const unsigned flags = cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : 0u;
+      return cuda_status(cudaEventRecordWithFlags(reinterpret_cast<cudaEvent_t>(events[i]), stp, flags),
+                         "moe_layer event record");
+    };
+    int rc = rec(0);
+    if (rc != MFI_OK) return rc;
+    rc = run_prefill(w, x_bf16, T, out, topi, topw, logits, workspace, workspace_bytes, stp);
+    for (int i = 1; rc == MFI_OK && i < 6; ++i) rc = rec(i);
+    return rc;
+  }
   if (workspace_bytes < mfi_moe_layer_workspace_bytes(T, H, Mi, E, k))
     return fail(MFI_ERR_WORKSPACE, "workspace too small for moe_layer");
   LayerScratch s = carve_layer(workspace, T, H, Mi, E, k);
@@ -451,6 +593,7 @@ int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float*
   ra.xp_atoms = tc ? s.xp_atoms : nullptr;
   ra.T_pad = s.T_pad;
   ra.err = mfi::device_error_flag();
+  ra.logit_bias = w->logit_bias;
   if (tc && w->prepared && (reinterpret_cast<uintptr_t>(w->prepared) & 15) == 0) {
     // the router issues the gate/up weight prefetch after its own loads
     ra.pf_base = static_cast<const uint8_t*>(w->prepared);
@@ -529,6 +672,7 @@ int mfi_moe_route(const mfi_moe_weights* w, const void* x_bf16, int T, uint8_t* 
   ra.T = T; ra.H = H; ra.E = E; ra.k = k;
   ra.logits = logits; ra.topi = topi; ra.topw = topw;
   ra.err = mfi::device_error_flag();
+  ra.logit_bias = w->logit_bias;
   // no work lists, no expert regions: the kernel stops after the routing
   return cuda_status(mfi::launch_route(ra, as_stream(stream)), "moe_route launch");
 }
@@ -815,6 +959,7 @@ int mfi_ep_route_dispatch(const mfi_moe_weights* w, const void* x_bf16, int T, i
   ra.T = T; ra.H = H; ra.E = E; ra.k = k;
   ra.topi = topi; ra.topw = topw;
   ra.err = mfi::device_error_flag();
+  ra.logit_bias = w->logit_bias;
   ra.ep.table = static_cast<const mfi::EpTable*>(table);
   ra.ep.flags = fl;
   ra.ep.pack_pos = pack_pos;

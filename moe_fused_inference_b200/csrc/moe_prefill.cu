@@ -1,0 +1,514 @@
+// moe_prefill.cu — prefill-sized grouped expert GEMMs on the tcgen05 tensor
+// cores (many tokens per expert).
+//
+// Replaces the reference's prefill MoE (runtime/model_runner_v2.py:108-122:
+// per expert, gather its tokens on the host and call mxfp4_linear three
+// times) with one routed pass and no host synchronisation:
+//
+//   route_cluster_kernel   quantise, route, count tokens per expert and give
+//                          each (token, slot) its position among its expert's
+//                          tokens (atomic cursor); clear the output rows
+//   prefill_scatter_kernel place each token's quantised row (and its scale
+//                          atoms) at expert base + position, where the bases
+//                          are the prefix sum of the per-expert counts rounded
+//                          up to 128-row tiles (computed in every CTA)
+//   moe_prefill_kernel     one persistent launch: gate/up items
+//                          (128-token tile, 64 gate + 64 up weight rows) with
+//                          SwiGLU + requantisation of h in the epilogue, then
+//                          down items (128-token tile, 128 output rows) whose
+//                          epilogue scales by the routing weight and adds into
+//                          the output with vector reductions
+//
+//   D (128 tokens x 128 weight rows) += X_tile (128 x 256 K) . W_tile^T,
+//   tcgen05.mma.cta_group::1.kind::mxf4.block_scale, M = N = 128, K = 64.
+//
+// The weight operand is the decode path's prepared block (pre-swizzled rows +
+// scale atoms, one bulk copy per stage); the token operand comes by TMA from
+// the compact rows.  The down items of a tile wait (bounded) for the 12
+// gate/up items of the same tile, as in moe_tc.cu.  The output sum over a
+// token's k slots is an fp32 reduction in arrival order, so prefill outputs
+// are checked against a tolerance, not bit for bit.
+#include "mx_common.cuh"
+#include "tc_ptx.cuh"
+#include "tmap.cuh"
+#include "work.cuh"
+
+namespace mfi {
+
+using namespace tc;
+
+namespace {
+
+#ifndef MFI_PF_STAGES
+#define MFI_PF_STAGES 5
+#endif
+constexpr int kPStages = MFI_PF_STAGES;
+constexpr int kPThreads = 192;
+constexpr int kPTile = 128;                    // token rows per tile (MMA M)
+constexpr int kPA = 16384;                     // 128 token rows x 128 B
+constexpr int kPSF = 1024;                     // two scale atoms
+constexpr int kPW = 16384 + 1024;              // prepared weight block (tile + atoms)
+constexpr int kPOffSFA = kPA;
+constexpr int kPOffW = kPA + kPSF;             // 1024-byte aligned
+constexpr int kPOffSFB = kPOffW + 16384;
+constexpr int kPStageBytes = kPA + kPSF + kPW; // 34816
+constexpr int kPAccBufs = 3;                   // 128 fp32 columns each
+constexpr uint32_t kPTmemCols = 512;
+constexpr uint32_t kPTmemSFA = kPAccBufs * 128;
+constexpr uint32_t kPTmemSFB = kPTmemSFA + 8;
+constexpr int kPMaxExperts = 256;
+constexpr int kPMaxChunks = kPMaxExperts + kPrefillMaxPairs / kPTile;
+
+struct PrefillArgs {
+  const int* counts;           // tokens per expert (router cursors)
+  int E;
+  const int* perm;             // row -> pair (token * k + slot)
+  const uint8_t* w_gu;         // prepared gate/up blocks [expert][Mi/64][H/256][block]
+  const uint8_t* w_dn;         // prepared down blocks [expert][H/128][Mi/256][block]
+  const uint8_t* xa;           // token-row scale atoms [row/128][H/128][512]
+  uint8_t* hp;                 // requantised h rows (rows, inter/2)
+  uint8_t* ha;                 // their scale atoms [row/128][inter/128][512]
+  const float* topw;           // (pairs) routing weights
+  float* out;                  // (T, hidden) fp32, cleared by the router
+  int hidden, inter, top_k;
+  int* err;
+  int* queue;                  // work-item counter, zero before the launch
+  unsigned* ready;             // per tile: finished gate/up items, zero before the launch
+};
+
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+
+// Rows of expert e start at base[e] = sum over e' < e of counts rounded up to
+// 128.  Warp 0 of the calling CTA fills s_base[0..E) and returns the total.
+__device__ int expert_bases(const int* s_cnt, int E, int* s_base) {
+  const int lane = threadIdx.x & 31;
+  int run = 0;
+  for (int e0 = 0; e0 < E; e0 += 32) {
+    const int e = e0 + lane;
+    const int v = e < E ? (s_cnt[e] + kPTile - 1) / kPTile * kPTile : 0;
+    int inc = v;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, inc, off);
+      if (lane >= off) inc += u;
+    }
+    if (e < E) s_base[e] = run + inc - v;
+    run += __shfl_sync(0xffffffffu, inc, 31);
+  }
+  return run;
+}
+
+// One CTA per token: copy its quantised row and scale atoms to each of its
+// k expert rows.
+__global__ void __launch_bounds__(128) prefill_scatter_kernel(
+    const uint8_t* __restrict__ xq, const uint8_t* __restrict__ xsc, const int* __restrict__ topi,
+    const int* __restrict__ slot_pos, const int* __restrict__ counts, int E, int k, int H,
+    int* __restrict__ perm, uint8_t* __restrict__ xp, uint8_t* __restrict__ xa) {
+  const int t = blockIdx.x;
+  __shared__ int s_cnt[kPMaxExperts];
+  __shared__ int s_base[kPMaxExperts];
+  __shared__ int s_row[32];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = counts[e];
+  __syncthreads();
+  if (threadIdx.x < 32) expert_bases(s_cnt, E, s_base);
+  __syncthreads();
+  if (threadIdx.x < k) {
+    const int j = threadIdx.x;
+    const int row = s_base[topi[size_t(t) * k + j]] + slot_pos[size_t(t) * k + j];
+    s_row[j] = row;
+    perm[row] = t * k + j;
+  }
+  __syncthreads();
+  const int q16 = H / 32, kc = H / 128;
+  for (int i = threadIdx.x; i < k * q16; i += blockDim.x) {
+    const int j = i / q16, c = i % q16;
+    reinterpret_cast<uint4*>(xp + size_t(s_row[j]) * (H / 2))[c] =
+        reinterpret_cast<const uint4*>(xq + size_t(t) * (H / 2))[c];
+  }
+  for (int i = threadIdx.x; i < k * kc; i += blockDim.x) {
+    const int j = i / kc, c = i % kc;
+    const int row = s_row[j];
+    *reinterpret_cast<uint32_t*>(xa + (size_t(row / kPTile) * kc + c) * 512 + (row % 32) * 16 +
+                                 ((row % kPTile) / 32) * 4) =
+        reinterpret_cast<const uint32_t*>(xsc + size_t(t) * (H / 32))[c];
+  }
+}
+
+__global__ void __launch_bounds__(kPThreads, 1)
+    moe_prefill_kernel(const __grid_constant__ CUtensorMap tma_x,
+                       const __grid_constant__ CUtensorMap tma_h, PrefillArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kPStages * kPStageBytes);
+  uint64_t* empty = full + kPStages;
+  uint64_t* acc_full = empty + kPStages;
+  uint64_t* acc_empty = acc_full + kPAccBufs;
+  uint64_t* item_full = acc_empty + kPAccBufs;
+  uint64_t* item_empty = item_full + kPAccBufs;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_empty + kPAccBufs);
+  __shared__ int s_item[kPAccBufs];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles_gu = p.inter / 64, tiles_dn = p.hidden / 128;
+  const int ks_gu = p.hidden / 256, ks_dn = p.inter / 256;
+  const int kc_gu = p.hidden / 128, kc_dn = p.inter / 128;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < kPAccBufs; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+      mbar_init(&item_full[b], 1);
+      mbar_init(&item_empty[b], 5);  // the MMA thread + the 4 epilogue warps
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tma_x);
+    prefetch_tmap(&tma_h);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kPTmemCols);
+  int first_item = 0;
+  if (warp == 0 && lane == 0) first_item = atomicAdd(p.queue, 1);
+  grid_dep_wait();
+  grid_dep_launch();
+
+  // tile table: tile -> (expert, m) with rows [base[e] + 128 m, + count)
+  __shared__ int s_cnt[kPMaxExperts];
+  __shared__ int s_base[kPMaxExperts];
+  __shared__ int s_tile[kPMaxChunks];
+  __shared__ int s_ntiles;
+  for (int e = threadIdx.x; e < p.E; e += blockDim.x) s_cnt[e] = p.counts[e];
+  __syncthreads();
+  if (warp == 0) {
+    expert_bases(s_cnt, p.E, s_base);
+    int run = 0;
+    for (int e0 = 0; e0 < p.E; e0 += 32) {
+      const int e = e0 + lane;
+      const int nt = e < p.E ? (s_cnt[e] + kPTile - 1) / kPTile : 0;
+      int inc = nt;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, inc, off);
+        if (lane >= off) inc += v;
+      }
+      for (int m = 0; m < nt; ++m)
+        if (run + inc - nt + m < kPMaxChunks) s_tile[run + inc - nt + m] = e | (m << 16);
+      run += __shfl_sync(0xffffffffu, inc, 31);
+    }
+    if (lane == 0) s_ntiles = min(run, kPMaxChunks);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int n_gu = s_ntiles * tiles_gu;
+  const int n_items = n_gu + s_ntiles * tiles_dn;
+  auto tile_of = [&](int tl, int& expert, int& row0, int& count) {
+    const int v = s_tile[tl];
+    expert = v & 0xffff;
+    const int m = v >> 16;
+    row0 = s_base[expert] + kPTile * m;
+    count = min(kPTile, s_cnt[expert] - kPTile * m);
+  };
+  auto decode = [&](int item, bool& gu, int& tl, int& tile) {
+    gu = item < n_gu;
+    const int i = gu ? item : item - n_gu;
+    const int tiles = gu ? tiles_gu : tiles_dn;
+    tl = i / tiles;
+    tile = i % tiles;
+  };
+
+  if (warp == 0) {
+    first_item = __shfl_sync(0xffffffffu, first_item, 0);
+    if (elect_one()) {
+      uint32_t it = 0;
+      bool ok = true;
+      int item = first_item;
+      for (uint32_t qi = 0; ok; ++qi) {
+        const uint32_t slot = qi % kPAccBufs;
+        if (!mbar_wait(&item_empty[slot], ((qi / kPAccBufs) & 1) ^ 1, p.err, 1)) break;
+        if (item >= n_items) item = -1;
+        s_item[slot] = item;
+        mbar_arrive(&item_full[slot]);
+        if (item < 0) break;
+        const int next = atomicAdd(p.queue, 1);
+        bool gu;
+        int tl, tile, e, row0, count;
+        decode(item, gu, tl, tile);
+        tile_of(tl, e, row0, count);
+        const uint8_t* wb;
+        if (gu) {
+          wb = p.w_gu + (size_t(e) * tiles_gu + tile) * ks_gu * size_t(kPW);
+        } else {
+          wb = p.w_dn + (size_t(e) * tiles_dn + tile) * ks_dn * size_t(kPW);
+          if (ld_acquire_u32(p.ready + tl) < unsigned(tiles_gu)) {
+            const uint64_t t0 = globaltimer_ns();
+            for (uint32_t i = 1;; ++i) {
+              __nanosleep(64);
+              if (ld_acquire_u32(p.ready + tl) >= unsigned(tiles_gu)) break;
+              if ((i & 255u) == 0 && (*reinterpret_cast<volatile int*>(p.err) != 0 ||
+                                      globaltimer_ns() - t0 > kWaitLimitNs)) {
+                atomicCAS(p.err, 0, 4);
+                ok = false;
+                break;
+              }
+            }
+            if (!ok) break;
+          }
+          fence_proxy_async_global();
+        }
+        const int ksn = gu ? ks_gu : ks_dn;
+        const int kc = gu ? kc_gu : kc_dn;
+        const uint8_t* sfa = gu ? p.xa : p.ha;
+        const CUtensorMap* ta = gu ? &tma_x : &tma_h;
+        for (int ks = 0; ks < ksn; ++ks, ++it) {
+          const int s = it % kPStages;
+          if (!mbar_wait(&empty[s], ((it / kPStages) & 1) ^ 1, p.err, 1)) { ok = false; break; }
+          uint8_t* st = ring + s * kPStageBytes;
+          mbar_expect_tx(&full[s], kPStageBytes);
+          tma_load_2d(st, ta, ks * 128, row0, &full[s]);
+          bulk_load(st + kPOffSFA, sfa + (size_t(row0 / kPTile) * kc + 2 * ks) * 512, kPSF, &full[s]);
+          bulk_load(st + kPOffW, wb + size_t(ks) * kPW, kPW, &full[s]);
+        }
+        item = next;
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (uint32_t acc_it = 0; ok; ++acc_it) {
+        const uint32_t buf = acc_it % kPAccBufs;
+        if (!mbar_wait(&item_full[buf], (acc_it / kPAccBufs) & 1, p.err, 2)) break;
+        const int item = s_item[buf];
+        mbar_arrive(&item_empty[buf]);
+        if (!mbar_wait(&acc_empty[buf], ((acc_it / kPAccBufs) & 1) ^ 1, p.err, 2)) { ok = false; break; }
+        if (item < 0) {
+          mbar_arrive(&acc_full[buf]);
+          break;
+        }
+        const int ksn = item < n_gu ? ks_gu : ks_dn;
+        tc_fence_after();
+        const uint32_t d = tmem + buf * 128;
+        for (int ks = 0; ks < ksn; ++ks, ++it) {
+          const int s = it % kPStages;
+          if (!mbar_wait(&full[s], (it / kPStages) & 1, p.err, 2)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t base = smem_u32(ring + s * kPStageBytes);
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            tmem_cp_sf(tmem + kPTmemSFA + 4 * c, make_sdesc(base + kPOffSFA + c * 512, 0, 128, kLayoutNone));
+            tmem_cp_sf(tmem + kPTmemSFB + 4 * c, make_sdesc(base + kPOffSFB + c * 512, 0, 128, kLayoutNone));
+          }
+#pragma unroll
+          for (int kb = 0; kb < 4; ++kb) {
+            const int c = kb >> 1;
+            const uint32_t byte = uint32_t(kb & 1) * 2;
+            mma_mxf4(d, make_sdesc(base + kb * 32, 16, 1024, kLayoutSW128),
+                     make_sdesc(base + kPOffW + kb * 32, 16, 1024, kLayoutSW128),
+                     make_idesc_mxf4(128, 128, int(byte), int(byte)), (ks | kb) != 0 ? 1u : 0u,
+                     (tmem + kPTmemSFA + 4 * c) | (byte << 30), (tmem + kPTmemSFB + 4 * c) | (byte << 30));
+          }
+          tc_commit(&empty[s]);
+        }
+        if (ok) tc_commit(&acc_full[buf]);
+      }
+    }
+  } else {
+    const int quad = warp & 3;          // TMEM lane quadrant of this warp
+    const int et = threadIdx.x - 64;    // 0..127
+    const int r = quad * 32 + lane;     // token row inside the tile
+    for (uint32_t acc_it = 0;; ++acc_it) {
+      const uint32_t buf = acc_it % kPAccBufs;
+      if (!mbar_wait(&item_full[buf], (acc_it / kPAccBufs) & 1, p.err, 3)) break;
+      const int item = s_item[buf];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[buf]);
+      if (item < 0) {
+        mbar_wait(&acc_full[buf], (acc_it / kPAccBufs) & 1, p.err, 3);
+        break;
+      }
+      bool gu;
+      int tl, tile, e, row0, count;
+      decode(item, gu, tl, tile);
+      tile_of(tl, e, row0, count);
+      const bool valid = r < count;
+      const int row = row0 + r;
+      int pair = 0;
+      float wgt = 0.0f;
+      if (!gu && valid) {
+        pair = p.perm[row];
+        wgt = p.topw[pair];
+      }
+      if (!mbar_wait(&acc_full[buf], (acc_it / kPAccBufs) & 1, p.err, 3)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem + (uint32_t(quad * 32) << 16) + buf * 128;
+      if (gu) {
+        // columns 0-63: gate outputs tile*64 + c, 64-127: the same up outputs
+        uint8_t* hrow = p.hp + size_t(row) * (p.inter / 2) + tile * 32;
+#pragma unroll 1
+        for (int hb = 0; hb < 2; ++hb) {
+          uint32_t g[32], u[32];
+          tmem_ld_32x32b_x32(tbase + hb * 32, g);
+          tmem_ld_32x32b_x32(tbase + 64 + hb * 32, u);
+          tmem_ld_wait();
+          if (hb == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+          }
+          float h[32];
+          float am = 0.0f;
+          bool nan = false;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float gv = __uint_as_float(g[i]), uv = __uint_as_float(u[i]);
+            h[i] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
+            am = fmaxf(am, fabsf(h[i]));
+            nan |= (h[i] != h[i]);
+          }
+          const BlockScale bs = block_scale(nan ? __uint_as_float(0x7fc00000u) : am);
+          uint32_t w4[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t wd = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) wd |= quant_nibble(h[q * 8 + i], bs.inv) << (4 * i);
+            w4[q] = wd;
+          }
+          if (valid) {
+            *reinterpret_cast<uint4*>(hrow + hb * 16) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+            const int kb = tile * 2 + hb;  // 32-element block of h along inter
+            p.ha[(size_t(row / kPTile) * kc_dn + kb / 4) * 512 + (row % 32) * 16 +
+                 ((row % kPTile) / 32) * 4 + (kb & 3)] = bs.code;
+          }
+        }
+        // publish this 64-column slice of the tile's h rows to its down items
+        named_bar_sync(1, 128);
+        if (et == 0) {
+          fence_proxy_async_global();
+          __threadfence();
+          atomicAdd(p.ready + tl, 1u);
+        }
+      } else {
+        const int t = pair / p.top_k;
+        float* orow = p.out + size_t(t) * p.hidden + tile * 128;
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t y[32];
+          tmem_ld_32x32b_x32(tbase + cc * 32, y);
+          tmem_ld_wait();
+          if (cc == 3) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+          }
+          if (valid) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              red_add_v4(orow + cc * 32 + i, __fmul_rn(wgt, __uint_as_float(y[i])),
+                         __fmul_rn(wgt, __uint_as_float(y[i + 1])),
+                         __fmul_rn(wgt, __uint_as_float(y[i + 2])),
+                         __fmul_rn(wgt, __uint_as_float(y[i + 3])));
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kPTmemCols);
+  }
+}
+
+size_t prefill_smem() {
+  return 1024 + size_t(kPStages) * kPStageBytes + 8 * (2 * kPStages + 4 * kPAccBufs) + 16;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+size_t prefill_rows(int pairs, int E) {
+  // every expert's rows rounded up to a whole tile
+  const size_t active = size_t(pairs < E ? pairs : E);
+  return (size_t(pairs) + kPTile - 1) / kPTile * kPTile + active * kPTile;
+}
+
+cudaError_t launch_prefill_scatter(const uint8_t* xq, const uint8_t* xsc, const int* topi,
+                                   const int* slot_pos, const int* counts, int T, int E, int k,
+                                   int H, int* perm, uint8_t* xp, uint8_t* xa,
+                                   cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  prefill_scatter_kernel<<<T, 128, 0, stream>>>(xq, xsc, topi, slot_pos, counts, E, k, H, perm,
+                                                xp, xa);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_moe_prefill(const PrefillLaunch& L, cudaStream_t stream) {
+  if (L.queue == nullptr || L.ready == nullptr) return cudaErrorInvalidValue;
+  static bool smem_set = false;
+  if (!smem_set) {
+    cudaError_t e = cudaFuncSetAttribute(moe_prefill_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(prefill_smem()));
+    if (e != cudaSuccess) return e;
+    smem_set = true;
+  }
+  const int E = L.E, H = L.H, Mi = L.Mi;
+  CUtensorMap tx, th;
+  if (!get_tmap(&tx, L.xp, H / 2, uint64_t(L.rows), kPTile) ||
+      !get_tmap(&th, L.hp, Mi / 2, uint64_t(L.rows), kPTile))
+    return cudaErrorInvalidValue;
+  PrefillArgs p{};
+  p.counts = L.counts;
+  p.E = E;
+  p.perm = L.perm;
+  p.w_gu = L.prepared;
+  p.w_dn = L.prepared + size_t(E) * (Mi / 64) * (H / 256) * kPW;
+  p.xa = L.xa;
+  p.hp = L.hp;
+  p.ha = L.ha;
+  p.topw = L.topw;
+  p.out = L.out;
+  p.hidden = H;
+  p.inter = Mi;
+  p.top_k = L.top_k;
+  p.err = L.err;
+  p.queue = L.queue;
+  p.ready = L.ready;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(L.grid);
+  cfg.blockDim = dim3(kPThreads);
+  cfg.dynamicSmemBytes = prefill_smem();
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = L.pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, moe_prefill_kernel, tx, th, p);
+}
+
+}  // namespace mfi

@@ -151,6 +151,11 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
     }
   }
   __syncthreads();
+  if (a.logit_bias) {
+    for (int e = threadIdx.x; e < a.E; e += blockDim.x)
+      s_logit[e] = __fadd_rn(s_logit[e], a.logit_bias[e]);
+    __syncthreads();
+  }
   if (a.logits)
     for (int e = threadIdx.x; e < a.E; e += blockDim.x) a.logits[long(t) * a.E + e] = s_logit[e];
 
@@ -533,8 +538,16 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
   cluster_wait_acquire();
   if (crank != 0) return;
 
+  if (a.logit_bias) {
+    for (int e = threadIdx.x; e < a.E; e += kClusterThreads)
+      s_logit[e] = __fadd_rn(s_logit[e], a.logit_bias[e]);
+    __syncthreads();
+  }
   if (a.logits)
     for (int e = threadIdx.x; e < a.E; e += kClusterThreads) a.logits[long(t) * a.E + e] = s_logit[e];
+  if (a.out_zero)
+    for (int i = threadIdx.x; i < (a.H >> 2); i += kClusterThreads)
+      reinterpret_cast<float4*>(a.out_zero + long(t) * a.H)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
 
   // ---- top-k, weights, expert-row claims (leader) ----------------------------
   __shared__ int s_sel[32];
@@ -561,6 +574,7 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
       a.topi[long(t) * a.k + lane] = s_sel[lane];
       a.topw[long(t) * a.k + lane] = wgt;
       s_tw[lane] = wgt;
+      if (a.slot_pos) a.slot_pos[long(t) * a.k + lane] = atomicAdd(a.cursor + s_sel[lane], 1);
       if (a.xp) {
         const int e = s_sel[lane];
         const int pos = atomicAdd(a.cursor + e, 1);

@@ -99,6 +99,11 @@ struct RouteArgs {
   const uint8_t* pf_base;
   unsigned long long pf_bytes;
   EpDispatch ep;       // ep.table == null: no expert-parallel dispatch
+  const float* logit_bias;  // [E] added to the logits before top-k, or null
+  // prefill placement: slot_pos[t*k + j] = the pair's position among the
+  // tokens of its expert (cursor claim, no row copy); out rows zeroed here
+  int* slot_pos;
+  float* out_zero;     // (T, H) fp32 rows to clear, or null
 };
 
 constexpr int kRouteMaxE = 256;
@@ -173,6 +178,28 @@ cudaError_t launch_scatter_sel(const uint8_t* xq, long long xq_ld, const uint8_t
 cudaError_t launch_combine_sel(const float* yd, const int* sel, long long sel_ld, const float* w,
                                long long w_ld, int R, int k, int E, int H, float* out,
                                long long out_ld, cudaStream_t stream);
+
+// Prefill-sized expert GEMMs (moe_prefill.cu).
+constexpr int kPrefillMaxPairs = 262144;   // T * top_k per call
+struct PrefillLaunch {
+  int E, H, Mi, top_k, grid;
+  const uint8_t* prepared;       // weight blocks from launch_moe_prepare
+  const int* counts;             // tokens per expert
+  const int* perm;               // row -> pair
+  int rows;                      // rows of xp / hp (prefill_rows)
+  const uint8_t* xp; const uint8_t* xa;   // token rows and their 128-row scale atoms
+  uint8_t* hp; uint8_t* ha;               // requantised h rows and atoms
+  const float* topw;             // (pairs)
+  float* out;                    // (T, H), zero before the launch
+  int* err; int* queue; unsigned* ready;
+  bool pdl;
+};
+size_t prefill_rows(int pairs, int E);
+cudaError_t launch_prefill_scatter(const uint8_t* xq, const uint8_t* xsc, const int* topi,
+                                   const int* slot_pos, const int* counts, int T, int E, int k,
+                                   int H, int* perm, uint8_t* xp, uint8_t* xa,
+                                   cudaStream_t stream);
+cudaError_t launch_moe_prefill(const PrefillLaunch& L, cudaStream_t stream);
 
 // Peer-memory exchange (ep.cu).
 cudaError_t launch_ep_scatter_wait(const EpTable* table, unsigned* flags, uint8_t* recv, int rank,

@@ -135,7 +135,9 @@ def random_layer_weights(n_experts=128, hidden=2048, inter=768, std=0.02, seed=0
 class MoELayer:
     """One device-routed MoE layer call per forward (library entry mfi_moe_layer)."""
 
-    def __init__(self, weights: MoELayerWeights, top_k: int = 8):
+    def __init__(self, weights: MoELayerWeights, top_k: int = 8, logit_bias=None):
+        """``logit_bias``: optional cuda float32 (E,) added to the router logits
+        before top-k (a synthetic load skew; the reference has no such term)."""
         weights.validate()
         if not 1 <= top_k <= min(weights.n_experts, 32):
             raise RuntimeError("top_k must be in [1, min(E, 32)]")
@@ -147,7 +149,14 @@ class MoELayer:
             weights.up_wp.data_ptr(), weights.up_sc.data_ptr(),
             weights.down_wp.data_ptr(), weights.down_sc.data_ptr(),
             weights.router_wp.data_ptr(), weights.router_sc.data_ptr(),
-            weights.n_experts, weights.hidden, weights.inter, top_k, None)
+            weights.n_experts, weights.hidden, weights.inter, top_k, None, None)
+        self.logit_bias = None
+        if logit_bias is not None:
+            lb = logit_bias.to(device=weights.gate_wp.device, dtype=torch.float32).contiguous()
+            if lb.shape != (weights.n_experts,):
+                raise RuntimeError("logit_bias must have shape (E,)")
+            self.logit_bias = lb
+            self._cw.logit_bias = lb.data_ptr()
         # tensor-core scale atoms, built once per weight set (mfi_moe_prepare)
         nprep = int(lib.mfi_moe_prepared_bytes(weights.n_experts, weights.hidden, weights.inter))
         self.prepared = None
@@ -169,6 +178,33 @@ class MoELayer:
             ws = torch.empty(self.workspace_bytes(T), dtype=torch.uint8, device=device)
             self._ws[T] = ws
         return ws
+
+    def prefill(self, x: torch.Tensor, out=None, topi=None, topw=None, logits=None):
+        """The prefill path (mfi_moe_layer_prefill) for any T: compact
+        count-based expert placement and 128-token tensor-core tiles.  forward()
+        takes it by itself when T * top_k > 4096."""
+        lib = _lib.load()
+        if not x.is_cuda or x.dtype != torch.bfloat16:
+            raise RuntimeError("x must be a cuda bfloat16 tensor")
+        x = x.contiguous()
+        T, H = x.shape
+        dev = x.device
+        k = self.top_k
+        out = torch.empty((T, H), dtype=torch.float32, device=dev) if out is None else out
+        topi = torch.empty((T, k), dtype=torch.int32, device=dev) if topi is None else topi
+        topw = torch.empty((T, k), dtype=torch.float32, device=dev) if topw is None else topw
+        nbytes = int(lib.mfi_moe_layer_prefill_workspace_bytes(T, self.w.hidden, self.w.inter,
+                                                                self.w.n_experts, k))
+        ws = self._ws.get(("prefill", T))
+        if ws is None:
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+            self._ws[("prefill", T)] = ws
+        st = lib.mfi_moe_layer_prefill(ctypes.byref(self._cw), x.data_ptr(), T, out.data_ptr(),
+                                       topi.data_ptr(), topw.data_ptr(),
+                                       0 if logits is None else logits.data_ptr(),
+                                       ws.data_ptr(), ws.numel(), _stream(dev))
+        _lib.check(st, "moe_layer_prefill")
+        return out, topi, topw
 
     def forward(self, x: torch.Tensor, out=None, topi=None, topw=None, logits=None, events=None):
         """x bf16 (T, hidden) -> (out fp32 (T, hidden), topi int32 (T, k), topw fp32 (T, k)).
