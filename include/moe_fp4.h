@@ -189,8 +189,8 @@ int mfi_moe_prepare(const mfi_moe_weights* w, void* prepared, size_t prepared_by
  * (with logit_bias set they hold the biased logits top-k ranked).
  * Decode sizes (T * top_k <= 4096) run the decode kernels; larger T, up to
  * T * top_k <= 262144, runs the prefill path of mfi_moe_layer_prefill
- * (needs hidden and inter multiples of 256).  The decode combine is
- * bit-reproducible; the prefill one sums a token's slots in arrival order. */
+ * (needs hidden and inter multiples of 256).  Both combine a token's slots
+ * in slot order with unfused fp32 multiply and add. */
 size_t mfi_moe_layer_workspace_bytes(int T, int hidden, int inter, int n_experts, int top_k);
 int mfi_moe_layer(const mfi_moe_weights* w, const void* x_bf16, int T, float* out, int32_t* topi,
                   float* topw, float* logits, void* workspace, size_t workspace_bytes,
@@ -210,9 +210,9 @@ int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float*
 
 /* Prefill path for any T >= 1 (T * top_k <= 262144): router with count-based
  * compact placement (per-expert rows rounded up to 128-token tiles), then one
- * persistent tcgen05 launch of 128-token x 128-row tiles: gate/up with the
- * SwiGLU requantisation in the epilogue, down scaled by the routing weight
- * and added into out (fp32 vector reductions).  Needs `prepared`. */
+ * persistent tcgen05 launch of 128-token x 128-row tiles — gate/up with the
+ * SwiGLU requantisation in the epilogue, down storing per-(token, slot) rows
+ * — and the top-k combine.  Needs `prepared`. */
 size_t mfi_moe_layer_prefill_workspace_bytes(int T, int hidden, int inter, int n_experts,
                                              int top_k);
 int mfi_moe_layer_prefill(const mfi_moe_weights* w, const void* x_bf16, int T, float* out,

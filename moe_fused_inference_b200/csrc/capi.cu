@@ -374,6 +374,7 @@ struct PrefillScratch {
   uint8_t* xq; uint8_t* xsc;
   int* perm;
   uint8_t* xp; uint8_t* xa; uint8_t* hp; uint8_t* ha;
+  float* yd;            // (T*k, H) per-(token, slot) down rows
   int rows;
   size_t bytes;
 };
@@ -396,6 +397,7 @@ PrefillScratch carve_prefill(void* ws, int T, int H, int Mi, int E, int k) {
   s.xa = c.take<uint8_t>(size_t(s.rows) / 128 * (H / 128) * 512);
   s.hp = c.take<uint8_t>(size_t(s.rows) * (Mi / 2));
   s.ha = c.take<uint8_t>(size_t(s.rows) / 128 * (Mi / 128) * 512);
+  s.yd = c.take<float>(size_t(P) * H);
   s.bytes = c.used + 256;
   return s;
 }
@@ -415,7 +417,6 @@ int run_prefill(const mfi_moe_weights* w, const void* x_bf16, int T, float* out,
     return fail(MFI_ERR_ARG, "the prefill path needs hidden and inter to be multiples of 256");
   if ((long long)T * k > mfi::kPrefillMaxPairs) return fail(MFI_ERR_ARG, "T * top_k must be <= 262144");
   if (bad_ptr(w->prepared)) return fail(MFI_ERR_ARG, "weights.prepared is null (mfi_moe_prepare)");
-  if ((reinterpret_cast<uintptr_t>(out) & 15) != 0) return fail(MFI_ERR_ARG, "out must be 16-byte aligned");
   PrefillScratch s = carve_prefill(workspace, T, H, Mi, E, k);
   if (workspace_bytes < s.bytes) return fail(MFI_ERR_WORKSPACE, "workspace too small for the prefill layer");
   int rc = cuda_status(cudaMemsetAsync(s.counts, 0, sizeof(int) * s.zero_words, st),
@@ -425,7 +426,8 @@ int run_prefill(const mfi_moe_weights* w, const void* x_bf16, int T, float* out,
   ra.x = x_bf16; ra.xq = s.xq; ra.xsc = s.xsc; ra.wr = w->router_wp; ra.sr = w->router_sc;
   ra.T = T; ra.H = H; ra.E = E; ra.k = k;
   ra.logits = logits; ra.topi = topi; ra.topw = topw;
-  ra.cursor = s.counts; ra.slot_pos = s.slot_pos; ra.out_zero = out;
+  ra.cursor = s.counts; ra.slot_pos = s.slot_pos;
+  ra.batch = T >= 512;  // enough tokens to fill the GPU one per warp
   ra.logit_bias = w->logit_bias;
   ra.err = mfi::device_error_flag();
   rc = cuda_status(mfi::launch_route(ra, st), "moe_layer prefill route launch");
@@ -442,10 +444,14 @@ int run_prefill(const mfi_moe_weights* w, const void* x_bf16, int T, float* out,
   L.prepared = static_cast<const uint8_t*>(w->prepared);
   L.counts = s.counts; L.perm = s.perm; L.rows = s.rows;
   L.xp = s.xp; L.xa = s.xa; L.hp = s.hp; L.ha = s.ha;
-  L.topw = topw; L.out = out;
+  L.yd = s.yd;
   L.err = mfi::device_error_flag(); L.queue = s.queue; L.ready = s.ready;
   L.pdl = true;
-  return cuda_status(mfi::launch_moe_prefill(L, st), "moe_layer prefill experts launch");
+  rc = cuda_status(mfi::launch_moe_prefill(L, st), "moe_layer prefill experts launch");
+  if (rc != MFI_OK) return rc;
+  // k <= 32 slots per token here; the decode combine's arithmetic
+  return cuda_status(mfi::launch_combine(s.yd, H, topw, k, k, out, T, H, st, true),
+                     "moe_layer prefill combine launch");
 }
 
 int layer_common_checks(const mfi_moe_weights* w, int T) {

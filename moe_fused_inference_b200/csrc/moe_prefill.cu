@@ -7,7 +7,7 @@
 //
 //   route_cluster_kernel   quantise, route, count tokens per expert and give
 //                          each (token, slot) its position among its expert's
-//                          tokens (atomic cursor); clear the output rows
+//                          tokens (atomic cursor)
 //   prefill_scatter_kernel place each token's quantised row (and its scale
 //                          atoms) at expert base + position, where the bases
 //                          are the prefix sum of the per-expert counts rounded
@@ -16,8 +16,9 @@
 //                          (128-token tile, 64 gate + 64 up weight rows) with
 //                          SwiGLU + requantisation of h in the epilogue, then
 //                          down items (128-token tile, 128 output rows) whose
-//                          epilogue scales by the routing weight and adds into
-//                          the output with vector reductions
+//                          epilogue stores each (token, slot) row of y
+//   combine_kernel         the decode path's top-k combine (slot order, unfused
+//                          fp32 multiply and add)
 //
 //   D (128 tokens x 128 weight rows) += X_tile (128 x 256 K) . W_tile^T,
 //   tcgen05.mma.cta_group::1.kind::mxf4.block_scale, M = N = 128, K = 64.
@@ -25,9 +26,7 @@
 // The weight operand is the decode path's prepared block (pre-swizzled rows +
 // scale atoms, one bulk copy per stage); the token operand comes by TMA from
 // the compact rows.  The down items of a tile wait (bounded) for the 12
-// gate/up items of the same tile, as in moe_tc.cu.  The output sum over a
-// token's k slots is an fp32 reduction in arrival order, so prefill outputs
-// are checked against a tolerance, not bit for bit.
+// gate/up items of the same tile, as in moe_tc.cu.
 #include "mx_common.cuh"
 #include "tc_ptx.cuh"
 #include "tmap.cuh"
@@ -43,7 +42,11 @@ namespace {
 #define MFI_PF_STAGES 5
 #endif
 constexpr int kPStages = MFI_PF_STAGES;
-constexpr int kPThreads = 192;
+// warp 0 loads, warp 1 issues MMAs, warps 2-9 run the epilogue: two warps
+// per TMEM lane quadrant, each taking half of the tile's columns (the SwiGLU
+// epilogue is latency-bound with one warp per scheduler)
+constexpr int kPEpiWarps = 8;
+constexpr int kPThreads = 64 + 32 * kPEpiWarps;
 constexpr int kPTile = 128;                    // token rows per tile (MMA M)
 constexpr int kPA = 16384;                     // 128 token rows x 128 B
 constexpr int kPSF = 1024;                     // two scale atoms
@@ -54,8 +57,9 @@ constexpr int kPOffSFB = kPOffW + 16384;
 constexpr int kPStageBytes = kPA + kPSF + kPW; // 34816
 constexpr int kPAccBufs = 3;                   // 128 fp32 columns each
 constexpr uint32_t kPTmemCols = 512;
-constexpr uint32_t kPTmemSFA = kPAccBufs * 128;
+constexpr uint32_t kPTmemSFA = kPAccBufs * 128;  // + 16 per ring slot: SFA 8 columns, SFB 8
 constexpr uint32_t kPTmemSFB = kPTmemSFA + 8;
+static_assert(kPTmemSFA + 16 * kPStages <= kPTmemCols, "scale-factor columns exceed the allocation");
 constexpr int kPMaxExperts = 256;
 constexpr int kPMaxChunks = kPMaxExperts + kPrefillMaxPairs / kPTile;
 
@@ -68,8 +72,7 @@ struct PrefillArgs {
   const uint8_t* xa;           // token-row scale atoms [row/128][H/128][512]
   uint8_t* hp;                 // requantised h rows (rows, inter/2)
   uint8_t* ha;                 // their scale atoms [row/128][inter/128][512]
-  const float* topw;           // (pairs) routing weights
-  float* out;                  // (T, hidden) fp32, cleared by the router
+  float* yd;                   // (pairs, hidden) fp32 per-(token, slot) down rows
   int hidden, inter, top_k;
   int* err;
   int* queue;                  // work-item counter, zero before the launch
@@ -86,11 +89,6 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
-}
-__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
-               "f"(d)
-               : "memory");
 }
 
 // Rows of expert e start at base[e] = sum over e' < e of counts rounded up to
@@ -176,9 +174,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
     for (int b = 0; b < kPAccBufs; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], kPEpiWarps);
       mbar_init(&item_full[b], 1);
-      mbar_init(&item_empty[b], 5);  // the MMA thread + the 4 epilogue warps
+      mbar_init(&item_empty[b], 1 + kPEpiWarps);  // the MMA thread + the epilogue warps
     }
     fence_mbar_init();
   }
@@ -315,10 +313,13 @@ __global__ void __launch_bounds__(kPThreads, 1)
           if (!mbar_wait(&full[s], (it / kPStages) & 1, p.err, 2)) { ok = false; break; }
           tc_fence_after();
           const uint32_t base = smem_u32(ring + s * kPStageBytes);
+          // each ring slot has its own scale-factor columns, so the copy for
+          // this stage need not wait for the MMAs of the previous one
+          const uint32_t sfa = tmem + kPTmemSFA + 16 * s, sfb = tmem + kPTmemSFB + 16 * s;
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
-            tmem_cp_sf(tmem + kPTmemSFA + 4 * c, make_sdesc(base + kPOffSFA + c * 512, 0, 128, kLayoutNone));
-            tmem_cp_sf(tmem + kPTmemSFB + 4 * c, make_sdesc(base + kPOffSFB + c * 512, 0, 128, kLayoutNone));
+            tmem_cp_sf(sfa + 4 * c, make_sdesc(base + kPOffSFA + c * 512, 0, 128, kLayoutNone));
+            tmem_cp_sf(sfb + 4 * c, make_sdesc(base + kPOffSFB + c * 512, 0, 128, kLayoutNone));
           }
 #pragma unroll
           for (int kb = 0; kb < 4; ++kb) {
@@ -327,7 +328,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
             mma_mxf4(d, make_sdesc(base + kb * 32, 16, 1024, kLayoutSW128),
                      make_sdesc(base + kPOffW + kb * 32, 16, 1024, kLayoutSW128),
                      make_idesc_mxf4(128, 128, int(byte), int(byte)), (ks | kb) != 0 ? 1u : 0u,
-                     (tmem + kPTmemSFA + 4 * c) | (byte << 30), (tmem + kPTmemSFB + 4 * c) | (byte << 30));
+                     (sfa + 4 * c) | (byte << 30), (sfb + 4 * c) | (byte << 30));
           }
           tc_commit(&empty[s]);
         }
@@ -336,7 +337,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
   } else {
     const int quad = warp & 3;          // TMEM lane quadrant of this warp
-    const int et = threadIdx.x - 64;    // 0..127
+    const int et = threadIdx.x - 64;    // 0..255
+    const int half = et >> 7;           // which half of the tile's columns
     const int r = quad * 32 + lane;     // token row inside the tile
     for (uint32_t acc_it = 0;; ++acc_it) {
       const uint32_t buf = acc_it % kPAccBufs;
@@ -354,29 +356,22 @@ __global__ void __launch_bounds__(kPThreads, 1)
       tile_of(tl, e, row0, count);
       const bool valid = r < count;
       const int row = row0 + r;
-      int pair = 0;
-      float wgt = 0.0f;
-      if (!gu && valid) {
-        pair = p.perm[row];
-        wgt = p.topw[pair];
-      }
+      const int pair = (!gu && valid) ? p.perm[row] : 0;
       if (!mbar_wait(&acc_full[buf], (acc_it / kPAccBufs) & 1, p.err, 3)) break;
       tc_fence_after();
       const uint32_t tbase = tmem + (uint32_t(quad * 32) << 16) + buf * 128;
       if (gu) {
         // columns 0-63: gate outputs tile*64 + c, 64-127: the same up outputs
         uint8_t* hrow = p.hp + size_t(row) * (p.inter / 2) + tile * 32;
-#pragma unroll 1
-        for (int hb = 0; hb < 2; ++hb) {
+        {
+          const int hb = half;  // outputs tile*64 + hb*32 .. +31
           uint32_t g[32], u[32];
           tmem_ld_32x32b_x32(tbase + hb * 32, g);
           tmem_ld_32x32b_x32(tbase + 64 + hb * 32, u);
           tmem_ld_wait();
-          if (hb == 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[buf]);
-          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[buf]);
           float h[32];
           float am = 0.0f;
           bool nan = false;
@@ -404,21 +399,20 @@ __global__ void __launch_bounds__(kPThreads, 1)
           }
         }
         // publish this 64-column slice of the tile's h rows to its down items
-        named_bar_sync(1, 128);
+        named_bar_sync(1, 32 * kPEpiWarps);
         if (et == 0) {
           fence_proxy_async_global();
           __threadfence();
           atomicAdd(p.ready + tl, 1u);
         }
       } else {
-        const int t = pair / p.top_k;
-        float* orow = p.out + size_t(t) * p.hidden + tile * 128;
+        float* yrow = p.yd + size_t(pair) * p.hidden + tile * 128;
 #pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
+        for (int cc = 2 * half; cc < 2 * half + 2; ++cc) {
           uint32_t y[32];
           tmem_ld_32x32b_x32(tbase + cc * 32, y);
           tmem_ld_wait();
-          if (cc == 3) {
+          if (cc == 2 * half + 1) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
@@ -426,10 +420,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
           if (valid) {
 #pragma unroll
             for (int i = 0; i < 32; i += 4)
-              red_add_v4(orow + cc * 32 + i, __fmul_rn(wgt, __uint_as_float(y[i])),
-                         __fmul_rn(wgt, __uint_as_float(y[i + 1])),
-                         __fmul_rn(wgt, __uint_as_float(y[i + 2])),
-                         __fmul_rn(wgt, __uint_as_float(y[i + 3])));
+              *reinterpret_cast<uint4*>(yrow + cc * 32 + i) = make_uint4(y[i], y[i + 1], y[i + 2], y[i + 3]);
           }
         }
       }
@@ -490,8 +481,7 @@ cudaError_t launch_moe_prefill(const PrefillLaunch& L, cudaStream_t stream) {
   p.xa = L.xa;
   p.hp = L.hp;
   p.ha = L.ha;
-  p.topw = L.topw;
-  p.out = L.out;
+  p.yd = L.yd;
   p.hidden = H;
   p.inter = Mi;
   p.top_k = L.top_k;

@@ -62,8 +62,9 @@ constexpr int kWBlock = kA + kSF;
 constexpr int kThreads = 192;
 constexpr int kAccBufs = 4;     // TMEM accumulators (32 fp32 columns each)
 constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kTmemSFA = kAccBufs * 32;
+constexpr uint32_t kTmemSFA = kAccBufs * 32;   // + 16 per ring slot: SFA 8 columns, SFB 8
 constexpr uint32_t kTmemSFB = kTmemSFA + 8;
+static_assert(kTmemSFA + 16 * kStages <= kTmemCols, "scale-factor columns exceed the allocation");
 constexpr int kChunk = 32;     // tokens per chunk (MMA N)
 
 constexpr int kMaxExperts = 256;
@@ -308,10 +309,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           if (!mbar_wait(&full[s], (it / kStages) & 1, p.err, 2)) { ok = false; break; }
           tc_fence_after();
           const uint32_t base = smem_u32(ring + s * kStageBytes);
+          // each ring slot has its own scale-factor columns, so the copy for
+          // this stage need not wait for the MMAs of the previous one
+          const uint32_t sfa = tmem + kTmemSFA + 16 * s, sfb = tmem + kTmemSFB + 16 * s;
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
-            tmem_cp_sf(tmem + kTmemSFA + 4 * c, make_sdesc(base + kOffSFA + c * 512, 0, 128, kLayoutNone));
-            tmem_cp_sf(tmem + kTmemSFB + 4 * c, make_sdesc(base + kOffSFB + c * 512, 0, 128, kLayoutNone));
+            tmem_cp_sf(sfa + 4 * c, make_sdesc(base + kOffSFA + c * 512, 0, 128, kLayoutNone));
+            tmem_cp_sf(sfb + 4 * c, make_sdesc(base + kOffSFB + c * 512, 0, 128, kLayoutNone));
           }
 #pragma unroll
           for (int kb = 0; kb < 4; ++kb) {
@@ -320,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             mma_mxf4(d, make_sdesc(base + kb * 32, 16, 1024, kLayoutSW128),
                      make_sdesc(base + kOffB + kb * 32, 16, 1024, kLayoutSW128),
                      make_idesc_mxf4(128, kChunk, int(byte), int(byte)), (ks | kb) != 0 ? 1u : 0u,
-                     (tmem + kTmemSFA + 4 * c) | (byte << 30), (tmem + kTmemSFB + 4 * c) | (byte << 30));
+                     (sfa + 4 * c) | (byte << 30), (sfb + 4 * c) | (byte << 30));
           }
           tc_commit(&empty[s]);
         }

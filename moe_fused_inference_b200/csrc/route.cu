@@ -545,9 +545,7 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
   }
   if (a.logits)
     for (int e = threadIdx.x; e < a.E; e += kClusterThreads) a.logits[long(t) * a.E + e] = s_logit[e];
-  if (a.out_zero)
-    for (int i = threadIdx.x; i < (a.H >> 2); i += kClusterThreads)
-      reinterpret_cast<float4*>(a.out_zero + long(t) * a.H)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+
 
   // ---- top-k, weights, expert-row claims (leader) ----------------------------
   __shared__ int s_sel[32];
@@ -637,6 +635,212 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
   }
 }
 
+// ---------------------------------------------------------------------------
+// Batch router for prefill sizes (many tokens): the whole router (E rows and
+// their scales) is staged once per CTA in shared memory and every warp routes
+// one token at a time — quantise, 128 logits with route_kernel's per-lane
+// order and butterfly (bit-identical), top-k by 8 rounds of warp arg-max
+// (value descending, lower index on ties: the same order as the rank method),
+// weights, and the per-expert position claim of the prefill placement.
+constexpr int kBatchThreads = 512;
+constexpr int kBatchWarps = kBatchThreads / 32;
+
+size_t route_batch_smem(int E, int H) {
+  return size_t(E) * (H / 2) + size_t(E) * (H / 32) + size_t(kBatchWarps) * (H / 2 + H / 32) +
+         size_t(kBatchWarps) * E * sizeof(float) + 64;
+}
+
+template <int kMaxBlk>
+__global__ void __launch_bounds__(kBatchThreads) route_batch_kernel(RouteArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int nb = a.H >> 5;
+  uint8_t* s_w = smem;                                          // [E][H/2]
+  uint8_t* s_ws = s_w + size_t(a.E) * (a.H >> 1);               // [E][H/32]
+  uint8_t* s_xq_all = s_ws + size_t(a.E) * nb;                  // [warps][H/2]
+  uint8_t* s_xsc_all = s_xq_all + size_t(kBatchWarps) * (a.H >> 1);
+  float* s_lg_all = reinterpret_cast<float*>(
+      (reinterpret_cast<uintptr_t>(s_xsc_all + size_t(kBatchWarps) * nb) + 15) & ~uintptr_t(15));
+  __shared__ __align__(8) uint64_t s_bar;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint8_t* s_xq = s_xq_all + size_t(warp) * (a.H >> 1);
+  uint8_t* s_xsc = s_xsc_all + size_t(warp) * nb;
+  float* s_lg = s_lg_all + size_t(warp) * a.E;
+
+  const uint32_t w_bytes = uint32_t(a.E) * uint32_t(a.H >> 1);
+  const uint32_t sc_bytes = uint32_t(a.E) * uint32_t(nb);
+  const bool sc_bulk = (sc_bytes % 16) == 0 && (reinterpret_cast<uintptr_t>(a.sr) % 16) == 0;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&s_bar, 1);
+    tc::fence_mbar_init();
+    tc::mbar_expect_tx(&s_bar, w_bytes + (sc_bulk ? sc_bytes : 0u));
+    tc::bulk_load(s_w, a.wr, w_bytes, &s_bar);
+    if (sc_bulk) tc::bulk_load(s_ws, a.sr, sc_bytes, &s_bar);
+  }
+  if (!sc_bulk)
+    for (uint32_t i = threadIdx.x; i < sc_bytes; i += kBatchThreads) s_ws[i] = a.sr[i];
+  __syncthreads();
+  const bool have_w = tc::mbar_wait(&s_bar, 0, a.err, 6);
+  __syncthreads();
+
+  for (int t = blockIdx.x * kBatchWarps + warp; t < a.T; t += gridDim.x * kBatchWarps) {
+    // ---- quantise token t (quads of lanes per 32-element block) ----------
+    for (int base = 0; base < (a.H >> 3); base += 32) {
+      const int c8 = base + lane;
+      const bool live = c8 < (a.H >> 3);
+      float v[8];
+      if (live) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(
+            reinterpret_cast<const __nv_bfloat16*>(a.x) + long(t) * a.H + c8 * 8);
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(h2[i]);
+          v[2 * i] = f.x;
+          v[2 * i + 1] = f.y;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+      }
+      BlockScale bs;
+      const uint32_t word = quant_group8(v, bs);
+      if (live) {
+        reinterpret_cast<uint32_t*>(s_xq)[c8] = word;
+        if ((c8 & 3) == 0) s_xsc[c8 >> 2] = bs.code;
+      }
+    }
+    __syncwarp();
+    if (a.xq) {
+      for (int i = lane; i < (a.H >> 5); i += 32)
+        reinterpret_cast<uint4*>(a.xq + long(t) * (a.H >> 1))[i] = reinterpret_cast<const uint4*>(s_xq)[i];
+      for (int i = lane; i < nb; i += 32) a.xsc[long(t) * nb + i] = s_xsc[i];
+    }
+    // ---- logits ------------------------------------------------------------
+    uint32_t xa8[kMaxBlk][8];
+    int xs[kMaxBlk];
+#pragma unroll
+    for (int j = 0; j < kMaxBlk; ++j) {
+      const int b = lane + 32 * j;
+      if (b < nb) {
+        const uint4 q = reinterpret_cast<const uint4*>(s_xq)[b];
+        nib8_to_i8(q.x, xa8[j][0], xa8[j][1]);
+        nib8_to_i8(q.y, xa8[j][2], xa8[j][3]);
+        nib8_to_i8(q.z, xa8[j][4], xa8[j][5]);
+        nib8_to_i8(q.w, xa8[j][6], xa8[j][7]);
+        xs[j] = s_xsc[b];
+      }
+    }
+    constexpr int kU = 8;
+    for (int e0 = 0; e0 < a.E; e0 += kU) {
+      double acc[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int e = e0 + u;
+        acc[u] = 0.0;
+#pragma unroll
+        for (int j = 0; j < kMaxBlk; ++j) {
+          const int b = lane + 32 * j;
+          if (have_w && e < a.E && b < nb) {
+            const uint4 wv = *reinterpret_cast<const uint4*>(s_w + size_t(e) * (a.H >> 1) + b * 16);
+            const int sdot = block_dot_pre(wv, xa8[j]);
+            acc[u] += double(sdot) * exp2i_d(xs[j] + int(s_ws[e * nb + b]) - 256);
+          }
+        }
+      }
+      int n = kU;
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) {
+        if (n > 1) {
+          const bool upper = (lane & off) != 0;
+          const int h = n >> 1;
+#pragma unroll
+          for (int i = 0; i < kU / 2; ++i) {
+            if (i < h) {
+              const double send = upper ? acc[i] : acc[i + h];
+              const double keep = upper ? acc[i + h] : acc[i];
+              acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+            }
+          }
+          n = h;
+        } else {
+          acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], off);
+        }
+      }
+      // after 3 halving steps lane l holds expert e0 + (l >> 2)
+      if ((lane & 3) == 0 && e0 + (lane >> 2) < a.E) s_lg[e0 + (lane >> 2)] = float(acc[0]);
+    }
+    __syncwarp();
+    if (a.logit_bias)
+      for (int e = lane; e < a.E; e += 32) s_lg[e] = __fadd_rn(s_lg[e], a.logit_bias[e]);
+    __syncwarp();
+    if (a.logits)
+      for (int e = lane; e < a.E; e += 32) a.logits[long(t) * a.E + e] = s_lg[e];
+    // ---- top-k: k rounds of warp arg-max ----------------------------------
+    constexpr int kPer = kRouteMaxE / 32;
+    float v[kPer];
+    uint32_t taken = 0;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) v[i] = (lane + 32 * i < a.E) ? s_lg[lane + 32 * i] : 0.0f;
+    int my_sel = -1;
+    float my_val = 0.0f;
+    for (int j = 0; j < a.k; ++j) {
+      float bv = 0.0f;
+      int bi = -1;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int e = lane + 32 * i;
+        if (e < a.E && !((taken >> i) & 1u) && (bi < 0 || better(v[i], e, bv, bi))) {
+          bv = v[i];
+          bi = e;
+        }
+      }
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (oi >= 0 && (bi < 0 || better(ov, oi, bv, bi))) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+      if (lane == j) {
+        my_sel = bi;
+        my_val = bv;
+      }
+    }
+    // ---- weights: exp(l - max) over the selected, normalised by their sum --
+    const float mx = __shfl_sync(0xffffffffu, my_val, 0);
+    const float pj = lane < a.k ? expf(my_val - mx) : 0.0f;
+    float sum = 0.0f;
+    for (int j = 0; j < a.k; ++j) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, pj, j));
+    if (lane < a.k) {
+      a.topi[long(t) * a.k + lane] = my_sel;
+      a.topw[long(t) * a.k + lane] = __fdiv_rn(pj, sum);
+      if (a.slot_pos) a.slot_pos[long(t) * a.k + lane] = atomicAdd(a.cursor + my_sel, 1);
+    }
+    __syncwarp();
+  }
+}
+
+template <int kMaxBlk>
+static cudaError_t launch_route_batch(const RouteArgs& a, cudaStream_t stream) {
+  const size_t smem = route_batch_smem(a.E, a.H);
+  static size_t smem_set = 0;  // largest dynamic size granted so far
+  if (smem > smem_set) {
+    cudaError_t e = cudaFuncSetAttribute(route_batch_kernel<kMaxBlk>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    smem_set = smem;
+  }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int need = (a.T + kBatchWarps - 1) / kBatchWarps;
+  route_batch_kernel<kMaxBlk><<<need < sms ? need : sms, kBatchThreads, smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
 template <int kMaxBlk>
 static cudaError_t launch_route_cluster(const RouteArgs& a, cudaStream_t stream) {
   static bool smem_set = false;
@@ -669,6 +873,11 @@ cudaError_t launch_route(const RouteArgs& a, cudaStream_t stream) {
   if (a.T < 0 || (a.T == 0 && !a.ep.table)) return cudaSuccess;
   if (a.H > 4096) return cudaErrorInvalidValue;
   if (!a.g_gu) {
+    // many tokens, placement by position claims, router fits in shared
+    // memory: one router copy per CTA, one token per warp
+    if (a.batch && !a.xp && !a.ep.table && route_batch_smem(a.E, a.H) <= 200 * 1024 &&
+        (size_t(a.E) * (a.H >> 5)) % 16 == 0 && (reinterpret_cast<uintptr_t>(a.wr) & 15) == 0)
+      return a.H <= 2048 ? launch_route_batch<2>(a, stream) : launch_route_batch<4>(a, stream);
     // routing alone, or routing + expert regions for the tensor-core kernels
     return a.H <= 2048 ? launch_route_cluster<2>(a, stream) : launch_route_cluster<4>(a, stream);
   }

@@ -101,9 +101,9 @@ struct RouteArgs {
   EpDispatch ep;       // ep.table == null: no expert-parallel dispatch
   const float* logit_bias;  // [E] added to the logits before top-k, or null
   // prefill placement: slot_pos[t*k + j] = the pair's position among the
-  // tokens of its expert (cursor claim, no row copy); out rows zeroed here
+  // tokens of its expert (cursor claim, no row copy)
   int* slot_pos;
-  float* out_zero;     // (T, H) fp32 rows to clear, or null
+  bool batch;          // prefer the one-token-per-warp batch router (many tokens)
 };
 
 constexpr int kRouteMaxE = 256;
@@ -189,8 +189,7 @@ struct PrefillLaunch {
   int rows;                      // rows of xp / hp (prefill_rows)
   const uint8_t* xp; const uint8_t* xa;   // token rows and their 128-row scale atoms
   uint8_t* hp; uint8_t* ha;               // requantised h rows and atoms
-  const float* topw;             // (pairs)
-  float* out;                    // (T, H), zero before the launch
+  float* yd;                     // (pairs, H) per-(token, slot) down rows
   int* err; int* queue; unsigned* ready;
   bool pdl;
 };

@@ -5,8 +5,8 @@ tiles, vs the kernel-path oracle.
 Contract (BASELINE north_star): top-k indices and router logits bit-exact;
 layer output max relative error <= 1e-2 and cosine >= 0.999 versus the
 fp32-accumulated dequantised reference (the oracle accumulates in float64).
-The prefill combine adds a token's slots in arrival order (fp32 reductions),
-so outputs are compared with a tolerance, never bit for bit.
+The prefill combine is the decode one (slot order, unfused fp32 multiply and
+add), so a call is bit-reproducible whatever order the rows were placed in.
 """
 
 import numpy as np
@@ -104,6 +104,5 @@ def test_prefill_repeatable_and_capturable(qwen_layer):
     out.zero_()
     g.replay()
     torch.cuda.synchronize()
-    # reductions in arrival order: equal to fp32 rounding, not necessarily bitwise
-    assert max_rel_err(out.cpu().numpy(), first.cpu().numpy()) <= 1e-5
+    assert torch.equal(out, first)  # placement order varies, results do not
     del g
