@@ -56,6 +56,11 @@ def parse():
     ap.add_argument("--tokens", type=int, default=64, help="decode tokens per GPU (T)")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="distinct MoE layers per step (48 = the model; fewer for profiling)")
+    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+                    help="decode (BASELINE config 2, the headline) or prefill (config 3: "
+                         "T = 16384 by default, Zipf(1.2)-skewed routing)")
+    ap.add_argument("--zipf-alpha", type=float, default=0.5,
+                    help="prefill: scale of the Zipf(1.2) per-expert logit bias")
     ap.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
                     help="multi-GPU token exchange: peer-memory stores fused into the kernels "
                          "(p2p) or two NCCL all_to_all_single calls (nccl)")
@@ -287,7 +292,66 @@ def cpu_baseline(args, T, weights):
                       "dequantised (runtime/model_runner.py:99-132 ported)"}
 
 
+def run_prefill(args, world, rank, local):
+    """one prefill-sized MoE layer call per layer (T tokens,
+    default 16384) with Zipf(1.2)-skewed routing; FLOP rate of the layer
+    against the dense FP4 tensor peak.  Single GPU; under torchrun every rank
+    runs its own copy (weak scaling)."""
+    from moe_fused_inference_b200.layer import MoELayer, random_layer_weights
+    from oracle import mxfp4 as mx
+
+    dev = torch.device("cuda", local if world > 1 else 0)
+    T = args.tokens if args.tokens != 64 else 16384
+    NL = args.layers if args.layers != N_LAYERS else 4
+    bias = torch.from_numpy(mx.zipf_bias(E, args.zipf_alpha, seed=3))
+    layers = [MoELayer(random_layer_weights(E, H, MI, 0.02, seed=l, device=dev), TOPK,
+                       logit_bias=bias) for l in range(NL)]
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    X = torch.randn((NL, T, H), generator=g, device=dev).bfloat16()
+    out = torch.empty((NL, T, H), dtype=torch.float32, device=dev)
+    topi = torch.empty((NL, T, TOPK), dtype=torch.int32, device=dev)
+    topw = torch.empty((NL, T, TOPK), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for l in range(NL):
+            layers[l](X[l], out=out[l], topi=topi[l], topw=topw[l])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    ms, clocks = timed_region(args, world, dev, stream, step)
+    ms_per_step = ms / args.steps
+    flop_tok = TOPK * (2 * H * 2 * MI + 2 * MI * H) + 2 * H * E   # experts + router
+    flops = flop_tok * T * NL
+    tflops = flops / (ms_per_step / 1e3) / 1e12
+    counts = torch.bincount(topi[0].flatten().long(), minlength=E).float()
+    fp4_peak = 9000.0  # dense MXFP4 tensor peak, nominal (no measured FP4 figure on this pool)
+    if rank != 0:
+        return
+    line = {
+        "metric": "MXFP4 MoE layer tokens/s (prefill)", "value": T * NL * args.steps * world / (ms / 1e3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "mxfp4 (e2m1 x e2m1, fp32 accumulate)",
+        "data": "synthetic (random-init weights N(0,0.02), activations N(0,1), seeded)",
+        "config": {"workload": f"prefill MoE layer, T={T} tokens, H=2048, E=128, top-8, Mi=768, "
+                               f"Zipf(1.2) logit bias alpha={args.zipf_alpha}",
+                   "step": f"{NL} MoE layers with distinct weights, plain launches",
+                   "expert_load_max_over_mean": float(counts.max() / counts.mean()),
+                   "experts_with_tokens": int((counts > 0).sum())},
+        "gpu_launches": 5 * NL * args.steps,  # route, scatter, experts, combine (+ memset)
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": fp4_peak, "unit": "TFLOP/s",
+                     "frac": tflops / fp4_peak, "peak_kind": "nominal dense FP4 (no measured FP4 peak)",
+                     "flops_per_layer": flop_tok * T},
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_ours(args, world, rank, local):
+    if args.workload == "prefill":
+        return run_prefill(args, world, rank, local)
     if world > 1:
         return run_ep(args, world, rank, local)
     from moe_fused_inference_b200.layer import MoELayer, random_layer_weights
