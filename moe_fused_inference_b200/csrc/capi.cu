@@ -368,6 +368,7 @@ namespace {
 struct PrefillScratch {
   int* counts;          // [E] tokens per expert (router cursors)
   int* queue;           // work-item counter
+  unsigned* gu_done;    // finished gate/up items
   unsigned* ready;      // [max tiles]
   size_t zero_words;
   int* slot_pos;        // [T*k]
@@ -384,10 +385,11 @@ PrefillScratch carve_prefill(void* ws, int T, int H, int Mi, int E, int k) {
   PrefillScratch s;
   const int P = T * k;
   const size_t max_tiles = size_t(E) + size_t(P) / 128 + 1;
-  s.zero_words = size_t(E) + 1 + max_tiles;
+  s.zero_words = size_t(E) + 2 + max_tiles;
   s.counts = c.take<int>(s.zero_words);
   s.queue = s.counts + E;
-  s.ready = reinterpret_cast<unsigned*>(s.counts + E + 1);
+  s.gu_done = reinterpret_cast<unsigned*>(s.counts + E + 1);
+  s.ready = reinterpret_cast<unsigned*>(s.counts + E + 2);
   s.slot_pos = c.take<int>(size_t(P));
   s.xq = c.take<uint8_t>(size_t(T) * (H / 2));
   s.xsc = c.take<uint8_t>(size_t(T) * (H / 32));
@@ -445,7 +447,7 @@ int run_prefill(const mfi_moe_weights* w, const void* x_bf16, int T, float* out,
   L.counts = s.counts; L.perm = s.perm; L.rows = s.rows;
   L.xp = s.xp; L.xa = s.xa; L.hp = s.hp; L.ha = s.ha;
   L.yd = s.yd;
-  L.err = mfi::device_error_flag(); L.queue = s.queue; L.ready = s.ready;
+  L.err = mfi::device_error_flag(); L.queue = s.queue; L.gu_done = s.gu_done; L.ready = s.ready;
   L.pdl = true;
   rc = cuda_status(mfi::launch_moe_prefill(L, st), "moe_layer prefill experts launch");
   if (rc != MFI_OK) return rc;

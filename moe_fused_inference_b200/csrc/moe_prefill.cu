@@ -42,10 +42,11 @@ namespace {
 #define MFI_PF_STAGES 5
 #endif
 constexpr int kPStages = MFI_PF_STAGES;
-// warp 0 loads, warp 1 issues MMAs, warps 2-9 run the epilogue: two warps
-// per TMEM lane quadrant, each taking half of the tile's columns (the SwiGLU
-// epilogue is latency-bound with one warp per scheduler)
-constexpr int kPEpiWarps = 8;
+// warp 0 loads, warp 1 issues MMAs, warps 2-17 run the epilogue: four warps
+// per TMEM lane quadrant, each taking a quarter of the tile's columns (the
+// SwiGLU epilogue is latency-bound: with fewer warps it, not the MMA, sets
+// the pace of the gate/up items)
+constexpr int kPEpiWarps = 16;
 constexpr int kPThreads = 64 + 32 * kPEpiWarps;
 constexpr int kPTile = 128;                    // token rows per tile (MMA M)
 constexpr int kPA = 16384;                     // 128 token rows x 128 B
@@ -76,6 +77,7 @@ struct PrefillArgs {
   int hidden, inter, top_k;
   int* err;
   int* queue;                  // work-item counter, zero before the launch
+  unsigned* gu_done;           // finished gate/up items in all, zero before the launch
   unsigned* ready;             // per tile: finished gate/up items, zero before the launch
 };
 
@@ -161,6 +163,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
   uint64_t* item_empty = item_full + kPAccBufs;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_empty + kPAccBufs);
   __shared__ int s_item[kPAccBufs];
+  __shared__ float s_am[4][kPTile];  // gate/up epilogue: partial block maxima per quarter
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_gu = p.inter / 64, tiles_dn = p.hidden / 128;
@@ -241,7 +244,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
     if (elect_one()) {
       uint32_t it = 0;
       bool ok = true;
+      bool all_ready = false;  // every gate/up item has published its h rows
       int item = first_item;
+      int next = atomicAdd(p.queue, 1);  // items are claimed two ahead
       for (uint32_t qi = 0; ok; ++qi) {
         const uint32_t slot = qi % kPAccBufs;
         if (!mbar_wait(&item_empty[slot], ((qi / kPAccBufs) & 1) ^ 1, p.err, 1)) break;
@@ -249,7 +254,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         s_item[slot] = item;
         mbar_arrive(&item_full[slot]);
         if (item < 0) break;
-        const int next = atomicAdd(p.queue, 1);
+        const int next2 = atomicAdd(p.queue, 1);
         bool gu;
         int tl, tile, e, row0, count;
         decode(item, gu, tl, tile);
@@ -259,7 +264,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
           wb = p.w_gu + (size_t(e) * tiles_gu + tile) * ks_gu * size_t(kPW);
         } else {
           wb = p.w_dn + (size_t(e) * tiles_dn + tile) * ks_dn * size_t(kPW);
-          if (ld_acquire_u32(p.ready + tl) < unsigned(tiles_gu)) {
+          if (!all_ready && ld_acquire_u32(p.gu_done) >= unsigned(n_gu)) all_ready = true;
+          if (!all_ready && ld_acquire_u32(p.ready + tl) < unsigned(tiles_gu)) {
             const uint64_t t0 = globaltimer_ns();
             for (uint32_t i = 1;; ++i) {
               __nanosleep(64);
@@ -289,6 +295,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
           bulk_load(st + kPOffW, wb + size_t(ks) * kPW, kPW, &full[s]);
         }
         item = next;
+        next = next2;
       }
     }
   } else if (warp == 1) {
@@ -337,8 +344,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
   } else {
     const int quad = warp & 3;          // TMEM lane quadrant of this warp
-    const int et = threadIdx.x - 64;    // 0..255
-    const int half = et >> 7;           // which half of the tile's columns
+    const int et = threadIdx.x - 64;    // 0..511
+    const int part = et >> 7;           // which quarter of the tile's columns
     const int r = quad * 32 + lane;     // token row inside the tile
     for (uint32_t acc_it = 0;; ++acc_it) {
       const uint32_t buf = acc_it % kPAccBufs;
@@ -361,67 +368,70 @@ __global__ void __launch_bounds__(kPThreads, 1)
       tc_fence_after();
       const uint32_t tbase = tmem + (uint32_t(quad * 32) << 16) + buf * 128;
       if (gu) {
-        // columns 0-63: gate outputs tile*64 + c, 64-127: the same up outputs
-        uint8_t* hrow = p.hp + size_t(row) * (p.inter / 2) + tile * 32;
-        {
-          const int hb = half;  // outputs tile*64 + hb*32 .. +31
-          uint32_t g[32], u[32];
-          tmem_ld_32x32b_x32(tbase + hb * 32, g);
-          tmem_ld_32x32b_x32(tbase + 64 + hb * 32, u);
-          tmem_ld_wait();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[buf]);
-          float h[32];
-          float am = 0.0f;
-          bool nan = false;
+        // columns 0-63: gate outputs tile*64 + c, 64-127: the same up outputs;
+        // this warp takes outputs part*16 .. +15 (half of 32-element block
+        // part/2), its partner warp (part^1) the other half
+        uint32_t g[16], u[16];
+        tmem_ld_32x32b_x16(tbase + part * 16, g);
+        tmem_ld_32x32b_x16(tbase + 64 + part * 16, u);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        float h[16];
+        float am = 0.0f;
+        bool nan = false;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float gv = __uint_as_float(g[i]), uv = __uint_as_float(u[i]);
-            h[i] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
-            am = fmaxf(am, fabsf(h[i]));
-            nan |= (h[i] != h[i]);
-          }
-          const BlockScale bs = block_scale(nan ? __uint_as_float(0x7fc00000u) : am);
-          uint32_t w4[4];
+        for (int i = 0; i < 16; ++i) {
+          const float gv = __uint_as_float(g[i]), uv = __uint_as_float(u[i]);
+          h[i] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
+          am = fmaxf(am, fabsf(h[i]));
+          nan |= (h[i] != h[i]);
+        }
+        s_am[part][r] = nan ? __uint_as_float(0x7fc00000u) : am;
+        named_bar_sync(2, 32 * kPEpiWarps);
+        const float other = s_am[part ^ 1][r];
+        // a NaN anywhere in the block gives code 127, like quant_group8
+        const float bam = (am != am || other != other) ? __uint_as_float(0x7fc00000u) : fmaxf(am, other);
+        const BlockScale bs = block_scale(nan || other != other ? __uint_as_float(0x7fc00000u) : bam);
+        uint32_t w0 = 0, w1 = 0;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint32_t wd = 0;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) wd |= quant_nibble(h[q * 8 + i], bs.inv) << (4 * i);
-            w4[q] = wd;
-          }
-          if (valid) {
-            *reinterpret_cast<uint4*>(hrow + hb * 16) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-            const int kb = tile * 2 + hb;  // 32-element block of h along inter
+        for (int i = 0; i < 8; ++i) {
+          w0 |= quant_nibble(h[i], bs.inv) << (4 * i);
+          w1 |= quant_nibble(h[8 + i], bs.inv) << (4 * i);
+        }
+        if (valid) {
+          const int b = part >> 1;
+          *reinterpret_cast<uint2*>(p.hp + size_t(row) * (p.inter / 2) + tile * 32 + part * 8) =
+              make_uint2(w0, w1);
+          if ((part & 1) == 0) {
+            const int kb = tile * 2 + b;  // 32-element block of h along inter
             p.ha[(size_t(row / kPTile) * kc_dn + kb / 4) * 512 + (row % 32) * 16 +
                  ((row % kPTile) / 32) * 4 + (kb & 3)] = bs.code;
           }
         }
         // publish this 64-column slice of the tile's h rows to its down items
+        // (the barrier also frees s_am for the next item)
         named_bar_sync(1, 32 * kPEpiWarps);
         if (et == 0) {
           fence_proxy_async_global();
           __threadfence();
           atomicAdd(p.ready + tl, 1u);
+          atomicAdd(p.gu_done, 1u);
         }
       } else {
-        float* yrow = p.yd + size_t(pair) * p.hidden + tile * 128;
-#pragma unroll 1
-        for (int cc = 2 * half; cc < 2 * half + 2; ++cc) {
-          uint32_t y[32];
-          tmem_ld_32x32b_x32(tbase + cc * 32, y);
-          tmem_ld_wait();
-          if (cc == 2 * half + 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[buf]);
-          }
-          if (valid) {
+        // this warp stores output columns part*32 .. +31 of the token rows
+        uint32_t y[32];
+        tmem_ld_32x32b_x32(tbase + part * 32, y);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        if (valid) {
+          float* yrow = p.yd + size_t(pair) * p.hidden + tile * 128 + part * 32;
 #pragma unroll
-            for (int i = 0; i < 32; i += 4)
-              *reinterpret_cast<uint4*>(yrow + cc * 32 + i) = make_uint4(y[i], y[i + 1], y[i + 2], y[i + 3]);
-          }
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<uint4*>(yrow + i) = make_uint4(y[i], y[i + 1], y[i + 2], y[i + 3]);
         }
       }
     }
@@ -458,7 +468,7 @@ cudaError_t launch_prefill_scatter(const uint8_t* xq, const uint8_t* xsc, const 
 }
 
 cudaError_t launch_moe_prefill(const PrefillLaunch& L, cudaStream_t stream) {
-  if (L.queue == nullptr || L.ready == nullptr) return cudaErrorInvalidValue;
+  if (L.queue == nullptr || L.ready == nullptr || L.gu_done == nullptr) return cudaErrorInvalidValue;
   static bool smem_set = false;
   if (!smem_set) {
     cudaError_t e = cudaFuncSetAttribute(moe_prefill_kernel,
@@ -487,6 +497,7 @@ cudaError_t launch_moe_prefill(const PrefillLaunch& L, cudaStream_t stream) {
   p.top_k = L.top_k;
   p.err = L.err;
   p.queue = L.queue;
+  p.gu_done = L.gu_done;
   p.ready = L.ready;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(L.grid);

@@ -645,9 +645,56 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
 constexpr int kBatchThreads = 512;
 constexpr int kBatchWarps = kBatchThreads / 32;
 
+// Each warp routes kBatchTok tokens together, so every router block is
+// expanded from nibbles to int8 once for all of them.
+#ifndef MFI_BATCH_TOK
+#define MFI_BATCH_TOK 2
+#endif
+#ifndef MFI_BATCH_U
+#define MFI_BATCH_U 4
+#endif
+constexpr int kBatchTok = MFI_BATCH_TOK;
+
+// per (warp, token): the quantised row (H/2 B, reused for the E logits once
+// the row is in registers) and its scales
+__host__ __device__ inline size_t route_batch_slot(int E, int H) {
+  const size_t row = size_t(H / 2) > size_t(E) * sizeof(float) ? size_t(H / 2) : size_t(E) * sizeof(float);
+  return (row + size_t(H / 32) + 15) / 16 * 16;
+}
 size_t route_batch_smem(int E, int H) {
-  return size_t(E) * (H / 2) + size_t(E) * (H / 32) + size_t(kBatchWarps) * (H / 2 + H / 32) +
-         size_t(kBatchWarps) * E * sizeof(float) + 64;
+  return size_t(E) * (H / 2) + size_t(E) * (H / 32) +
+         size_t(kBatchWarps) * kBatchTok * route_batch_slot(E, H) + 64;
+}
+
+// Quantise token t into (s_xq, s_xsc) with the whole warp (quads of lanes per
+// 32-element block); t < 0: zeros.
+__device__ __forceinline__ void warp_quant_token(const RouteArgs& a, int t, uint8_t* s_xq,
+                                                 uint8_t* s_xsc, int lane) {
+  for (int base = 0; base < (a.H >> 3); base += 32) {
+    const int c8 = base + lane;
+    const bool live = c8 < (a.H >> 3);
+    float v[8];
+    if (live && t >= 0) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(
+          reinterpret_cast<const __nv_bfloat16*>(a.x) + long(t) * a.H + c8 * 8);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h2[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+    }
+    BlockScale bs;
+    const uint32_t word = quant_group8(v, bs);
+    if (live) {
+      reinterpret_cast<uint32_t*>(s_xq)[c8] = word;
+      if ((c8 & 3) == 0) s_xsc[c8 >> 2] = bs.code;
+    }
+  }
 }
 
 template <int kMaxBlk>
@@ -656,15 +703,11 @@ __global__ void __launch_bounds__(kBatchThreads) route_batch_kernel(RouteArgs a)
   const int nb = a.H >> 5;
   uint8_t* s_w = smem;                                          // [E][H/2]
   uint8_t* s_ws = s_w + size_t(a.E) * (a.H >> 1);               // [E][H/32]
-  uint8_t* s_xq_all = s_ws + size_t(a.E) * nb;                  // [warps][H/2]
-  uint8_t* s_xsc_all = s_xq_all + size_t(kBatchWarps) * (a.H >> 1);
-  float* s_lg_all = reinterpret_cast<float*>(
-      (reinterpret_cast<uintptr_t>(s_xsc_all + size_t(kBatchWarps) * nb) + 15) & ~uintptr_t(15));
+  uint8_t* s_slots = s_ws + size_t(a.E) * nb;                   // [warps][tok][slot]
+  const size_t slot = route_batch_slot(a.E, a.H);
+  const size_t row_bytes = a.H / 2 > a.E * 4 ? size_t(a.H / 2) : size_t(a.E) * 4;
   __shared__ __align__(8) uint64_t s_bar;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  uint8_t* s_xq = s_xq_all + size_t(warp) * (a.H >> 1);
-  uint8_t* s_xsc = s_xsc_all + size_t(warp) * nb;
-  float* s_lg = s_lg_all + size_t(warp) * a.E;
 
   const uint32_t w_bytes = uint32_t(a.E) * uint32_t(a.H >> 1);
   const uint32_t sc_bytes = uint32_t(a.E) * uint32_t(nb);
@@ -682,79 +725,85 @@ __global__ void __launch_bounds__(kBatchThreads) route_batch_kernel(RouteArgs a)
   const bool have_w = tc::mbar_wait(&s_bar, 0, a.err, 6);
   __syncthreads();
 
-  for (int t = blockIdx.x * kBatchWarps + warp; t < a.T; t += gridDim.x * kBatchWarps) {
-    // ---- quantise token t (quads of lanes per 32-element block) ----------
-    for (int base = 0; base < (a.H >> 3); base += 32) {
-      const int c8 = base + lane;
-      const bool live = c8 < (a.H >> 3);
-      float v[8];
-      if (live) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(
-            reinterpret_cast<const __nv_bfloat16*>(a.x) + long(t) * a.H + c8 * 8);
-        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+  const int groups = (a.T + kBatchTok - 1) / kBatchTok;
+  for (int grp = blockIdx.x * kBatchWarps + warp; grp < groups; grp += gridDim.x * kBatchWarps) {
+    int tok[kBatchTok];
+    uint32_t xa8[kBatchTok][kMaxBlk][8];
+    int xs[kBatchTok][kMaxBlk];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = __bfloat1622float2(h2[i]);
-          v[2 * i] = f.x;
-          v[2 * i + 1] = f.y;
+    for (int q = 0; q < kBatchTok; ++q) {
+      const int t = grp * kBatchTok + q;
+      tok[q] = t < a.T ? t : -1;
+      uint8_t* s_xq = s_slots + size_t(warp * kBatchTok + q) * slot;
+      uint8_t* s_xsc = s_xq + row_bytes;
+      warp_quant_token(a, tok[q], s_xq, s_xsc, lane);
+      __syncwarp();
+      if (a.xq && tok[q] >= 0) {
+        for (int i = lane; i < (a.H >> 5); i += 32)
+          reinterpret_cast<uint4*>(a.xq + long(tok[q]) * (a.H >> 1))[i] =
+              reinterpret_cast<const uint4*>(s_xq)[i];
+        for (int i = lane; i < nb; i += 32) a.xsc[long(tok[q]) * nb + i] = s_xsc[i];
+      }
+#pragma unroll
+      for (int j = 0; j < kMaxBlk; ++j) {
+        const int bl = lane + 32 * j;
+        if (bl < nb) {
+          const uint4 qv = reinterpret_cast<const uint4*>(s_xq)[bl];
+          nib8_to_i8(qv.x, xa8[q][j][0], xa8[q][j][1]);
+          nib8_to_i8(qv.y, xa8[q][j][2], xa8[q][j][3]);
+          nib8_to_i8(qv.z, xa8[q][j][4], xa8[q][j][5]);
+          nib8_to_i8(qv.w, xa8[q][j][6], xa8[q][j][7]);
+          xs[q][j] = s_xsc[bl];
         }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = 0.0f;
-      }
-      BlockScale bs;
-      const uint32_t word = quant_group8(v, bs);
-      if (live) {
-        reinterpret_cast<uint32_t*>(s_xq)[c8] = word;
-        if ((c8 & 3) == 0) s_xsc[c8 >> 2] = bs.code;
       }
     }
-    __syncwarp();
-    if (a.xq) {
-      for (int i = lane; i < (a.H >> 5); i += 32)
-        reinterpret_cast<uint4*>(a.xq + long(t) * (a.H >> 1))[i] = reinterpret_cast<const uint4*>(s_xq)[i];
-      for (int i = lane; i < nb; i += 32) a.xsc[long(t) * nb + i] = s_xsc[i];
-    }
-    // ---- logits ------------------------------------------------------------
-    uint32_t xa8[kMaxBlk][8];
-    int xs[kMaxBlk];
-#pragma unroll
-    for (int j = 0; j < kMaxBlk; ++j) {
-      const int b = lane + 32 * j;
-      if (b < nb) {
-        const uint4 q = reinterpret_cast<const uint4*>(s_xq)[b];
-        nib8_to_i8(q.x, xa8[j][0], xa8[j][1]);
-        nib8_to_i8(q.y, xa8[j][2], xa8[j][3]);
-        nib8_to_i8(q.z, xa8[j][4], xa8[j][5]);
-        nib8_to_i8(q.w, xa8[j][6], xa8[j][7]);
-        xs[j] = s_xsc[b];
-      }
-    }
-    constexpr int kU = 8;
+    __syncwarp();  // the rows are in registers: their slots now take the logits
+    // ---- logits: kU experts x kBatchTok tokens per pass ---------------------
+    constexpr int kU = MFI_BATCH_U;
+    constexpr int kV = kU * kBatchTok;  // values reduced together, index q * kU + u
     for (int e0 = 0; e0 < a.E; e0 += kU) {
-      double acc[kU];
+      double acc[kV];
+#pragma unroll
+      for (int v = 0; v < kV; ++v) acc[v] = 0.0;
 #pragma unroll
       for (int u = 0; u < kU; ++u) {
         const int e = e0 + u;
-        acc[u] = 0.0;
 #pragma unroll
         for (int j = 0; j < kMaxBlk; ++j) {
-          const int b = lane + 32 * j;
-          if (have_w && e < a.E && b < nb) {
-            const uint4 wv = *reinterpret_cast<const uint4*>(s_w + size_t(e) * (a.H >> 1) + b * 16);
-            const int sdot = block_dot_pre(wv, xa8[j]);
-            acc[u] += double(sdot) * exp2i_d(xs[j] + int(s_ws[e * nb + b]) - 256);
+          const int bl = lane + 32 * j;
+          if (have_w && e < a.E && bl < nb) {
+            const uint4 wv = *reinterpret_cast<const uint4*>(s_w + size_t(e) * (a.H >> 1) + bl * 16);
+            uint32_t w8[8];
+            nib8_to_i8(wv.x, w8[0], w8[1]);
+            nib8_to_i8(wv.y, w8[2], w8[3]);
+            nib8_to_i8(wv.z, w8[4], w8[5]);
+            nib8_to_i8(wv.w, w8[6], w8[7]);
+            const int sc = int(s_ws[e * nb + bl]);
+#pragma unroll
+            for (int q = 0; q < kBatchTok; ++q) {
+              // two independent dp4a chains, then one add (exact integers)
+              int d0 = 0, d1 = 0;
+#pragma unroll
+              for (int i = 0; i < 8; i += 2) {
+                d0 = __dp4a(int(xa8[q][j][i]), int(w8[i]), d0);
+                d1 = __dp4a(int(xa8[q][j][i + 1]), int(w8[i + 1]), d1);
+              }
+              const int sdot = d0 + d1;
+              acc[q * kU + u] += double(sdot) * exp2i_d(xs[q][j] + sc - 256);
+            }
           }
         }
       }
-      int n = kU;
+      // reduce-scatter butterfly over the kV values (same pairwise sums per
+      // value as a full butterfly 16, 8, 4, 2, 1)
+      int n = kV;
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1) {
         if (n > 1) {
           const bool upper = (lane & off) != 0;
           const int h = n >> 1;
 #pragma unroll
-          for (int i = 0; i < kU / 2; ++i) {
+          for (int i = 0; i < kV / 2; ++i) {
             if (i < h) {
               const double send = upper ? acc[i] : acc[i + h];
               const double keep = upper ? acc[i + h] : acc[i];
@@ -766,60 +815,72 @@ __global__ void __launch_bounds__(kBatchThreads) route_batch_kernel(RouteArgs a)
           acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], off);
         }
       }
-      // after 3 halving steps lane l holds expert e0 + (l >> 2)
-      if ((lane & 3) == 0 && e0 + (lane >> 2) < a.E) s_lg[e0 + (lane >> 2)] = float(acc[0]);
+      // after log2(kV) halving steps lane l holds value l >> (5 - log2 kV)
+      constexpr int kLog = kV == 16 ? 4 : (kV == 8 ? 3 : (kV == 4 ? 2 : 1));
+      static_assert(kV == 2 || kV == 4 || kV == 8 || kV == 16, "values per pass");
+      if ((lane & ((32 >> kLog) - 1)) == 0) {
+        const int v = lane >> (5 - kLog);
+        const int q = v / kU, e = e0 + v % kU;
+        if (e < a.E)
+          reinterpret_cast<float*>(s_slots + size_t(warp * kBatchTok + q) * slot)[e] = float(acc[0]);
+      }
     }
     __syncwarp();
-    if (a.logit_bias)
-      for (int e = lane; e < a.E; e += 32) s_lg[e] = __fadd_rn(s_lg[e], a.logit_bias[e]);
-    __syncwarp();
-    if (a.logits)
-      for (int e = lane; e < a.E; e += 32) a.logits[long(t) * a.E + e] = s_lg[e];
-    // ---- top-k: k rounds of warp arg-max ----------------------------------
-    constexpr int kPer = kRouteMaxE / 32;
-    float v[kPer];
-    uint32_t taken = 0;
+    // ---- per token: bias, logits out, top-k, weights, position claims -------
+#pragma unroll 1
+    for (int q = 0; q < kBatchTok; ++q) {
+      const int t = tok[q];
+      if (t < 0) continue;
+      float* s_lg = reinterpret_cast<float*>(s_slots + size_t(warp * kBatchTok + q) * slot);
+      if (a.logit_bias)
+        for (int e = lane; e < a.E; e += 32) s_lg[e] = __fadd_rn(s_lg[e], a.logit_bias[e]);
+      __syncwarp();
+      if (a.logits)
+        for (int e = lane; e < a.E; e += 32) a.logits[long(t) * a.E + e] = s_lg[e];
+      constexpr int kPer = kRouteMaxE / 32;
+      float v[kPer];
+      uint32_t taken = 0;
 #pragma unroll
-    for (int i = 0; i < kPer; ++i) v[i] = (lane + 32 * i < a.E) ? s_lg[lane + 32 * i] : 0.0f;
-    int my_sel = -1;
-    float my_val = 0.0f;
-    for (int j = 0; j < a.k; ++j) {
-      float bv = 0.0f;
-      int bi = -1;
+      for (int i = 0; i < kPer; ++i) v[i] = (lane + 32 * i < a.E) ? s_lg[lane + 32 * i] : 0.0f;
+      int my_sel = -1;
+      float my_val = 0.0f;
+      for (int j = 0; j < a.k; ++j) {
+        float bv = 0.0f;
+        int bi = -1;
 #pragma unroll
-      for (int i = 0; i < kPer; ++i) {
-        const int e = lane + 32 * i;
-        if (e < a.E && !((taken >> i) & 1u) && (bi < 0 || better(v[i], e, bv, bi))) {
-          bv = v[i];
-          bi = e;
+        for (int i = 0; i < kPer; ++i) {
+          const int e = lane + 32 * i;
+          if (e < a.E && !((taken >> i) & 1u) && (bi < 0 || better(v[i], e, bv, bi))) {
+            bv = v[i];
+            bi = e;
+          }
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+          if (oi >= 0 && (bi < 0 || better(ov, oi, bv, bi))) {
+            bv = ov;
+            bi = oi;
+          }
+        }
+        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+        if (lane == j) {
+          my_sel = bi;
+          my_val = bv;
         }
       }
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-        if (oi >= 0 && (bi < 0 || better(ov, oi, bv, bi))) {
-          bv = ov;
-          bi = oi;
-        }
+      const float mx = __shfl_sync(0xffffffffu, my_val, 0);
+      const float pj = lane < a.k ? expf(my_val - mx) : 0.0f;
+      float sum = 0.0f;
+      for (int j = 0; j < a.k; ++j) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, pj, j));
+      if (lane < a.k) {
+        a.topi[long(t) * a.k + lane] = my_sel;
+        a.topw[long(t) * a.k + lane] = __fdiv_rn(pj, sum);
+        if (a.slot_pos) a.slot_pos[long(t) * a.k + lane] = atomicAdd(a.cursor + my_sel, 1);
       }
-      if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-      if (lane == j) {
-        my_sel = bi;
-        my_val = bv;
-      }
+      __syncwarp();
     }
-    // ---- weights: exp(l - max) over the selected, normalised by their sum --
-    const float mx = __shfl_sync(0xffffffffu, my_val, 0);
-    const float pj = lane < a.k ? expf(my_val - mx) : 0.0f;
-    float sum = 0.0f;
-    for (int j = 0; j < a.k; ++j) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, pj, j));
-    if (lane < a.k) {
-      a.topi[long(t) * a.k + lane] = my_sel;
-      a.topw[long(t) * a.k + lane] = __fdiv_rn(pj, sum);
-      if (a.slot_pos) a.slot_pos[long(t) * a.k + lane] = atomicAdd(a.cursor + my_sel, 1);
-    }
-    __syncwarp();
   }
 }
 
@@ -836,7 +897,7 @@ static cudaError_t launch_route_batch(const RouteArgs& a, cudaStream_t stream) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int need = (a.T + kBatchWarps - 1) / kBatchWarps;
+  const int need = (a.T + kBatchWarps * kBatchTok - 1) / (kBatchWarps * kBatchTok);
   route_batch_kernel<kMaxBlk><<<need < sms ? need : sms, kBatchThreads, smem, stream>>>(a);
   return cudaGetLastError();
 }
@@ -875,7 +936,7 @@ cudaError_t launch_route(const RouteArgs& a, cudaStream_t stream) {
   if (!a.g_gu) {
     // many tokens, placement by position claims, router fits in shared
     // memory: one router copy per CTA, one token per warp
-    if (a.batch && !a.xp && !a.ep.table && route_batch_smem(a.E, a.H) <= 200 * 1024 &&
+    if (a.batch && !a.xp && !a.ep.table && route_batch_smem(a.E, a.H) <= 220 * 1024 &&
         (size_t(a.E) * (a.H >> 5)) % 16 == 0 && (reinterpret_cast<uintptr_t>(a.wr) & 15) == 0)
       return a.H <= 2048 ? launch_route_batch<2>(a, stream) : launch_route_batch<4>(a, stream);
     // routing alone, or routing + expert regions for the tensor-core kernels

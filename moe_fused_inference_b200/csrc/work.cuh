@@ -190,7 +190,7 @@ struct PrefillLaunch {
   const uint8_t* xp; const uint8_t* xa;   // token rows and their 128-row scale atoms
   uint8_t* hp; uint8_t* ha;               // requantised h rows and atoms
   float* yd;                     // (pairs, H) per-(token, slot) down rows
-  int* err; int* queue; unsigned* ready;
+  int* err; int* queue; unsigned* gu_done; unsigned* ready;
   bool pdl;
 };
 size_t prefill_rows(int pairs, int E);
