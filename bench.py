@@ -327,6 +327,31 @@ def run_prefill(args, world, rank, local):
     tflops = flops / (ms_per_step / 1e3) / 1e12
     counts = torch.bincount(topi[0].flatten().long(), minlength=E).float()
     fp4_peak = 9000.0  # dense MXFP4 tensor peak, nominal (no measured FP4 figure on this pool)
+
+    # ---- dense mxfp4_linear of the attention projections at T tokens (config 3):
+    # lin_pq on pre-quantised activations (the GEMM incl. its scale re-layout)
+    from moe_fused_inference_b200 import fp4_ext
+    from moe_fused_inference_b200.layer import quantize_rows
+    dec = fp4_ext.get_decode_ext()
+    dense = {}
+    del X, out
+    torch.cuda.empty_cache()
+    for name, (n_out, k_in) in {"q": (4096, 2048), "k": (512, 2048), "v": (512, 2048),
+                                "o": (2048, 4096)}.items():
+        wq, wsc = quantize_rows((torch.randn((n_out, k_in), generator=g, device=dev) * 0.02).bfloat16())
+        xq, xsc = quantize_rows(torch.randn((T, k_in), generator=g, device=dev).bfloat16())
+        for _ in range(2):
+            dec.lin_pq(xq, xsc, wq, wsc, T, n_out, k_in)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(5):
+            dec.lin_pq(xq, xsc, wq, wsc, T, n_out, k_in)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) / 5 * 1e3
+        dense[name] = {"us": us, "tflops": 2.0 * T * n_out * k_in / us / 1e6}
+        del wq, wsc, xq, xsc
     if rank != 0:
         return
     line = {
@@ -343,7 +368,10 @@ def run_prefill(args, world, rank, local):
         "gpu_launches": 5 * NL * args.steps,  # route, scatter, experts, combine (+ memset)
         "roofline": {"bound": "tensor", "achieved": tflops, "peak": fp4_peak, "unit": "TFLOP/s",
                      "frac": tflops / fp4_peak, "peak_kind": "nominal dense FP4 (no measured FP4 peak)",
-                     "flops_per_layer": flop_tok * T},
+                     "flops_per_layer": flop_tok * T,
+                     "dense_projections": {k: {"us": v["us"], "tflops": v["tflops"],
+                                               "frac": v["tflops"] / fp4_peak}
+                                           for k, v in dense.items()}},
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
