@@ -469,13 +469,10 @@ cudaError_t launch_prefill_scatter(const uint8_t* xq, const uint8_t* xsc, const 
 
 cudaError_t launch_moe_prefill(const PrefillLaunch& L, cudaStream_t stream) {
   if (L.queue == nullptr || L.ready == nullptr || L.gu_done == nullptr) return cudaErrorInvalidValue;
-  static bool smem_set = false;
-  if (!smem_set) {
-    cudaError_t e = cudaFuncSetAttribute(moe_prefill_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         int(prefill_smem()));
+  {
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(moe_prefill_kernel),
+                                        prefill_smem());
     if (e != cudaSuccess) return e;
-    smem_set = true;
   }
   const int E = L.E, H = L.H, Mi = L.Mi;
   CUtensorMap tx, th;

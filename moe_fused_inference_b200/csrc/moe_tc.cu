@@ -545,13 +545,10 @@ static unsigned long long cap_prefetch(size_t want, size_t region) {
 
 cudaError_t launch_moe_tc(const MoeTcLaunch& L, cudaStream_t stream) {
   if (L.queue == nullptr || L.ready == nullptr) return cudaErrorInvalidValue;
-  static bool smem_set = false;
-  if (!smem_set) {
-    cudaError_t e = cudaFuncSetAttribute(moe_experts_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         int(moe_tc_smem()));
+  {
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(moe_experts_kernel),
+                                        moe_tc_smem());
     if (e != cudaSuccess) return e;
-    smem_set = true;
   }
   const int E = L.E, H = L.H, Mi = L.Mi;
   CUtensorMap tx, th;

@@ -16,6 +16,7 @@
 #include "mx_common.cuh"
 #include "work.cuh"
 #include "tc_ptx.cuh"
+#include "tmap.cuh"
 
 namespace mfi {
 
@@ -887,12 +888,9 @@ __global__ void __launch_bounds__(kBatchThreads) route_batch_kernel(RouteArgs a)
 template <int kMaxBlk>
 static cudaError_t launch_route_batch(const RouteArgs& a, cudaStream_t stream) {
   const size_t smem = route_batch_smem(a.E, a.H);
-  static size_t smem_set = 0;  // largest dynamic size granted so far
-  if (smem > smem_set) {
-    cudaError_t e = cudaFuncSetAttribute(route_batch_kernel<kMaxBlk>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  {
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(route_batch_kernel<kMaxBlk>), smem);
     if (e != cudaSuccess) return e;
-    smem_set = smem;
   }
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -904,15 +902,11 @@ static cudaError_t launch_route_batch(const RouteArgs& a, cudaStream_t stream) {
 
 template <int kMaxBlk>
 static cudaError_t launch_route_cluster(const RouteArgs& a, cudaStream_t stream) {
-  static bool smem_set = false;
   const int n_split = (a.E + kExpertsPerCta - 1) / kExpertsPerCta;  // <= 8
   const size_t smem = size_t(kExpertsPerCta) * (a.H >> 1);
-  if (!smem_set) {
-    cudaError_t e = cudaFuncSetAttribute(route_cluster_kernel<kMaxBlk>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kExpertsPerCta * (kMaxBlk * 32 * 16));
+  {
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(route_cluster_kernel<kMaxBlk>), smem);
     if (e != cudaSuccess) return e;
-    smem_set = true;
   }
   cudaLaunchConfig_t cfg{};
   const int clusters = a.ep.table ? (a.T > 0 ? a.T : 1) : a.T;

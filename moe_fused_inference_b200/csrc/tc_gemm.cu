@@ -262,13 +262,10 @@ cudaError_t launch_tc_gemm(const uint8_t* a, const uint8_t* sfa_atoms, const uin
   if (!make_tmap(&ta, a, uint64_t(Kp / 2), uint64_t(M), kBM) ||
       !make_tmap(&tb, b, uint64_t(Kp / 2), uint64_t(N), kBN))
     return cudaErrorInvalidValue;
-  static bool attr_set = false;
   const size_t smem = tc_gemm_smem_bytes();
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(tc_gemm_mxf4_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  {
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(tc_gemm_mxf4_kernel), smem);
     if (e != cudaSuccess) return e;
-    attr_set = true;
   }
   TcGemmArgs p;
   p.M = M; p.N = N; p.Kp = Kp;

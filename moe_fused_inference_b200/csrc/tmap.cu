@@ -58,4 +58,18 @@ bool get_tmap(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t row
   return true;
 }
 
+cudaError_t ensure_dynamic_smem(const void* fn, size_t bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, size_t> granted;
+  std::lock_guard<std::mutex> g(mu);
+  size_t& have = granted[{dev, fn}];
+  if (have >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+  if (e == cudaSuccess) have = bytes;
+  return e;
+}
+
 }  // namespace mfi
