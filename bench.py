@@ -123,8 +123,15 @@ class ClockSampler:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=self.f, stderr=subprocess.DEVNULL)
+            # sampling must be live before the timed region starts
+            t0 = time.time()
+            while time.time() - t0 < 5.0 and self.proc.poll() is None:
+                self.f.flush()
+                if os.path.getsize(self.path) > 0:
+                    break
+                time.sleep(0.02)
         except Exception:
             self.proc = None
 

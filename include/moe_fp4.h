@@ -192,6 +192,14 @@ int mfi_moe_prepare(const mfi_moe_weights* w, void* prepared, size_t prepared_by
  * (needs hidden and inter multiples of 256).  Both combine a token's slots
  * in slot order with unfused fp32 multiply and add. */
 size_t mfi_moe_layer_workspace_bytes(int T, int hidden, int inter, int n_experts, int top_k);
+/* The decode tensor-core path keeps per-call counters in the workspace (so a
+ * layer call needs no memset node): initialise a workspace once with
+ * mfi_moe_layer_init_workspace for its (T, shape) and pass it unchanged to
+ * every call with that T; each call leaves the counters zeroed.  A workspace
+ * that was not initialised gives wrong results and device error 5, never an
+ * out-of-bounds write. */
+int mfi_moe_layer_init_workspace(void* workspace, size_t workspace_bytes, int T, int hidden,
+                                 int inter, int n_experts, int top_k, void* stream);
 int mfi_moe_layer(const mfi_moe_weights* w, const void* x_bf16, int T, float* out, int32_t* topi,
                   float* topw, float* logits, void* workspace, size_t workspace_bytes,
                   void* stream);
@@ -344,7 +352,10 @@ int mfi_ep_route_dispatch(const mfi_moe_weights* w, const void* x_bf16, int T, i
 
 /* Wait for every rank's dispatch, run the local experts (`w`: this rank's
  * E/n experts, prepared) on the received rows and send each row's weighted
- * slot sum back to its source.  n_ranks * (capacity + 1) * top_k <= 16384. */
+ * slot sum back to its source.  n_ranks * (capacity + 1) * top_k <= 16384.
+ * The workspace keeps counters between calls: zero it before the first call
+ * and pass the same one, unchanged, to every call of this exchange (each call
+ * leaves its counters at zero, as mfi_ep_unpack_wait does for the flags). */
 size_t mfi_ep_experts_workspace_bytes(int n_ranks, int capacity, int hidden, int inter,
                                       int local_experts, int top_k);
 int mfi_ep_experts_return(const mfi_moe_weights* w, int rank, int n_ranks, int capacity,

@@ -41,6 +41,7 @@ SIGNATURES = {
     "mfi_moe_prepared_bytes": (_SZ, [_I, _I, _I]),
     "mfi_moe_prepare": (_I, [_VP, _VP, _SZ, _VP]),
     "mfi_moe_layer_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
+    "mfi_moe_layer_init_workspace": (_I, [_VP, _SZ, _I, _I, _I, _I, _I, _VP]),
     "mfi_moe_layer": (_I, [_VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _SZ, _VP]),
     "mfi_moe_layer_ex": (_I, [_VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _SZ, _VP, _I, _VP]),
     "mfi_moe_route": (_I, [_VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _VP]),

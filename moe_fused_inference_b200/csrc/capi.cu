@@ -523,6 +523,19 @@ size_t mfi_moe_layer_workspace_bytes(int T, int hidden, int inter, int n_experts
   return carve_layer(nullptr, T, hidden, inter, n_experts, top_k).bytes;
 }
 
+int mfi_moe_layer_init_workspace(void* workspace, size_t workspace_bytes, int T, int hidden,
+                                 int inter, int n_experts, int top_k, void* stream) {
+  if (bad_ptr(workspace)) return fail(MFI_ERR_ARG, "null pointer");
+  if (T <= 0 || hidden <= 0 || inter <= 0 || n_experts <= 0 || top_k <= 0)
+    return fail(MFI_ERR_ARG, "invalid shape");
+  if (workspace_bytes < mfi_moe_layer_workspace_bytes(T, hidden, inter, n_experts, top_k))
+    return fail(MFI_ERR_WORKSPACE, "workspace too small for moe_layer");
+  if (use_prefill(T, hidden, inter, top_k)) return MFI_OK;  // zeroed per call
+  LayerScratch s = carve_layer(workspace, T, hidden, inter, n_experts, top_k);
+  return cuda_status(cudaMemsetAsync(s.done, 0, sizeof(unsigned) * s.zero_words, as_stream(stream)),
+                     "moe_layer_init_workspace memset");
+}
+
 int mfi_moe_layer(const mfi_moe_weights* w, const void* x_bf16, int T, float* out, int32_t* topi,
                   float* topw, float* logits, void* workspace, size_t workspace_bytes,
                   void* stream) {
@@ -577,13 +590,18 @@ int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float*
   };
   int rc = mark(0);
   if (rc != MFI_OK) return rc;
-  rc = cuda_status(cudaMemsetAsync(s.done, 0, sizeof(unsigned) * s.zero_words, st),
-                   "moe_layer memset");
-  if (rc != MFI_OK) return rc;
+  const bool tc = layer_uses_tc(H, Mi);
+  if (!tc) {
+    // CUDA-core path: counters zeroed per call
+    rc = cuda_status(cudaMemsetAsync(s.done, 0, sizeof(unsigned) * s.zero_words, st),
+                     "moe_layer memset");
+    if (rc != MFI_OK) return rc;
+  }
+  // tensor-core path: the counters were zeroed by mfi_moe_layer_init_workspace
+  // and every call's combine clears them again (no memset node per layer)
   if ((reinterpret_cast<uintptr_t>(x_bf16) & 15) != 0 ||
       (reinterpret_cast<uintptr_t>(w->router_wp) & 15) != 0)
     return fail(MFI_ERR_ARG, "x and router_wp must be 16-byte aligned");
-  const bool tc = layer_uses_tc(H, Mi);
   mfi::RouteArgs ra{};
   ra.x = x_bf16;
   ra.xq = s.xq; ra.xsc = s.xsc; ra.wr = w->router_wp; ra.sr = w->router_sc;
@@ -648,7 +666,8 @@ int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float*
                      "moe_layer down launch");
     if (rc != MFI_OK || (rc = mark(4)) != MFI_OK) return rc;
   }
-  rc = cuda_status(mfi::launch_combine(s.yd, H, topw, k, k, out, T, H, st, tc && !events),
+  rc = cuda_status(mfi::launch_combine(s.yd, H, topw, k, k, out, T, H, st, tc && !events,
+                                       tc ? s.done : nullptr, tc ? int(s.zero_words) : 0),
                    "moe_layer combine launch");
   if (rc != MFI_OK) return rc;
   return mark(5);
@@ -958,10 +977,8 @@ int mfi_ep_route_dispatch(const mfi_moe_weights* w, const void* x_bf16, int T, i
     return fail(MFI_ERR_ARG, "x and router_wp must be 16-byte aligned");
   cudaStream_t st = as_stream(stream);
   unsigned* fl = static_cast<unsigned*>(flags);
-  rc = cuda_status(cudaMemsetAsync(fl + mfi::kFlagZeroFirst, 0,
-                                   sizeof(unsigned) * (mfi::kFlagWords - mfi::kFlagZeroFirst), st),
-                   "ep_route_dispatch memset");
-  if (rc != MFI_OK) return rc;
+  // the per-call counters are zero: mfi_ipc_alloc zeroes the flag area and
+  // every call's mfi_ep_unpack_wait clears them again
   mfi::RouteArgs ra{};
   ra.x = x_bf16; ra.wr = w->router_wp; ra.sr = w->router_sc;
   ra.T = T; ra.H = H; ra.E = E; ra.k = k;
@@ -1002,9 +1019,8 @@ int mfi_ep_experts_return(const mfi_moe_weights* w, int rank, int n_ranks, int c
   cudaStream_t st = as_stream(stream);
   const mfi::EpTable* tb = static_cast<const mfi::EpTable*>(table);
   unsigned* fl = static_cast<unsigned*>(flags);
-  rc = cuda_status(cudaMemsetAsync(s.cursor, 0, sizeof(int) * s.zero_words, st),
-                   "ep_experts_return memset");
-  if (rc != MFI_OK) return rc;
+  // cursors, work counter and readiness counters are zero (workspace zeroed
+  // before the first call; each call's combine/return kernel clears them)
   rc = cuda_status(mfi::launch_ep_scatter_wait(tb, fl, recv, rank, n_ranks, capacity, H, k, E,
                                                s.T_pad, s.cursor, s.perm, s.xp, s.xp_atoms,
                                                mfi::device_error_flag(), st),
@@ -1028,7 +1044,8 @@ int mfi_ep_experts_return(const mfi_moe_weights* w, int rank, int n_ranks, int c
   rc = cuda_status(mfi::launch_moe_tc(L, st), "ep_experts_return experts launch");
   if (rc != MFI_OK) return rc;
   return cuda_status(mfi::launch_ep_combine_return(tb, fl, s.yd, recv, rank, n_ranks, capacity, H,
-                                                   k, E, mfi::device_error_flag(), st),
+                                                   k, E, s.cursor, int(s.zero_words),
+                                                   mfi::device_error_flag(), st),
                      "ep_experts_return combine launch");
 }
 

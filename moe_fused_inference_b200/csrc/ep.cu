@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(128) ep_scatter_wait_kernel(
 __global__ void __launch_bounds__(128) ep_combine_return_kernel(
     const EpTable* __restrict__ table, unsigned* __restrict__ flags, const float* __restrict__ yd,
     const uint8_t* __restrict__ recv, int rank, int n, int C, RowLayout L, int E,
-    int* __restrict__ err) {
+    int* __restrict__ ws_counters, int n_counters, int* __restrict__ err) {
   tc::grid_dep_wait();  // yd comes from the expert kernel
   const unsigned call = current_call(flags);
   const int R = n * (C + 1);
@@ -357,10 +357,17 @@ __global__ void __launch_bounds__(128) ep_combine_return_kernel(
     }
     __syncthreads();
   }
-  // release: every thread's stores precede thread 0's system fence
+  // Release: every thread's stores precede thread 0's fence (bar.sync); a
+  // GPU-scope fence orders them before this CTA's count, and the last CTA's
+  // system-scope fence (cumulative over everything that happened before it on
+  // this GPU) orders them all before the flags the peers poll.  One system
+  // fence per call instead of one per CTA.
   if (threadIdx.x != 0) return;
-  __threadfence_system();
+  __threadfence();
   if (atomicAdd(flags + kFlagDone + 1, 1u) != gridDim.x - 1) return;
+  // the expert launch and the scatter are complete (programmatic wait at the
+  // top): their counters start the next call at zero
+  for (int i = 0; i < n_counters; ++i) ws_counters[i] = 0;
   __threadfence_system();
   for (int d = 0; d < n; ++d) tc::st_relaxed_sys(table->flags[d] + kFlagReturn + rank, call);
 }
@@ -395,8 +402,13 @@ __global__ void __launch_bounds__(128) ep_unpack_wait_kernel(
     for (int c4 = threadIdx.x * 4; c4 < H; c4 += blockDim.x * 4)
       *reinterpret_cast<float4*>(out + size_t(t) * H + c4) = ordered_sum4<true>(s_rows, nullptr, s_m, c4);
   __syncthreads();
-  if (threadIdx.x == 0 && atomicAdd(flags + kFlagDone + 2, 1u) == gridDim.x - 1)
+  if (threadIdx.x == 0 && atomicAdd(flags + kFlagDone + 2, 1u) == gridDim.x - 1) {
+    // last CTA of the call's last kernel: clear the per-call counters for the
+    // next call (nothing of this call reads them any more), then close it
+    for (int i = kFlagZeroFirst; i < kFlagWords; ++i) flags[i] = 0u;
+    __threadfence();
     atomicAdd(flags + kFlagEpoch, 1u);
+  }
 }
 
 }  // namespace
@@ -415,11 +427,12 @@ cudaError_t launch_ep_scatter_wait(const EpTable* table, unsigned* flags, uint8_
 
 cudaError_t launch_ep_combine_return(const EpTable* table, unsigned* flags, const float* yd,
                                      const uint8_t* recv, int rank, int n, int C, int H, int k,
-                                     int E, int* err, cudaStream_t stream) {
+                                     int E, int* ws_counters, int n_counters, int* err,
+                                     cudaStream_t stream) {
   RowLayout L{H, k, ep_row_bytes(H, k)};
   const int R = n * (C + 1);
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(R < 296 ? R : 296);
+  cfg.gridDim = dim3(R);  // one received row per CTA
   cfg.blockDim = dim3(128);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -428,7 +441,7 @@ cudaError_t launch_ep_combine_return(const EpTable* table, unsigned* flags, cons
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, ep_combine_return_kernel, table, flags, yd, recv, rank, n, C, L,
-                            E, err);
+                            E, ws_counters, n_counters, err);
 }
 
 cudaError_t launch_ep_unpack_wait(unsigned* flags, const float* ret, const int* pack_pos, int T,

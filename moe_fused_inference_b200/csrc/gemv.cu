@@ -287,8 +287,12 @@ cudaError_t launch_build_groups(const uint8_t* const* wp_tab, const uint8_t* con
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ yd, long ystride,
                                                       const float* __restrict__ w, int E, int E_sum,
-                                                      float* __restrict__ out, int M, int N) {
+                                                      float* __restrict__ out, int M, int N,
+                                                      unsigned* __restrict__ clear, int n_clear) {
   tc::grid_dep_wait();  // yd comes from the previous kernel
+  // the layer's per-call counters: every kernel that used them has completed
+  if (clear && blockIdx.x == 0 && blockIdx.y == 0)
+    for (int i = threadIdx.x; i < n_clear; i += blockDim.x) clear[i] = 0u;
   const int m = blockIdx.y;
   const int c4 = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (m >= M || c4 >= N) return;
@@ -315,7 +319,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
 }
 
 cudaError_t launch_combine(const float* yd, long ystride, const float* w, int E, int E_sum,
-                           float* out, int M, int N, cudaStream_t stream, bool pdl) {
+                           float* out, int M, int N, cudaStream_t stream, bool pdl,
+                           unsigned* clear, int n_clear) {
   if (M == 0 || N == 0) return cudaSuccess;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((N / 4 + 255) / 256 + 1, M);
@@ -326,7 +331,8 @@ cudaError_t launch_combine(const float* yd, long ystride, const float* w, int E,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, combine_kernel, yd, ystride, w, E, E_sum, out, M, N);
+  return cudaLaunchKernelEx(&cfg, combine_kernel, yd, ystride, w, E, E_sum, out, M, N, clear,
+                            n_clear);
 }
 
 }  // namespace mfi

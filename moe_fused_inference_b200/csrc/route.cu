@@ -189,9 +189,14 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
         // claim a row in each selected expert's region
         const int e = s_sel[lane];
         const int pos = atomicAdd(a.cursor + e, 1);
-        const int row = e * a.T_pad + pos;
+        int row = -1;
+        if (pos < a.T_pad) {
+          row = e * a.T_pad + pos;
+          a.perm[row] = t * a.k + lane;
+        } else if (a.err) {
+          atomicCAS(a.err, 0, 5);  // cursors not zero at entry
+        }
         s_row[lane] = row;
-        a.perm[row] = t * a.k + lane;
       }
     }
   }
@@ -201,6 +206,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
     const int q16 = a.H >> 5;  // uint4 per row
     for (int i = threadIdx.x; i < a.k * q16; i += kRouteThreads) {
       const int j = i / q16, c = i % q16;
+      if (s_row[j] < 0) continue;
       reinterpret_cast<uint4*>(a.xp + size_t(s_row[j]) * (a.H >> 1))[c] =
           reinterpret_cast<const uint4*>(s_xq)[c];
     }
@@ -208,6 +214,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
     for (int i = threadIdx.x; i < a.k * kc; i += kRouteThreads) {
       const int j = i / kc, c = i % kc;
       const int row = s_row[j];
+      if (row < 0) continue;
       *reinterpret_cast<uint32_t*>(a.xp_atoms + (size_t(row >> 5) * kc + c) * 512 + (row & 31) * 16) =
           reinterpret_cast<const uint32_t*>(s_xsc)[c];
     }
@@ -367,7 +374,9 @@ __device__ void ep_finish_dispatch(const EpDispatch& ep, int H, int k, int n_lea
   __shared__ int s_last;
   __syncthreads();  // every thread's row stores precede thread 0's fence
   if (threadIdx.x == 0) {
-    __threadfence_system();
+    // GPU-scope release per leader; the last leader's system-scope fences
+    // below are cumulative over every leader's rows
+    __threadfence();
     s_last = atomicAdd(ep.flags + kFlagDone + 0, 1u) == unsigned(n_leaders - 1);
     if (s_last) __threadfence_system();  // the other leaders' rows and counts
   }
@@ -577,9 +586,14 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
       if (a.xp) {
         const int e = s_sel[lane];
         const int pos = atomicAdd(a.cursor + e, 1);
-        const int row = e * a.T_pad + pos;
+        int row = -1;
+        if (pos < a.T_pad) {
+          row = e * a.T_pad + pos;
+          a.perm[row] = t * a.k + lane;
+        } else if (a.err) {
+          atomicCAS(a.err, 0, 5);  // cursors not zero at entry
+        }
         s_row[lane] = row;
-        a.perm[row] = t * a.k + lane;
       }
     }
   }
@@ -623,6 +637,7 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
     const int q16 = a.H >> 5;
     for (int i = threadIdx.x; i < a.k * q16; i += kClusterThreads) {
       const int j = i / q16, c = i % q16;
+      if (s_row[j] < 0) continue;
       reinterpret_cast<uint4*>(a.xp + size_t(s_row[j]) * (a.H >> 1))[c] =
           reinterpret_cast<const uint4*>(s_xq)[c];
     }
@@ -630,6 +645,7 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
     for (int i = threadIdx.x; i < a.k * kc; i += kClusterThreads) {
       const int j = i / kc, c = i % kc;
       const int row = s_row[j];
+      if (row < 0) continue;
       *reinterpret_cast<uint32_t*>(a.xp_atoms + (size_t(row >> 5) * kc + c) * 512 + (row & 31) * 16) =
           reinterpret_cast<const uint32_t*>(s_xsc)[c];
     }

@@ -124,8 +124,11 @@ cudaError_t launch_dense_gemv(const uint8_t* xq, const uint8_t* xsc, const uint8
 cudaError_t launch_build_groups(const uint8_t* const* wp_tab, const uint8_t* const* wsc_tab, int P,
                                 int mode, int E, int N, GroupDesc* groups, int* n_groups,
                                 EntryDesc* entries, cudaStream_t stream);
+// clear/n_clear: counters zeroed by the launch once the previous kernel is
+// complete (the fused layer's per-call counters), or null
 cudaError_t launch_combine(const float* yd, long ystride, const float* w, int E, int E_sum,
-                           float* out, int M, int N, cudaStream_t stream, bool pdl = false);
+                           float* out, int M, int N, cudaStream_t stream, bool pdl = false,
+                           unsigned* clear = nullptr, int n_clear = 0);
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t stream);
 
 // tcgen05 MXFP4 GEMM (tc_gemm.cu)
@@ -207,7 +210,8 @@ cudaError_t launch_ep_scatter_wait(const EpTable* table, unsigned* flags, uint8_
                                    cudaStream_t stream);
 cudaError_t launch_ep_combine_return(const EpTable* table, unsigned* flags, const float* yd,
                                      const uint8_t* recv, int rank, int n, int C, int H, int k,
-                                     int E, int* err, cudaStream_t stream);
+                                     int E, int* ws_counters, int n_counters, int* err,
+                                     cudaStream_t stream);
 cudaError_t launch_ep_unpack_wait(unsigned* flags, const float* ret, const int* pack_pos, int T,
                                   int n, int C, int H, float* out, int* err, cudaStream_t stream);
 

@@ -169,7 +169,9 @@ class CudaEPOps:
                                        _stream(dev)), "moe_prepare")
         self.R = world * (capacity + 1)
         nws = int(lib.mfi_moe_experts_workspace_bytes(self.R, H, Mi, El, top_k))
-        self.ws = torch.empty(nws, dtype=torch.uint8, device=dev)
+        # zero once: the peer-memory transport keeps its counters here between
+        # calls (each call leaves them at zero)
+        self.ws = torch.zeros(nws, dtype=torch.uint8, device=dev)
 
     def route(self, x, xq, xsc, topi, topw, logits=None):
         T = x.shape[0]

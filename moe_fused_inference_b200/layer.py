@@ -175,7 +175,11 @@ class MoELayer:
     def _workspace(self, T: int, device) -> torch.Tensor:
         ws = self._ws.get(T)
         if ws is None:
+            lib = _lib.load()
             ws = torch.empty(self.workspace_bytes(T), dtype=torch.uint8, device=device)
+            _lib.check(lib.mfi_moe_layer_init_workspace(
+                ws.data_ptr(), ws.numel(), T, self.w.hidden, self.w.inter, self.w.n_experts,
+                self.top_k, _stream(device)), "moe_layer_init_workspace")
             self._ws[T] = ws
         return ws
 
