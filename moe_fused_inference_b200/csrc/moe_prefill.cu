@@ -42,11 +42,15 @@ namespace {
 #define MFI_PF_STAGES 5
 #endif
 constexpr int kPStages = MFI_PF_STAGES;
-// warp 0 loads, warp 1 issues MMAs, warps 2-17 run the epilogue: four warps
-// per TMEM lane quadrant, each taking a quarter of the tile's columns (the
-// SwiGLU epilogue is latency-bound: with fewer warps it, not the MMA, sets
-// the pace of the gate/up items)
+// warp 0 loads, warp 1 issues MMAs, warps 2-17 run the epilogue in two
+// independent groups of eight: group g takes the accumulators of items
+// g, g + 2, g + 4, ... of the CTA, so one group's SwiGLU overlaps the other's
+// (no CTA-wide barrier between items).  Inside a group two warps share each
+// TMEM lane quadrant, each taking one 32-element block of h (gate/up) or 64
+// output columns (down) of its 32 token rows.
 constexpr int kPEpiWarps = 16;
+constexpr int kPGroups = 2;
+constexpr int kPGroupWarps = kPEpiWarps / kPGroups;
 constexpr int kPThreads = 64 + 32 * kPEpiWarps;
 constexpr int kPTile = 128;                    // token rows per tile (MMA M)
 constexpr int kPA = 16384;                     // 128 token rows x 128 B
@@ -77,13 +81,10 @@ struct PrefillArgs {
   int hidden, inter, top_k;
   int* err;
   int* queue;                  // work-item counter, zero before the launch
-  unsigned* gu_done;           // finished gate/up items in all, zero before the launch
-  unsigned* ready;             // per tile: finished gate/up items, zero before the launch
+  unsigned* gu_done;           // finished gate/up warp slices in all, zero before the launch
+  unsigned* ready;             // per tile: finished gate/up warp slices, zero before the launch
 };
 
-__device__ __forceinline__ void named_bar_sync(int id, int n) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
 __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
@@ -163,7 +164,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
   uint64_t* item_empty = item_full + kPAccBufs;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_empty + kPAccBufs);
   __shared__ int s_item[kPAccBufs];
-  __shared__ float s_am[4][kPTile];  // gate/up epilogue: partial block maxima per quarter
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_gu = p.inter / 64, tiles_dn = p.hidden / 128;
@@ -177,9 +177,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
     for (int b = 0; b < kPAccBufs; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], kPEpiWarps);
+      mbar_init(&acc_empty[b], kPGroupWarps);
       mbar_init(&item_full[b], 1);
-      mbar_init(&item_empty[b], 1 + kPEpiWarps);  // the MMA thread + the epilogue warps
+      mbar_init(&item_empty[b], 1 + kPGroupWarps);  // the MMA thread + one epilogue group
     }
     fence_mbar_init();
   }
@@ -247,13 +247,18 @@ __global__ void __launch_bounds__(kPThreads, 1)
       bool all_ready = false;  // every gate/up item has published its h rows
       int item = first_item;
       int next = atomicAdd(p.queue, 1);  // items are claimed two ahead
+      int stops = 0;
       for (uint32_t qi = 0; ok; ++qi) {
         const uint32_t slot = qi % kPAccBufs;
         if (!mbar_wait(&item_empty[slot], ((qi / kPAccBufs) & 1) ^ 1, p.err, 1)) break;
         if (item >= n_items) item = -1;
         s_item[slot] = item;
         mbar_arrive(&item_full[slot]);
-        if (item < 0) break;
+        if (item < 0) {
+          // one end marker per epilogue group (consecutive slots)
+          if (++stops == kPGroups) break;
+          continue;
+        }
         const int next2 = atomicAdd(p.queue, 1);
         bool gu;
         int tl, tile, e, row0, count;
@@ -264,12 +269,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
           wb = p.w_gu + (size_t(e) * tiles_gu + tile) * ks_gu * size_t(kPW);
         } else {
           wb = p.w_dn + (size_t(e) * tiles_dn + tile) * ks_dn * size_t(kPW);
-          if (!all_ready && ld_acquire_u32(p.gu_done) >= unsigned(n_gu)) all_ready = true;
-          if (!all_ready && ld_acquire_u32(p.ready + tl) < unsigned(tiles_gu)) {
+          const unsigned tile_slices = unsigned(tiles_gu) * kPGroupWarps;
+          if (!all_ready && ld_acquire_u32(p.gu_done) >= unsigned(n_gu) * kPGroupWarps)
+            all_ready = true;
+          if (!all_ready && ld_acquire_u32(p.ready + tl) < tile_slices) {
             const uint64_t t0 = globaltimer_ns();
             for (uint32_t i = 1;; ++i) {
               __nanosleep(64);
-              if (ld_acquire_u32(p.ready + tl) >= unsigned(tiles_gu)) break;
+              if (ld_acquire_u32(p.ready + tl) >= tile_slices) break;
               if ((i & 255u) == 0 && (*reinterpret_cast<volatile int*>(p.err) != 0 ||
                                       globaltimer_ns() - t0 > kWaitLimitNs)) {
                 atomicCAS(p.err, 0, 4);
@@ -302,6 +309,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     if (elect_one()) {
       uint32_t it = 0;
       bool ok = true;
+      int stops = 0;
       for (uint32_t acc_it = 0; ok; ++acc_it) {
         const uint32_t buf = acc_it % kPAccBufs;
         if (!mbar_wait(&item_full[buf], (acc_it / kPAccBufs) & 1, p.err, 2)) break;
@@ -310,7 +318,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
         if (!mbar_wait(&acc_empty[buf], ((acc_it / kPAccBufs) & 1) ^ 1, p.err, 2)) { ok = false; break; }
         if (item < 0) {
           mbar_arrive(&acc_full[buf]);
-          break;
+          if (++stops == kPGroups) break;
+          continue;
         }
         const int ksn = item < n_gu ? ks_gu : ks_dn;
         tc_fence_after();
@@ -343,11 +352,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
       }
     }
   } else {
-    const int quad = warp & 3;          // TMEM lane quadrant of this warp
-    const int et = threadIdx.x - 64;    // 0..511
-    const int part = et >> 7;           // which quarter of the tile's columns
-    const int r = quad * 32 + lane;     // token row inside the tile
-    for (uint32_t acc_it = 0;; ++acc_it) {
+    const int ew = warp - 2;             // 0..15
+    const int quad = warp & 3;           // TMEM lane quadrant of this warp
+    const int grp = ew / kPGroupWarps;   // epilogue group
+    const int half = (ew >> 2) & 1;      // which half of the tile's columns
+    const int r = quad * 32 + lane;      // token row inside the tile
+    for (uint32_t acc_it = grp;; acc_it += kPGroups) {
       const uint32_t buf = acc_it % kPAccBufs;
       if (!mbar_wait(&item_full[buf], (acc_it / kPAccBufs) & 1, p.err, 3)) break;
       const int item = s_item[buf];
@@ -369,69 +379,63 @@ __global__ void __launch_bounds__(kPThreads, 1)
       const uint32_t tbase = tmem + (uint32_t(quad * 32) << 16) + buf * 128;
       if (gu) {
         // columns 0-63: gate outputs tile*64 + c, 64-127: the same up outputs;
-        // this warp takes outputs part*16 .. +15 (half of 32-element block
-        // part/2), its partner warp (part^1) the other half
-        uint32_t g[16], u[16];
-        tmem_ld_32x32b_x16(tbase + part * 16, g);
-        tmem_ld_32x32b_x16(tbase + 64 + part * 16, u);
+        // this warp takes h block `half` (outputs half*32 .. +31) whole, so
+        // the block maximum needs no exchange with another warp
+        uint32_t g[32], u[32];
+        tmem_ld_32x32b_x32(tbase + half * 32, g);
+        tmem_ld_32x32b_x32(tbase + 64 + half * 32, u);
         tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[buf]);
-        float h[16];
         float am = 0.0f;
         bool nan = false;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float gv = __uint_as_float(g[i]), uv = __uint_as_float(u[i]);
-          h[i] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
-          am = fmaxf(am, fabsf(h[i]));
-          nan |= (h[i] != h[i]);
+        for (int i = 0; i < 32; ++i) {
+          const float h = swiglu_fast(__uint_as_float(g[i]), __uint_as_float(u[i]));
+          g[i] = __float_as_uint(h);
+          am = fmaxf(am, fabsf(h));
+          nan |= (h != h);
         }
-        s_am[part][r] = nan ? __uint_as_float(0x7fc00000u) : am;
-        named_bar_sync(2, 32 * kPEpiWarps);
-        const float other = s_am[part ^ 1][r];
         // a NaN anywhere in the block gives code 127, like quant_group8
-        const float bam = (am != am || other != other) ? __uint_as_float(0x7fc00000u) : fmaxf(am, other);
-        const BlockScale bs = block_scale(nan || other != other ? __uint_as_float(0x7fc00000u) : bam);
-        uint32_t w0 = 0, w1 = 0;
+        const BlockScale bs = block_scale(nan ? __uint_as_float(0x7fc00000u) : am);
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          w0 |= quant_nibble(h[i], bs.inv) << (4 * i);
-          w1 |= quant_nibble(h[8 + i], bs.inv) << (4 * i);
-        }
+        for (int i = 0; i < 32; ++i)
+          w[i >> 3] |= quant_nibble(__uint_as_float(g[i]), bs.inv) << (4 * (i & 7));
         if (valid) {
-          const int b = part >> 1;
-          *reinterpret_cast<uint2*>(p.hp + size_t(row) * (p.inter / 2) + tile * 32 + part * 8) =
-              make_uint2(w0, w1);
-          if ((part & 1) == 0) {
-            const int kb = tile * 2 + b;  // 32-element block of h along inter
-            p.ha[(size_t(row / kPTile) * kc_dn + kb / 4) * 512 + (row % 32) * 16 +
-                 ((row % kPTile) / 32) * 4 + (kb & 3)] = bs.code;
-          }
+          *reinterpret_cast<uint4*>(p.hp + size_t(row) * (p.inter / 2) + tile * 32 + half * 16) =
+              make_uint4(w[0], w[1], w[2], w[3]);
+          const int kb = tile * 2 + half;  // 32-element block of h along inter
+          p.ha[(size_t(row / kPTile) * kc_dn + kb / 4) * 512 + (row % 32) * 16 +
+               ((row % kPTile) / 32) * 4 + (kb & 3)] = bs.code;
         }
-        // publish this 64-column slice of the tile's h rows to its down items
-        // (the barrier also frees s_am for the next item)
-        named_bar_sync(1, 32 * kPEpiWarps);
-        if (et == 0) {
+        // publish this warp's slice (32 rows x one block) of the tile's h
+        // rows to its down items
+        __syncwarp();
+        if (lane == 0) {
           fence_proxy_async_global();
           __threadfence();
           atomicAdd(p.ready + tl, 1u);
           atomicAdd(p.gu_done, 1u);
         }
       } else {
-        // this warp stores output columns part*32 .. +31 of the token rows
-        uint32_t y[32];
-        tmem_ld_32x32b_x32(tbase + part * 32, y);
+        // this warp stores output columns half*64 .. +63 of its token rows
+        uint32_t y[2][32];
+        tmem_ld_32x32b_x32(tbase + half * 64, y[0]);
+        tmem_ld_32x32b_x32(tbase + half * 64 + 32, y[1]);
         tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[buf]);
         if (valid) {
-          float* yrow = p.yd + size_t(pair) * p.hidden + tile * 128 + part * 32;
+          float* yrow = p.yd + size_t(pair) * p.hidden + tile * 128 + half * 64;
 #pragma unroll
-          for (int i = 0; i < 32; i += 4)
-            *reinterpret_cast<uint4*>(yrow + i) = make_uint4(y[i], y[i + 1], y[i + 2], y[i + 3]);
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<uint4*>(yrow + c * 32 + i) =
+                  make_uint4(y[c][i], y[c][i + 1], y[c][i + 2], y[c][i + 3]);
         }
       }
     }

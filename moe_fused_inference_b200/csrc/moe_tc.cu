@@ -389,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           if (active && i < q) {
             const float g = sg[(j0 + i) * 33 + n];
             const float u = sg[(64 + j0 + i) * 33 + n];
-            h[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+            h[i] = swiglu_fast(g, u);
             am = fmaxf(am, fabsf(h[i]));
             nan |= (h[i] != h[i]);
           }

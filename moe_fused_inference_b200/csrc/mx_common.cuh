@@ -105,6 +105,15 @@ __device__ __forceinline__ void nib8_to_i8(uint32_t w, uint32_t& lo, uint32_t& h
   hi = __byte_perm(ph, nh, 0x3210u | (s >> 16));
 }
 
+// SwiGLU of the fused expert kernels, h = g / (1 + e^-g) * u, evaluated the
+// way the reference's CUDA build evaluates it: src/ext/mxfp4_decode.cu:258
+// is compiled with --use_fast_math (CMakeLists.txt:22), which turns expf into
+// __expf and '/' into __fdividef.  (The standalone moe_down operator keeps
+// IEEE expf and division, like the reference's Python restatement.)
+__device__ __forceinline__ float swiglu_fast(float g, float u) {
+  return __fmul_rn(__fdividef(g, __fadd_rn(1.0f, __expf(-g))), u);
+}
+
 // 2^e as float for e in the normal range; ldexpf outside it.
 __device__ __forceinline__ float exp2i(int e) {
   if (e >= -126 && e <= 127) return __uint_as_float(uint32_t(e + 127) << 23);
