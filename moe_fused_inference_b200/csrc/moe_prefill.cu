@@ -39,7 +39,7 @@ using namespace tc;
 namespace {
 
 #ifndef MFI_PF_STAGES
-#define MFI_PF_STAGES 5
+#define MFI_PF_STAGES 4
 #endif
 constexpr int kPStages = MFI_PF_STAGES;
 // warp 0 loads, warp 1 issues MMAs, warps 2-17 run the epilogue in two
@@ -60,6 +60,10 @@ constexpr int kPOffSFA = kPA;
 constexpr int kPOffW = kPA + kPSF;             // 1024-byte aligned
 constexpr int kPOffSFB = kPOffW + 16384;
 constexpr int kPStageBytes = kPA + kPSF + kPW; // 34816
+// down epilogue: per warp a 32-row x 32-column fp32 staging tile, so that each
+// global store instruction writes whole 128-byte row segments (four rows per
+// instruction) instead of 16 bytes of 32 different rows
+constexpr int kPOutStage = 32 * 32 * 4;
 constexpr int kPAccBufs = 3;                   // 128 fp32 columns each
 constexpr uint32_t kPTmemCols = 512;
 constexpr uint32_t kPTmemSFA = kPAccBufs * 128;  // + 16 per ring slot: SFA 8 columns, SFB 8
@@ -156,7 +160,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kPStages * kPStageBytes);
+  uint8_t* out_stage = ring + kPStages * kPStageBytes;  // [kPEpiWarps][32 rows][128 B]
+  uint64_t* full = reinterpret_cast<uint64_t*>(out_stage + kPEpiWarps * kPOutStage);
   uint64_t* empty = full + kPStages;
   uint64_t* acc_full = empty + kPStages;
   uint64_t* acc_empty = acc_full + kPAccBufs;
@@ -420,23 +425,44 @@ __global__ void __launch_bounds__(kPThreads, 1)
           atomicAdd(p.gu_done, 1u);
         }
       } else {
-        // this warp stores output columns half*64 .. +63 of its token rows
-        uint32_t y[2][32];
-        tmem_ld_32x32b_x32(tbase + half * 64, y[0]);
-        tmem_ld_32x32b_x32(tbase + half * 64 + 32, y[1]);
+        // this warp stores output columns half*64 .. +63 of its token rows,
+        // transposed through shared memory: lane r holds row r; the stores go
+        // out as 4 rows x 8 lanes x 16 B.  16-byte chunk q of row r sits at
+        // chunk q ^ (r & 7), so both phases are free of bank conflicts.
+        uint4* stg = reinterpret_cast<uint4*>(out_stage + ew * kPOutStage);
+        auto stage = [&](const uint32_t (&v)[32]) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            stg[lane * 8 + (q ^ (lane & 7))] =
+                make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          __syncwarp();
+        };
+        auto drain = [&](int c) {
+          const int sub_row = lane >> 3, chunk = lane & 7;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int rr = 4 * i + sub_row;  // row of this lane's store
+            const int pr = __shfl_sync(0xffffffffu, pair, rr);
+            const bool ok_row = __shfl_sync(0xffffffffu, int(valid), rr) != 0;
+            const uint4 v = stg[rr * 8 + (chunk ^ (rr & 7))];
+            if (ok_row)
+              *reinterpret_cast<uint4*>(p.yd + size_t(pr) * p.hidden + tile * 128 + half * 64 +
+                                        c * 32 + chunk * 4) = v;
+          }
+          __syncwarp();
+        };
+        uint32_t y[32];
+        tmem_ld_32x32b_x32(tbase + half * 64, y);
+        tmem_ld_wait();
+        stage(y);
+        tmem_ld_32x32b_x32(tbase + half * 64 + 32, y);
         tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[buf]);
-        if (valid) {
-          float* yrow = p.yd + size_t(pair) * p.hidden + tile * 128 + half * 64;
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int i = 0; i < 32; i += 4)
-              *reinterpret_cast<uint4*>(yrow + c * 32 + i) =
-                  make_uint4(y[c][i], y[c][i + 1], y[c][i + 2], y[c][i + 3]);
-        }
+        drain(0);
+        stage(y);
+        drain(1);
       }
     }
   }
@@ -449,7 +475,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
 }
 
 size_t prefill_smem() {
-  return 1024 + size_t(kPStages) * kPStageBytes + 8 * (2 * kPStages + 4 * kPAccBufs) + 16;
+  return 1024 + size_t(kPStages) * kPStageBytes + size_t(kPEpiWarps) * kPOutStage +
+         8 * (2 * kPStages + 4 * kPAccBufs) + 16;
 }
 
 }  // namespace
