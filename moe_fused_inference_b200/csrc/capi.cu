@@ -376,6 +376,8 @@ struct PrefillScratch {
   int* perm;
   uint8_t* xp; uint8_t* xa; uint8_t* hp; uint8_t* ha;
   float* yd;            // (T*k, H) per-(token, slot) down rows
+  uint8_t* x8;          // tensor-core router scratch (aliases yd: used before it)
+  uint8_t* r8;          // the router rows as int8 blocks (E x H bytes)
   int rows;
   size_t bytes;
 };
@@ -399,7 +401,13 @@ PrefillScratch carve_prefill(void* ws, int T, int H, int Mi, int E, int k) {
   s.xa = c.take<uint8_t>(size_t(s.rows) / 128 * (H / 128) * 512);
   s.hp = c.take<uint8_t>(size_t(s.rows) * (Mi / 2));
   s.ha = c.take<uint8_t>(size_t(s.rows) / 128 * (Mi / 128) * 512);
-  s.yd = c.take<float>(size_t(P) * H);
+  // the router's int8 token rows (ceil(T/128)*128 x H bytes) live in the
+  // yd region: the router finishes before the expert kernel writes yd
+  const size_t x8_bytes = (size_t(T) + 127) / 128 * 128 * size_t(H);
+  const size_t yd_floats = size_t(P) * H;
+  s.yd = c.take<float>(yd_floats * 4 >= x8_bytes ? yd_floats : (x8_bytes + 3) / 4);
+  s.x8 = reinterpret_cast<uint8_t*>(s.yd);
+  s.r8 = c.take<uint8_t>(size_t(E) * H);
   s.bytes = c.used + 256;
   return s;
 }
@@ -430,6 +438,8 @@ int run_prefill(const mfi_moe_weights* w, const void* x_bf16, int T, float* out,
   ra.logits = logits; ra.topi = topi; ra.topw = topw;
   ra.cursor = s.counts; ra.slot_pos = s.slot_pos;
   ra.batch = T >= 512;  // enough tokens to fill the GPU one per warp
+  ra.x8 = s.x8;
+  ra.r8 = s.r8;
   ra.logit_bias = w->logit_bias;
   ra.err = mfi::device_error_flag();
   rc = cuda_status(mfi::launch_route(ra, st), "moe_layer prefill route launch");

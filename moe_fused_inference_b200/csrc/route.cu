@@ -17,15 +17,12 @@
 #include "work.cuh"
 #include "tc_ptx.cuh"
 #include "tmap.cuh"
+#include "route_common.cuh"
 
 namespace mfi {
 
 constexpr int kRouteThreads = 512;
 constexpr int kMaxE = kRouteMaxE;
-
-__device__ __forceinline__ bool better(float v, int i, float w, int j) {
-  return v > w || (v == w && i < j);
-}
 
 template <int kMaxBlk>
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
@@ -685,35 +682,6 @@ size_t route_batch_smem(int E, int H) {
 
 // Quantise token t into (s_xq, s_xsc) with the whole warp (quads of lanes per
 // 32-element block); t < 0: zeros.
-__device__ __forceinline__ void warp_quant_token(const RouteArgs& a, int t, uint8_t* s_xq,
-                                                 uint8_t* s_xsc, int lane) {
-  for (int base = 0; base < (a.H >> 3); base += 32) {
-    const int c8 = base + lane;
-    const bool live = c8 < (a.H >> 3);
-    float v[8];
-    if (live && t >= 0) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(
-          reinterpret_cast<const __nv_bfloat16*>(a.x) + long(t) * a.H + c8 * 8);
-      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(h2[i]);
-        v[2 * i] = f.x;
-        v[2 * i + 1] = f.y;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = 0.0f;
-    }
-    BlockScale bs;
-    const uint32_t word = quant_group8(v, bs);
-    if (live) {
-      reinterpret_cast<uint32_t*>(s_xq)[c8] = word;
-      if ((c8 & 3) == 0) s_xsc[c8 >> 2] = bs.code;
-    }
-  }
-}
-
 template <int kMaxBlk>
 __global__ void __launch_bounds__(kBatchThreads) route_batch_kernel(RouteArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -848,55 +816,8 @@ __global__ void __launch_bounds__(kBatchThreads) route_batch_kernel(RouteArgs a)
     for (int q = 0; q < kBatchTok; ++q) {
       const int t = tok[q];
       if (t < 0) continue;
-      float* s_lg = reinterpret_cast<float*>(s_slots + size_t(warp * kBatchTok + q) * slot);
-      if (a.logit_bias)
-        for (int e = lane; e < a.E; e += 32) s_lg[e] = __fadd_rn(s_lg[e], a.logit_bias[e]);
-      __syncwarp();
-      if (a.logits)
-        for (int e = lane; e < a.E; e += 32) a.logits[long(t) * a.E + e] = s_lg[e];
-      constexpr int kPer = kRouteMaxE / 32;
-      float v[kPer];
-      uint32_t taken = 0;
-#pragma unroll
-      for (int i = 0; i < kPer; ++i) v[i] = (lane + 32 * i < a.E) ? s_lg[lane + 32 * i] : 0.0f;
-      int my_sel = -1;
-      float my_val = 0.0f;
-      for (int j = 0; j < a.k; ++j) {
-        float bv = 0.0f;
-        int bi = -1;
-#pragma unroll
-        for (int i = 0; i < kPer; ++i) {
-          const int e = lane + 32 * i;
-          if (e < a.E && !((taken >> i) & 1u) && (bi < 0 || better(v[i], e, bv, bi))) {
-            bv = v[i];
-            bi = e;
-          }
-        }
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) {
-          const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-          const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-          if (oi >= 0 && (bi < 0 || better(ov, oi, bv, bi))) {
-            bv = ov;
-            bi = oi;
-          }
-        }
-        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-        if (lane == j) {
-          my_sel = bi;
-          my_val = bv;
-        }
-      }
-      const float mx = __shfl_sync(0xffffffffu, my_val, 0);
-      const float pj = lane < a.k ? expf(my_val - mx) : 0.0f;
-      float sum = 0.0f;
-      for (int j = 0; j < a.k; ++j) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, pj, j));
-      if (lane < a.k) {
-        a.topi[long(t) * a.k + lane] = my_sel;
-        a.topw[long(t) * a.k + lane] = __fdiv_rn(pj, sum);
-        if (a.slot_pos) a.slot_pos[long(t) * a.k + lane] = atomicAdd(a.cursor + my_sel, 1);
-      }
-      __syncwarp();
+      finish_token(a, t, reinterpret_cast<float*>(s_slots + size_t(warp * kBatchTok + q) * slot),
+                   lane);
     }
   }
 }
@@ -944,6 +865,8 @@ cudaError_t launch_route(const RouteArgs& a, cudaStream_t stream) {
   if (a.T < 0 || (a.T == 0 && !a.ep.table)) return cudaSuccess;
   if (a.H > 4096) return cudaErrorInvalidValue;
   if (!a.g_gu) {
+    // prefill sizes, Qwen-shaped router: the tensor-core router
+    if (route_tc_applies(a)) return launch_route_tc(a, stream);
     // many tokens, placement by position claims, router fits in shared
     // memory: one router copy per CTA, one token per warp
     if (a.batch && !a.xp && !a.ep.table && route_batch_smem(a.E, a.H) <= 220 * 1024 &&

@@ -139,7 +139,31 @@ __host__ __device__ constexpr uint32_t make_idesc_mxf4(int M, int N, int a_sf_id
          (1u << 23) | (uint32_t(M >> 4) << 24) | (uint32_t(a_sf_id & 3) << 29);
 }
 
+// Instruction descriptor for kind::i8 (signed 8-bit A and B, K = 32, both
+// operands K-major, s32 accumulate).
+//   [4,6) D fmt=S32(2)  [7,10) A fmt=S8(1)  [10,13) B fmt=S8(1)  [17,23) N>>3
+//   [24,29) M>>4
+__host__ __device__ constexpr uint32_t make_idesc_i8(int M, int N) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+
 // ---------------------------------------------------------------- tcgen05 ops
+// D(tmem) (+)= A(smem) . B(smem)^T, signed 8-bit operands, s32 accumulators.
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Order this thread's generic-proxy shared-memory writes before later
+// async-proxy accesses (tensor-core operand reads, TMA writes) of the CTA.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // D(tmem) (+)= A(smem) . B(smem)^T with block scales from TMEM.  The scale
 // addresses carry the byte-in-word selector in bits 31:30, matching the
 // sf_id fields of the instruction descriptor.

@@ -15,6 +15,11 @@ bool make_tmap(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t ro
 bool get_tmap(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows,
               uint32_t box_rows);
 
+// Unswizzled map with a box of box_bytes (a multiple of 16) x box_rows,
+// memoised like get_tmap.
+bool get_tmap_plain(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows,
+                    uint32_t box_bytes, uint32_t box_rows);
+
 // Grant kernel `fn` `bytes` of dynamic shared memory on the current device
 // (cudaFuncSetAttribute once per device and size; thread-safe).
 cudaError_t ensure_dynamic_smem(const void* fn, size_t bytes);

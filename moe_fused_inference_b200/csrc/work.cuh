@@ -104,6 +104,11 @@ struct RouteArgs {
   // tokens of its expert (cursor claim, no row copy)
   int* slot_pos;
   bool batch;          // prefer the one-token-per-warp batch router (many tokens)
+  // scratch of the tensor-core router (route_tc.cu): ceil(T/128)*128 x H
+  // bytes of int8 token rows and E x H bytes of int8 router rows; null: that
+  // router is not used
+  uint8_t* x8;
+  uint8_t* r8;
 };
 
 constexpr int kRouteMaxE = 256;
@@ -111,6 +116,11 @@ constexpr int kRouteMaxPairs = 4096;
 constexpr int kBuildGroupsMaxP = 4096;
 
 cudaError_t launch_quant_rows(const QuantArgs& a, cudaStream_t stream);
+// Prefill router on the tensor cores (E = 128, H a multiple of 128, <= 2048,
+// a.x8 set); launch_route picks it when it applies.
+bool route_tc_applies(const RouteArgs& a);
+cudaError_t launch_route_tc(const RouteArgs& a, cudaStream_t stream);
+
 cudaError_t launch_swiglu_quant(const float* gu, long ld_gu, const int* rows, int n_rows,
                                 const int* n_rows_dev, uint8_t* hq, uint8_t* hsc, int K, int Kp,
                                 cudaStream_t stream);

@@ -106,3 +106,29 @@ def test_prefill_repeatable_and_capturable(qwen_layer):
     torch.cuda.synchronize()
     assert torch.equal(out, first)  # placement order varies, results do not
     del g
+
+
+@pytest.mark.parametrize("span", [5, 70])
+def test_prefill_router_ragged_tile_and_wide_scales(qwen_layer, span):
+    """T = 677 through the tensor-core router (a partial last 128-token tile),
+    with every 50th token given 32-element blocks 2^span apart in magnitude.
+    span 5: those tokens cannot carry their block scales in the int8 operand,
+    so their tiles take the per-block accumulators (fp64 epilogue); span 70:
+    beyond the span where that fp64 sum is order-free, so the router
+    recomputes them in the fixed order.  Every logit stays bit-exact."""
+    T = 677
+    x = _x(T, 91).float()
+    x[::50, :32] *= 2.0 ** (span // 2 + span % 2)
+    x[::50, 32:64] *= 2.0 ** -(span // 2)
+    x = x.bfloat16()
+    layer = MoELayer(qwen_layer, top_k=8)
+    logits = torch.empty((T, 128), dtype=torch.float32, device="cuda")
+    out, topi, topw = layer.prefill(x, logits=logits)
+    torch.cuda.synchronize()
+    from moe_fused_inference_b200 import _lib
+    assert _lib.load().mfi_device_error(1) == 0
+    ref = mx.moe_layer(x.float().cpu().numpy(), oracle_weights(qwen_layer), topk=8, fast=True)
+    assert np.array_equal(logits.cpu().numpy(), ref["logits"])
+    assert np.array_equal(topi.cpu().numpy(), ref["idx"])
+    np.testing.assert_allclose(topw.cpu().numpy(), ref["w"], rtol=2e-6, atol=1e-7)
+    assert torch.isfinite(out).all()
