@@ -375,7 +375,7 @@ struct PrefillScratch {
   uint8_t* xq; uint8_t* xsc;
   int* perm;
   uint8_t* xp; uint8_t* xa; uint8_t* hp; uint8_t* ha;
-  float* yd;            // (T*k, H) per-(token, slot) down rows
+  __nv_bfloat16* yd;    // (T*k, H) per-(token, slot) down rows, bf16
   uint8_t* x8;          // tensor-core router scratch (aliases yd: used before it)
   uint8_t* r8;          // the router rows as int8 blocks (E x H bytes)
   int rows;
@@ -404,8 +404,8 @@ PrefillScratch carve_prefill(void* ws, int T, int H, int Mi, int E, int k) {
   // the router's int8 token rows (ceil(T/128)*128 x H bytes) live in the
   // yd region: the router finishes before the expert kernel writes yd
   const size_t x8_bytes = (size_t(T) + 127) / 128 * 128 * size_t(H);
-  const size_t yd_floats = size_t(P) * H;
-  s.yd = c.take<float>(yd_floats * 4 >= x8_bytes ? yd_floats : (x8_bytes + 3) / 4);
+  const size_t yd_elems = size_t(P) * H;
+  s.yd = c.take<__nv_bfloat16>(yd_elems * 2 >= x8_bytes ? yd_elems : (x8_bytes + 1) / 2);
   s.x8 = reinterpret_cast<uint8_t*>(s.yd);
   s.r8 = c.take<uint8_t>(size_t(E) * H);
   s.bytes = c.used + 256;
@@ -461,8 +461,8 @@ int run_prefill(const mfi_moe_weights* w, const void* x_bf16, int T, float* out,
   L.pdl = true;
   rc = cuda_status(mfi::launch_moe_prefill(L, st), "moe_layer prefill experts launch");
   if (rc != MFI_OK) return rc;
-  // k <= 32 slots per token here; the decode combine's arithmetic
-  return cuda_status(mfi::launch_combine(s.yd, H, topw, k, k, out, T, H, st, true),
+  // the decode combine's arithmetic on bf16 rows
+  return cuda_status(mfi::launch_combine_bf16(s.yd, topw, k, out, T, H, st, true),
                      "moe_layer prefill combine launch");
 }
 

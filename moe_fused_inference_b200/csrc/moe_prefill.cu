@@ -81,7 +81,7 @@ struct PrefillArgs {
   const uint8_t* xa;           // token-row scale atoms [row/128][H/128][512]
   uint8_t* hp;                 // requantised h rows (rows, inter/2)
   uint8_t* ha;                 // their scale atoms [row/128][inter/128][512]
-  float* yd;                   // (pairs, hidden) fp32 per-(token, slot) down rows
+  __nv_bfloat16* yd;           // (pairs, hidden) bf16 per-(token, slot) down rows
   int hidden, inter, top_k;
   int* err;
   int* queue;                  // work-item counter, zero before the launch
@@ -91,6 +91,11 @@ struct PrefillArgs {
 
 __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// Two fp32 values (as bits) -> packed bf16 pair, round to nearest even.
+__device__ __forceinline__ uint32_t bf16x2_bits(uint32_t lo, uint32_t hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(__uint_as_float(lo), __uint_as_float(hi));
+  return *reinterpret_cast<const uint32_t*>(&v);
 }
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
   unsigned v;
@@ -425,44 +430,43 @@ __global__ void __launch_bounds__(kPThreads, 1)
           atomicAdd(p.gu_done, 1u);
         }
       } else {
-        // this warp stores output columns half*64 .. +63 of its token rows,
-        // transposed through shared memory: lane r holds row r; the stores go
-        // out as 4 rows x 8 lanes x 16 B.  16-byte chunk q of row r sits at
-        // chunk q ^ (r & 7), so both phases are free of bank conflicts.
+        // this warp stores output columns half*64 .. +63 of its token rows in
+        // bf16 (each expert's output row is rounded to the activation type,
+        // as the reference's prefill does with y, runtime/model_runner_v2.py
+        // :119), transposed through shared memory: lane r holds row r (128
+        // bytes); the stores go out as 4 rows x 8 lanes x 16 B.  16-byte
+        // chunk q of row r sits at chunk q ^ (r & 7), so both phases are free
+        // of bank conflicts.
         uint4* stg = reinterpret_cast<uint4*>(out_stage + ew * kPOutStage);
-        auto stage = [&](const uint32_t (&v)[32]) {
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            stg[lane * 8 + (q ^ (lane & 7))] =
-                make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-          __syncwarp();
-        };
-        auto drain = [&](int c) {
-          const int sub_row = lane >> 3, chunk = lane & 7;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int rr = 4 * i + sub_row;  // row of this lane's store
-            const int pr = __shfl_sync(0xffffffffu, pair, rr);
-            const bool ok_row = __shfl_sync(0xffffffffu, int(valid), rr) != 0;
-            const uint4 v = stg[rr * 8 + (chunk ^ (rr & 7))];
-            if (ok_row)
-              *reinterpret_cast<uint4*>(p.yd + size_t(pr) * p.hidden + tile * 128 + half * 64 +
-                                        c * 32 + chunk * 4) = v;
-          }
-          __syncwarp();
-        };
-        uint32_t y[32];
+        uint32_t y[32], pk[32];
         tmem_ld_32x32b_x32(tbase + half * 64, y);
         tmem_ld_wait();
-        stage(y);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = bf16x2_bits(y[2 * i], y[2 * i + 1]);
         tmem_ld_32x32b_x32(tbase + half * 64 + 32, y);
         tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[buf]);
-        drain(0);
-        stage(y);
-        drain(1);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[16 + i] = bf16x2_bits(y[2 * i], y[2 * i + 1]);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          stg[lane * 8 + (q ^ (lane & 7))] =
+              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        __syncwarp();
+        const int sub_row = lane >> 3, chunk = lane & 7;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int rr = 4 * i + sub_row;  // row of this lane's store
+          const int pr = __shfl_sync(0xffffffffu, pair, rr);
+          const bool ok_row = __shfl_sync(0xffffffffu, int(valid), rr) != 0;
+          const uint4 v = stg[rr * 8 + (chunk ^ (rr & 7))];
+          if (ok_row)
+            *reinterpret_cast<uint4*>(p.yd + size_t(pr) * p.hidden + tile * 128 + half * 64 +
+                                      chunk * 8) = v;
+        }
+        __syncwarp();
       }
     }
   }

@@ -3,6 +3,7 @@
 #pragma once
 #include <cstdint>
 #include <cuda_runtime.h>
+#include <cuda_bf16.h>
 
 namespace mfi {
 
@@ -136,6 +137,10 @@ cudaError_t launch_build_groups(const uint8_t* const* wp_tab, const uint8_t* con
                                 EntryDesc* entries, cudaStream_t stream);
 // clear/n_clear: counters zeroed by the launch once the previous kernel is
 // complete (the fused layer's per-call counters), or null
+// Prefill combine: out[m] = sum over slots e (ascending) of w[m][e] * y[m][e],
+// y rows in bf16, products and sums in fp32 as in combine_kernel.
+cudaError_t launch_combine_bf16(const __nv_bfloat16* yd, const float* w, int k, float* out, int M,
+                                int N, cudaStream_t stream, bool pdl);
 cudaError_t launch_combine(const float* yd, long ystride, const float* w, int E, int E_sum,
                            float* out, int M, int N, cudaStream_t stream, bool pdl = false,
                            unsigned* clear = nullptr, int n_clear = 0);
@@ -202,7 +207,7 @@ struct PrefillLaunch {
   int rows;                      // rows of xp / hp (prefill_rows)
   const uint8_t* xp; const uint8_t* xa;   // token rows and their 128-row scale atoms
   uint8_t* hp; uint8_t* ha;               // requantised h rows and atoms
-  float* yd;                     // (pairs, H) per-(token, slot) down rows
+  __nv_bfloat16* yd;             // (pairs, H) per-(token, slot) down rows, bf16
   int* err; int* queue; unsigned* gu_done; unsigned* ready;
   bool pdl;
 };

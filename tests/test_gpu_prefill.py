@@ -5,8 +5,11 @@ tiles, vs the kernel-path oracle.
 Contract (BASELINE north_star): top-k indices and router logits bit-exact;
 layer output max relative error <= 1e-2 and cosine >= 0.999 versus the
 fp32-accumulated dequantised reference (the oracle accumulates in float64).
-The prefill combine is the decode one (slot order, unfused fp32 multiply and
-add), so a call is bit-reproducible whatever order the rows were placed in.
+Each (token, slot) output row of the prefill path is rounded to bf16 (as the
+reference's prefill rounds y to the activation type,
+runtime/model_runner_v2.py:119); the combine then adds them in slot order
+with the decode combine's unfused fp32 multiply and add, so a call is
+bit-reproducible whatever order the rows were placed in.
 """
 
 import numpy as np
@@ -52,11 +55,13 @@ def test_prefill_forced_small_T(qwen_layer, T):
     o = out.cpu().numpy()
     assert cosine(o, ref["out"]) >= 0.999
     assert max_rel_err(o, ref["out"]) <= 1e-2
-    # the decode kernels on the same input agree to fp32 rounding
+    # the decode kernels (fp32 rows) on the same input agree to the bf16
+    # rounding of the prefill rows: 2^-9 of the largest row, a few 1e-3 of
+    # the largest output
     dec, dtopi, _ = layer(x)
     torch.cuda.synchronize()
     assert torch.equal(dtopi, topi)
-    assert max_rel_err(o, dec.cpu().numpy()) <= 2e-3
+    assert max_rel_err(o, dec.cpu().numpy()) <= 6e-3
 
 
 def test_prefill_auto_zipf_T2048(qwen_layer):
