@@ -123,39 +123,42 @@ __device__ int expert_bases(const int* s_cnt, int E, int* s_base) {
   return run;
 }
 
-// One CTA per token: copy its quantised row and scale atoms to each of its
-// k expert rows.
-__global__ void __launch_bounds__(128) prefill_scatter_kernel(
+// One CTA per kScTok tokens: copy each token's quantised row and scale atoms
+// to its k expert rows (the expert bases are computed once per CTA).
+constexpr int kScTok = 16;
+constexpr int kScThreads = 256;
+__global__ void __launch_bounds__(kScThreads) prefill_scatter_kernel(
     const uint8_t* __restrict__ xq, const uint8_t* __restrict__ xsc, const int* __restrict__ topi,
-    const int* __restrict__ slot_pos, const int* __restrict__ counts, int E, int k, int H,
+    const int* __restrict__ slot_pos, const int* __restrict__ counts, int T, int E, int k, int H,
     int* __restrict__ perm, uint8_t* __restrict__ xp, uint8_t* __restrict__ xa) {
-  const int t = blockIdx.x;
+  const int tok0 = blockIdx.x * kScTok;
+  const int nt = min(kScTok, T - tok0);
   __shared__ int s_cnt[kPMaxExperts];
   __shared__ int s_base[kPMaxExperts];
-  __shared__ int s_row[32];
+  __shared__ int s_row[kScTok * 32];
   for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = counts[e];
   __syncthreads();
   if (threadIdx.x < 32) expert_bases(s_cnt, E, s_base);
   __syncthreads();
-  if (threadIdx.x < k) {
-    const int j = threadIdx.x;
-    const int row = s_base[topi[size_t(t) * k + j]] + slot_pos[size_t(t) * k + j];
-    s_row[j] = row;
-    perm[row] = t * k + j;
+  for (int p = threadIdx.x; p < nt * k; p += blockDim.x) {
+    const long pair = long(tok0) * k + p;
+    const int row = s_base[topi[pair]] + slot_pos[pair];
+    s_row[p] = row;
+    perm[row] = int(pair);
   }
   __syncthreads();
   const int q16 = H / 32, kc = H / 128;
-  for (int i = threadIdx.x; i < k * q16; i += blockDim.x) {
-    const int j = i / q16, c = i % q16;
-    reinterpret_cast<uint4*>(xp + size_t(s_row[j]) * (H / 2))[c] =
-        reinterpret_cast<const uint4*>(xq + size_t(t) * (H / 2))[c];
+  for (int p = threadIdx.x; p < nt * k * q16; p += blockDim.x) {
+    const int pj = p / q16, c = p - pj * q16;  // pair (token i = pj / k), 16-byte chunk c
+    reinterpret_cast<uint4*>(xp + size_t(s_row[pj]) * (H / 2))[c] =
+        reinterpret_cast<const uint4*>(xq + size_t(tok0 + pj / k) * (H / 2))[c];
   }
-  for (int i = threadIdx.x; i < k * kc; i += blockDim.x) {
-    const int j = i / kc, c = i % kc;
-    const int row = s_row[j];
+  for (int p = threadIdx.x; p < nt * k * kc; p += blockDim.x) {
+    const int pj = p / kc, c = p - pj * kc;
+    const int row = s_row[pj];
     *reinterpret_cast<uint32_t*>(xa + (size_t(row / kPTile) * kc + c) * 512 + (row % 32) * 16 +
                                  ((row % kPTile) / 32) * 4) =
-        reinterpret_cast<const uint32_t*>(xsc + size_t(t) * (H / 32))[c];
+        reinterpret_cast<const uint32_t*>(xsc + size_t(tok0 + pj / k) * (H / 32))[c];
   }
 }
 
@@ -497,8 +500,8 @@ cudaError_t launch_prefill_scatter(const uint8_t* xq, const uint8_t* xsc, const 
                                    int H, int* perm, uint8_t* xp, uint8_t* xa,
                                    cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
-  prefill_scatter_kernel<<<T, 128, 0, stream>>>(xq, xsc, topi, slot_pos, counts, E, k, H, perm,
-                                                xp, xa);
+  prefill_scatter_kernel<<<(T + kScTok - 1) / kScTok, kScThreads, 0, stream>>>(
+      xq, xsc, topi, slot_pos, counts, T, E, k, H, perm, xp, xa);
   return cudaGetLastError();
 }
 

@@ -145,16 +145,55 @@ __global__ void __launch_bounds__(kQxThreads) quant_x8_kernel(RouteArgs a, int n
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nb = a.H >> 5, nchunk = a.H >> 7;
   if (int(blockIdx.x) < n_tok_ctas) {
-    __shared__ __align__(16) uint8_t s_q[kQxTok][2048 / 2];
-    __shared__ __align__(16) uint8_t s_s[kQxTok][kRtMaxBlk];
+    // lane l quantises blocks l and l + 32 whole (the arithmetic of
+    // quant_group8: block maximum, NaN -> code 127, nibbles at 2^-e)
     const int t = blockIdx.x * kQxTok + warp;  // < ceil(T/128) * 128
     const int tt = t < a.T ? t : -1;
-    warp_quant_token(a, tt, s_q[warp], s_s[warp], lane);
-    __syncwarp();
+    uint4 packed[kRtMaxBlk / 32];
+    int code[kRtMaxBlk / 32];
     int lo = 255, hi = 0;
-    for (int b = lane; b < nb; b += 32) {
-      lo = min(lo, int(s_s[warp][b]));
-      hi = max(hi, int(s_s[warp][b]));
+#pragma unroll
+    for (int jb = 0; jb < kRtMaxBlk / 32; ++jb) {
+      const int b = lane + 32 * jb;
+      code[jb] = 127;
+      packed[jb] = make_uint4(0u, 0u, 0u, 0u);
+      if (b >= nb) continue;
+      float v[32];
+      if (tt >= 0) {
+        const uint4* src = reinterpret_cast<const uint4*>(
+            reinterpret_cast<const __nv_bfloat16*>(a.x) + long(tt) * a.H + b * 32);
+        uint4 raw[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) raw[q] = src[q];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw[q]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h2[i]);
+            v[q * 8 + 2 * i] = f.x;
+            v[q * 8 + 2 * i + 1] = f.y;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.0f;
+      }
+      float am = 0.0f;
+      bool nan = false;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        am = fmaxf(am, fabsf(v[i]));
+        nan |= (v[i] != v[i]);
+      }
+      const BlockScale bs = block_scale(nan ? __uint_as_float(0x7fc00000u) : am);
+      uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+      for (int i = 0; i < 32; ++i) w[i >> 3] |= quant_nibble(v[i], bs.inv) << (4 * (i & 7));
+      packed[jb] = make_uint4(w[0], w[1], w[2], w[3]);
+      code[jb] = bs.code;
+      lo = min(lo, int(bs.code));
+      hi = max(hi, int(bs.code));
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) {
@@ -162,17 +201,18 @@ __global__ void __launch_bounds__(kQxThreads) quant_x8_kernel(RouteArgs a, int n
       hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, off));
     }
     const bool scaled = hi - lo <= kShiftMax;
-    if (tt >= 0) {
-      for (int c = lane; c < nb; c += 32)
-        reinterpret_cast<uint4*>(a.xq + long(t) * (a.H >> 1))[c] =
-            reinterpret_cast<const uint4*>(s_q[warp])[c];
-      for (int b = lane; b < nb; b += 32) a.xsc[long(t) * nb + b] = s_s[warp][b];
-    }
     uint8_t* x8t = a.x8 + size_t(t / kRtTile) * nchunk * kRtBlock;
-    for (int u = lane; u < nb; u += 32)
-      store_i8_row_part(x8t + size_t(u >> 2) * kRtBlock, t % kRtTile, u & 3,
-                        reinterpret_cast<const uint4*>(s_q[warp])[u],
-                        scaled ? int(s_s[warp][u]) - lo : 0);
+#pragma unroll
+    for (int jb = 0; jb < kRtMaxBlk / 32; ++jb) {
+      const int b = lane + 32 * jb;
+      if (b >= nb) continue;
+      if (tt >= 0) {
+        reinterpret_cast<uint4*>(a.xq + long(tt) * (a.H >> 1))[b] = packed[jb];
+        a.xsc[long(tt) * nb + b] = uint8_t(code[jb]);
+      }
+      store_i8_row_part(x8t + size_t(b >> 2) * kRtBlock, t % kRtTile, b & 3, packed[jb],
+                        scaled ? code[jb] - lo : 0);
+    }
   } else {
     // one warp per expert
     for (int e = (blockIdx.x - n_tok_ctas) * kQxTok + warp; e < a.E; e += kQxRouterCtas * kQxTok) {
