@@ -61,6 +61,9 @@ def parse():
                          "T = 16384 by default, Zipf(1.2)-skewed routing)")
     ap.add_argument("--zipf-alpha", type=float, default=0.5,
                     help="prefill: scale of the Zipf(1.2) per-expert logit bias")
+    ap.add_argument("--ep-zipf", action="store_true",
+                    help="expert parallelism: add the Zipf(1.2) logit bias (--zipf-alpha) to "
+                         "the router, for the skewed-load scaling report")
     ap.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
                     help="multi-GPU token exchange: peer-memory stores fused into the kernels "
                          "(p2p) or two NCCL all_to_all_single calls (nccl)")
@@ -334,6 +337,12 @@ def run_prefill(args, world, rank, local):
     tflops = flops / (ms_per_step / 1e3) / 1e12
     counts = torch.bincount(topi[0].flatten().long(), minlength=E).float()
     fp4_peak = 9000.0  # dense MXFP4 tensor peak, nominal (no measured FP4 figure on this pool)
+    # algorithmic bytes of one layer call: every expert with tokens once, the
+    # MXFP4 router, bf16 in, fp32 out, ids and weights
+    hbm_bytes = (int((counts > 0).sum()) * EXPERT_BYTES + ROUTER_BYTES + T * H * 2 + T * H * 4
+                 + T * TOPK * 8)
+    hbm_gbs = hbm_bytes / (ms_per_step / NL / 1e3) / 1e9
+    hbm_peak, hbm_kind = measured_peaks()
 
     # ---- dense mxfp4_linear of the attention projections at T tokens (config 3):
     # lin_pq on pre-quantised activations (the GEMM incl. its scale re-layout)
@@ -372,13 +381,16 @@ def run_prefill(args, world, rank, local):
                    "step": f"{NL} MoE layers with distinct weights, plain launches",
                    "expert_load_max_over_mean": float(counts.max() / counts.mean()),
                    "experts_with_tokens": int((counts > 0).sum())},
-        "gpu_launches": 5 * NL * args.steps,  # route, scatter, experts, combine (+ memset)
+        "gpu_launches": 5 * NL * args.steps,  # quantise, route, scatter, experts, combine
         "roofline": {"bound": "tensor", "achieved": tflops, "peak": fp4_peak, "unit": "TFLOP/s",
                      "frac": tflops / fp4_peak, "peak_kind": "nominal dense FP4 (no measured FP4 peak)",
                      "flops_per_layer": flop_tok * T,
                      "dense_projections": {k: {"us": v["us"], "tflops": v["tflops"],
                                                "frac": v["tflops"] / fp4_peak}
-                                           for k, v in dense.items()}},
+                                           for k, v in dense.items()},
+                     # the other roof: at small T the weights, not the math, set the time
+                     "hbm": {"bytes_per_layer": hbm_bytes, "achieved": hbm_gbs, "peak": hbm_peak,
+                             "unit": "GB/s", "frac": hbm_gbs / hbm_peak, "peak_kind": hbm_kind}},
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
@@ -512,8 +524,12 @@ def run_ep(args, world, rank, local):
 
     dev = torch.device("cuda", local)
     T, NL = args.tokens, args.layers
+    bias = None
+    if args.ep_zipf:
+        from oracle import mxfp4 as mx
+        bias = torch.from_numpy(mx.zipf_bias(E, args.zipf_alpha, seed=3)).to(dev)
     layers = [EPMoELayer(random_shard(E, world, rank, H, MI, 0.02, seed=l, device=dev), TOPK, T,
-                         transport=args.ep_transport)
+                         transport=args.ep_transport, logit_bias=bias)
               for l in range(NL)]
     g = torch.Generator(device=dev).manual_seed(7 + rank)
     X = torch.randn((NL, T, H), generator=g, device=dev).bfloat16()
@@ -604,6 +620,10 @@ def run_ep(args, world, rank, local):
     allstats = [torch.zeros_like(stats) for _ in range(world)]
     dist.all_gather(allstats, stats)
     allstats = torch.stack(allstats).cpu()
+    # expert load over all ranks' tokens (layer 0's routing)
+    load = torch.bincount(layers[0].topi[:T].flatten().long(), minlength=E).to(torch.float64)
+    dist.all_reduce(load)
+    load_max_over_mean = float(load.max() / load.mean())
 
     # ---- e2e: host activations in, host outputs back, plain launches ----
     if graph is not None:
@@ -643,6 +663,9 @@ def run_ep(args, world, rank, local):
                        "route, pack, NCCL all-to-all dispatch, tcgen05 experts, all-to-all "
                        "return, unpack") + ", " + graph_note,
                    "ep_transport": args.ep_transport,
+                   "routing": (f"Zipf(1.2) logit bias alpha={args.zipf_alpha}" if args.ep_zipf
+                               else "near-uniform (random router)"),
+                   "expert_load_max_over_mean": load_max_over_mean,
                    "global_batch": T * world, "parallelism": f"ep{world} ({E // world} experts/GPU)",
                    "l2": f"inputs larger than L2: {NL} distinct layer shards "
                          f"({NL * (E // world) * EXPERT_BYTES / 1e9:.1f} GB/GPU) per step",

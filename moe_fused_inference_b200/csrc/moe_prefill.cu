@@ -125,7 +125,7 @@ __device__ int expert_bases(const int* s_cnt, int E, int* s_base) {
 
 // One CTA per kScTok tokens: copy each token's quantised row and scale atoms
 // to its k expert rows (the expert bases are computed once per CTA).
-constexpr int kScTok = 16;
+constexpr int kScTok = 4;
 constexpr int kScThreads = 256;
 __global__ void __launch_bounds__(kScThreads) prefill_scatter_kernel(
     const uint8_t* __restrict__ xq, const uint8_t* __restrict__ xsc, const int* __restrict__ topi,

@@ -139,7 +139,8 @@ def row_offsets(hidden: int, top_k: int):
 class CudaEPOps:
     """The per-step operations on the GPU, through libmoe_fp4.so."""
 
-    def __init__(self, shard: EPShard, top_k: int, capacity: int, world: int):
+    def __init__(self, shard: EPShard, top_k: int, capacity: int, world: int,
+                 logit_bias: torch.Tensor | None = None):
         lib = _lib.load()
         self.lib = lib
         self.shard = shard
@@ -155,6 +156,13 @@ class CudaEPOps:
         self._route_w = _lib.MoEWeights(0, 0, 0, 0, 0, 0, shard.router_wp.data_ptr(),
                                         shard.router_sc.data_ptr(), shard.n_experts, H, Mi,
                                         top_k, None)
+        # optional per-expert logit bias (E fp32), added before the top-k
+        self.logit_bias = None
+        if logit_bias is not None:
+            self.logit_bias = logit_bias.to(shard.router_wp.device, torch.float32).contiguous()
+            if self.logit_bias.numel() != shard.n_experts:
+                raise RuntimeError("logit_bias needs one value per expert")
+            self._route_w.logit_bias = self.logit_bias.data_ptr()
         self._exp_w = _lib.MoEWeights(
             shard.gate_wp.data_ptr(), shard.gate_sc.data_ptr(), shard.up_wp.data_ptr(),
             shard.up_sc.data_ptr(), shard.down_wp.data_ptr(), shard.down_sc.data_ptr(),
@@ -314,7 +322,8 @@ class EPMoELayer:
 
     def __init__(self, shard: EPShard, top_k: int, capacity: int, group=None, ops=None,
                  device=None, world: int | None = None, rank: int | None = None,
-                 transport: str | None = None, connect: bool = True):
+                 transport: str | None = None, connect: bool = True,
+                 logit_bias: torch.Tensor | None = None):
         self.group = group
         # world / rank may be given to drive the steps without a process group
         # (all ranks of a test in one process, the exchange done by copies)
@@ -327,7 +336,10 @@ class EPMoELayer:
         self.shard = shard
         self.k = top_k
         self.C = int(capacity)
-        self.ops = ops if ops is not None else CudaEPOps(shard, top_k, self.C, self.world)
+        if ops is not None and logit_bias is not None:
+            raise RuntimeError("logit_bias is applied by the GPU router only")
+        self.ops = ops if ops is not None else CudaEPOps(shard, top_k, self.C, self.world,
+                                                         logit_bias=logit_bias)
         dev = device if device is not None else shard.gate_wp.device
         H, n, C = shard.hidden, self.world, self.C
         rb = ep_row_bytes(H, top_k)

@@ -87,14 +87,14 @@ def test_ep_emulated_matches_single_gpu(world, counts):
         assert cosine(a, b) >= 0.999999
 
 
-def _emulate_p2p(w, xs, world, k, capacity, calls=1):
+def _emulate_p2p(w, xs, world, k, capacity, calls=1, logit_bias=None):
     """The peer-memory transport over `world` virtual ranks on one GPU: every
     rank's block is an allocation of this process, so the peer table holds
     plain device addresses.  Launch order keeps every wait already satisfied
     when it runs: all dispatches, then all expert steps, then all unpacks."""
     from moe_fused_inference_b200.ep import EPMoELayer, EPShard
     layers = [EPMoELayer(EPShard.from_layer(w, r, world), k, capacity, world=world, rank=r,
-                         transport="p2p", connect=False)
+                         transport="p2p", connect=False, logit_bias=logit_bias)
               for r in range(world)]
     bases = [L.xch.base for L in layers]
     for L in layers:
@@ -329,3 +329,29 @@ def test_ep_nccl_two_ranks(tmp_path, transport):
     for r in range(2):
         rel, same = np.load(os.path.join(tmp_path, f"nccl{r}.npy"))
         assert same == 1.0 and rel <= 1e-5
+
+
+def test_ep_p2p_zipf_bias_routes_like_single_gpu():
+    """The Zipf(1.2) logit bias of the skewed scaling runs: the expert-parallel
+    router applies it like the single-GPU layer (bit-identical top-k), and the
+    outputs agree to the rank-ordered summation."""
+    from moe_fused_inference_b200.layer import MoELayer
+    E, H, Mi, k, world = 128, 2048, 768, 8, 4
+    w = _layer_w(E, H, Mi, seed=23)
+    bias = torch.from_numpy(mx.zipf_bias(E, alpha=0.5, seed=3))
+    counts = [64, 40, 64, 9]
+    xs = [_x(t, H, 130 + r) for r, t in enumerate(counts)]
+    layers, outs = _emulate_p2p(w, xs, world, k, max(counts), logit_bias=bias.cuda())
+    try:
+        single = MoELayer(w, top_k=k, logit_bias=bias)
+        for r, x in enumerate(xs):
+            ref, topi, _ = single(x)
+            torch.cuda.synchronize()
+            T = x.shape[0]
+            assert torch.equal(layers[r].topi[:T], topi)
+            a, b = outs[r].cpu().numpy(), ref.cpu().numpy()
+            assert max_rel_err(a, b) <= 1e-5
+        assert _lib().load().mfi_device_error(1) == 0
+    finally:
+        for L in layers:
+            L.close()
