@@ -235,6 +235,48 @@ __global__ void __launch_bounds__(kQxThreads) quant_x8_kernel(RouteArgs a, int n
   }
 }
 
+// Compare-exchange: after it, (va, ia) is the better of the two in the
+// routers' order (larger value, ties to the lower index).
+__device__ __forceinline__ void cex(float& va, int& ia, float& vb, int& ib) {
+  const bool sw = better(vb, ib, va, ia);
+  const float t = va;
+  const int u = ia;
+  va = sw ? vb : va;
+  ia = sw ? ib : ia;
+  vb = sw ? t : vb;
+  ib = sw ? u : ib;
+}
+
+// Sort 8 entries best first (an optimal 19-comparator network, depth 6).
+__device__ __forceinline__ void sort8(float (&v)[8], int (&i)[8]) {
+#define MFI_CX(a, b) cex(v[a], i[a], v[b], i[b])
+  MFI_CX(0, 2); MFI_CX(1, 3); MFI_CX(4, 6); MFI_CX(5, 7);
+  MFI_CX(0, 4); MFI_CX(1, 5); MFI_CX(2, 6); MFI_CX(3, 7);
+  MFI_CX(0, 1); MFI_CX(2, 3); MFI_CX(4, 5); MFI_CX(6, 7);
+  MFI_CX(2, 4); MFI_CX(3, 5);
+  MFI_CX(1, 4); MFI_CX(3, 6);
+  MFI_CX(1, 2); MFI_CX(3, 4); MFI_CX(5, 6);
+#undef MFI_CX
+}
+
+// (v, i) <- the best 8 of two sorted runs, sorted: pairing a[m] with
+// b[7 - m] keeps the 8 best as a bitonic sequence, three half-cleaner
+// layers sort it.
+__device__ __forceinline__ void merge8(float (&v)[8], int (&i)[8], const float (&bv)[8],
+                                       const int (&bi)[8]) {
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    const bool sw = better(bv[7 - m], bi[7 - m], v[m], i[m]);
+    v[m] = sw ? bv[7 - m] : v[m];
+    i[m] = sw ? bi[7 - m] : i[m];
+  }
+#pragma unroll
+  for (int d = 4; d >= 1; d >>= 1)
+#pragma unroll
+    for (int m = 0; m < 8; ++m)
+      if ((m & d) == 0) cex(v[m], i[m], v[m + d], i[m + d]);
+}
+
 // Logits of token t in the routers' fixed order (lane l sums blocks l, l+32,
 // ... ascending, then the xor butterfly 16..1), plus the logit bias.  One
 // warp; used only when the scale span of the token could make the order
@@ -475,30 +517,27 @@ __global__ void __launch_bounds__(kRtThreads, 1) route_tc_kernel(RouteArgs a) {
       s_lg[r * kRtLgStride + e] = lg[j];
     }
     if (a.k <= kRtMaxK) {
-      // the best k of this thread's 32 experts, in the routers' order
-      // (larger first; the experts come in ascending order, so a tie keeps
-      // the earlier, lower one ahead); branch-free to keep the warp converged
-      float tv[kRtMaxK];
-      int ti[kRtMaxK];
+      // the best 8 of this thread's 32 experts in the routers' order (larger
+      // first, ties to the lower expert): each run of 8 sorted by a
+      // 19-comparator network, runs merged two at a time keeping the top 8
+      // (bitonic merge); branch-free, so the warp stays converged
+      float tv[8], gv[8];
+      int ti[8], gi[8];
 #pragma unroll
-      for (int m = 0; m < kRtMaxK; ++m) {
-        tv[m] = 0.0f;
-        ti[m] = -1;
+      for (int m = 0; m < 8; ++m) {
+        tv[m] = lg[m];
+        ti[m] = eg * 32 + m;
       }
+      sort8(tv, ti);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        float cv = lg[j];
-        int ci = eg * 32 + j;
+      for (int g = 1; g < 4; ++g) {
 #pragma unroll
-        for (int m = 0; m < kRtMaxK; ++m) {
-          const bool take = m < a.k && ci >= 0 && (ti[m] < 0 || better(cv, ci, tv[m], ti[m]));
-          const float ov = tv[m];
-          const int oi = ti[m];
-          tv[m] = take ? cv : ov;
-          ti[m] = take ? ci : oi;
-          cv = take ? ov : cv;
-          ci = take ? oi : ci;
+        for (int m = 0; m < 8; ++m) {
+          gv[m] = lg[g * 8 + m];
+          gi[m] = eg * 32 + g * 8 + m;
         }
+        sort8(gv, gi);
+        merge8(tv, ti, gv, gi);
       }
 #pragma unroll
       for (int m = 0; m < kRtMaxK; ++m)
