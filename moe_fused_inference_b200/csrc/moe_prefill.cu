@@ -5,20 +5,22 @@
 // per expert, gather its tokens on the host and call mxfp4_linear three
 // times) with one routed pass and no host synchronisation:
 //
-//   route_cluster_kernel   quantise, route, count tokens per expert and give
-//                          each (token, slot) its position among its expert's
-//                          tokens (atomic cursor)
+//   quant_x8_kernel,       quantise the tokens, route them on the tensor
+//   route_tc_kernel        cores (route_tc.cu; route_batch_kernel for other
+//                          router shapes), count tokens per expert and give
+//                          each (token, slot) its position among its
+//                          expert's tokens
 //   prefill_scatter_kernel place each token's quantised row (and its scale
 //                          atoms) at expert base + position, where the bases
 //                          are the prefix sum of the per-expert counts rounded
-//                          up to 128-row tiles (computed in every CTA)
+//                          up to 128-row tiles (computed once per CTA)
 //   moe_prefill_kernel     one persistent launch: gate/up items
 //                          (128-token tile, 64 gate + 64 up weight rows) with
 //                          SwiGLU + requantisation of h in the epilogue, then
 //                          down items (128-token tile, 128 output rows) whose
-//                          epilogue stores each (token, slot) row of y
-//   combine_kernel         the decode path's top-k combine (slot order, unfused
-//                          fp32 multiply and add)
+//                          epilogue stores each (token, slot) row of y in bf16
+//   combine_bf16_kernel    the top-k combine (slot order, unfused fp32
+//                          multiply and add of the bf16 rows)
 //
 //   D (128 tokens x 128 weight rows) += X_tile (128 x 256 K) . W_tile^T,
 //   tcgen05.mma.cta_group::1.kind::mxf4.block_scale, M = N = 128, K = 64.
