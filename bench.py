@@ -56,9 +56,10 @@ def parse():
     ap.add_argument("--tokens", type=int, default=64, help="decode tokens per GPU (T)")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="distinct MoE layers per step (48 = the model; fewer for profiling)")
-    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
-                    help="decode (BASELINE config 2, the headline) or prefill (config 3: "
-                         "T = 16384 by default, Zipf(1.2)-skewed routing)")
+    ap.add_argument("--workload", choices=["decode", "prefill", "linear"], default="decode",
+                    help="decode (BASELINE config 2, the headline), prefill (config 3: "
+                         "T = 16384 by default, Zipf(1.2)-skewed routing) or linear (the "
+                         "static decode projections and lm_head through lin_pq)")
     ap.add_argument("--zipf-alpha", type=float, default=0.5,
                     help="prefill: scale of the Zipf(1.2) per-expert logit bias")
     ap.add_argument("--ep-zipf", action="store_true",
@@ -396,9 +397,76 @@ def run_prefill(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def run_linear(args, world, rank, local):
+    """Static MXFP4 projections of a decode step through lin_pq (the lm_head,
+    151936 x 2048, and the attention projections q 4096 x 2048, k/v 512 x
+    2048, o 2048 x 4096) at T in {1, 8} rows: weight-stream GB/s against the
+    measured HBM peak.  Each shape runs 24 calls over distinct weight copies
+    (one for the 165 MB lm_head) captured in one CUDA graph, so the time is
+    the kernels' and the weights come from HBM."""
+    from moe_fused_inference_b200 import fp4_ext
+    from moe_fused_inference_b200.layer import quantize_rows
+
+    dev = torch.device("cuda", local if world > 1 else 0)
+    dec = fp4_ext.get_decode_ext()
+    g = torch.Generator(device=dev).manual_seed(11 + rank)
+    peak, peak_kind = measured_peaks()
+    shapes = {"lm_head": (151936, 2048), "q": (4096, 2048), "kv": (512, 2048), "o": (2048, 4096)}
+    res = {}
+    stream = torch.cuda.current_stream(dev)
+    for name, (n_out, k_in) in shapes.items():
+        nw = 1 if name == "lm_head" else 24
+        ws = [quantize_rows((torch.randn((n_out, k_in), generator=g, device=dev) * 0.02).bfloat16())
+              for _ in range(nw)]
+        w_bytes = n_out * (k_in // 2 + k_in // 32)
+        for T in (1, 8):
+            xq, xsc = quantize_rows(torch.randn((T, k_in), generator=g, device=dev).bfloat16())
+            reps = 24
+
+            def calls():
+                for i in range(reps):
+                    dec.lin_pq(xq, xsc, ws[i % nw][0], ws[i % nw][1], T, n_out, k_in)
+
+            graph = capture(dev, stream, calls, 1)
+            for _ in range(max(args.warmup, 1)):
+                graph.replay()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            us = e0.elapsed_time(e1) / (args.steps * reps) * 1e3
+            res[f"{name}_T{T}"] = {"us": us, "GBps": w_bytes / us / 1e3,
+                                   "frac": w_bytes / us / 1e3 / peak}
+            del graph
+        del ws
+        torch.cuda.empty_cache()
+    if rank != 0:
+        return
+    head = res["lm_head_T1"]
+    line = {
+        "metric": "MXFP4 lin_pq weight stream GB/s (decode lm_head, T=1)", "value": head["GBps"],
+        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": head["us"] * 24 / 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "mxfp4 (e2m1 x e2m1, fp32 accumulate)",
+        "data": "synthetic (random-init weights N(0,0.02), activations N(0,1), seeded)",
+        "config": {"workload": "decode static projections through lin_pq: lm_head 151936x2048, "
+                               "q 4096x2048, k/v 512x2048, o 2048x4096 at T in {1, 8}",
+                   "step": "24 lin_pq calls in one CUDA graph"},
+        "gpu_launches": 24 * args.steps,  # per shape: one kernel per lin_pq call
+        "roofline": {"bound": "hbm", "achieved": head["GBps"], "peak": peak, "unit": "GB/s",
+                     "frac": head["frac"], "peak_kind": peak_kind, "shapes": res},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_ours(args, world, rank, local):
     if args.workload == "prefill":
         return run_prefill(args, world, rank, local)
+    if args.workload == "linear":
+        return run_linear(args, world, rank, local)
     if world > 1:
         return run_ep(args, world, rank, local)
     from moe_fused_inference_b200.layer import MoELayer, random_layer_weights

@@ -187,6 +187,11 @@ cudaError_t launch_grouped_gemv(const GroupDesc* groups, const int* n_groups_dev
 cudaError_t launch_dense_gemv(const uint8_t* xq, const uint8_t* xsc, const uint8_t* wp,
                               const uint8_t* wsc, float* y, long long ldy, int M, int N, int Kp,
                               cudaStream_t stream) {
+  // a long weight stream, or enough rows to keep the CUDA cores busy: the
+  // tensor-core form (~100 KB in flight per SM) is faster; short matrices at
+  // one to a few rows stay on the GEMV (one tile per CTA, lower latency)
+  if ((N >= 16384 || M >= 6) && lin_tc_supported(xq, xsc, wp, wsc, M, Kp))
+    return launch_lin_tc(xq, xsc, wp, wsc, y, ldy, M, N, Kp, stream);
   DenseDesc d{wp, wsc, M, ldy};
   const int ng = (M + kDenseChunk - 1) / kDenseChunk;
   return launch_gemv_impl(nullptr, nullptr, ng, nullptr, d, xq, xsc, y, N, Kp, 1 << 30, stream);

@@ -117,6 +117,15 @@ constexpr int kRouteMaxPairs = 4096;
 constexpr int kBuildGroupsMaxP = 4096;
 
 cudaError_t launch_quant_rows(const QuantArgs& a, cudaStream_t stream);
+// Decode-sized dense GEMM on the tensor cores (lin_tc.cu): M <= 32
+// activation rows, Kp a multiple of 512 up to 4096; launch_dense_gemv uses it
+// when it applies.
+bool lin_tc_supported(const void* xq, const uint8_t* xsc, const void* wp, const uint8_t* wsc, int M,
+                      int Kp);
+cudaError_t launch_lin_tc(const uint8_t* xq, const uint8_t* xsc, const uint8_t* wp,
+                          const uint8_t* wsc, float* y, long long ldy, int M, int N, int Kp,
+                          cudaStream_t stream);
+
 // Prefill router on the tensor cores (E = 128, H a multiple of 128, <= 2048,
 // a.x8 set); launch_route picks it when it applies.
 bool route_tc_applies(const RouteArgs& a);
