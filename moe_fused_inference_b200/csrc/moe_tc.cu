@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, p.err, 1)) { ok = false; break; }
           uint8_t* st = ring + s * kStageBytes;
           mbar_expect_tx(&full[s], kStageBytes);
-          bulk_load(st, wb + size_t(ks) * kWBlock, kWBlock, &full[s]);
+          bulk_load_stream(st, wb + size_t(ks) * kWBlock, kWBlock, &full[s]);
           tma_load_2d(st + kOffB, tb, ks * 128, cd.row0, &full[s]);
           bulk_load(st + kOffSFB, sfb + (size_t(cd.row0 / kChunk) * kc + 2 * ks) * 512, kSF,
                     &full[s]);

@@ -86,6 +86,18 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// A bulk copy whose lines L2 should drop first: for data streamed exactly
+// once per call (the decode weight stream), so that what is reused across
+// calls (the routers, the activations) stays resident.
+__device__ __forceinline__ void bulk_load_stream(void* dst, const void* src, uint32_t bytes,
+                                                 uint64_t* bar) {
+  asm volatile(
+      "{\n .reg .b64 pol;\n createpolicy.fractional.L2::evict_first.b64 pol, 1.0;\n"
+      " cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], pol;\n}\n" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
 // Bring [src, src + bytes) into L2 without waiting (bytes a multiple of 16).
 __device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
