@@ -336,7 +336,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
 // shared memory.  The leader then runs top-k, the weights and the expert-row
 // claims.  Logits are bit-identical to route_kernel's.
 constexpr int kClusterThreads = 256;
-constexpr int kExpertsPerCta = 32;
+constexpr int kExpertsPerCta = 32;  // most experts per CTA (clusters of <= 8 for 256 experts)
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -393,14 +393,16 @@ __device__ void ep_finish_dispatch(const EpDispatch& ep, int H, int k, int n_lea
   }
 }
 
-template <int kMaxBlk>
+// kEPC experts per CTA: 16 (8-CTA clusters for 128 experts: each CTA loads
+// and reduces half as many router rows) or 32 (4-CTA clusters).
+template <int kMaxBlk, int kEPC>
 __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArgs a, int n_split) {
   tc::grid_dep_launch();
   extern __shared__ __align__(128) uint8_t s_w[];  // [32][H/2] router rows of this CTA
   __shared__ float s_logit[kMaxE];
   __shared__ __align__(16) uint8_t s_xq[kMaxBlk * 32 * 16];
   __shared__ __align__(16) uint8_t s_xsc[kMaxBlk * 32];
-  __shared__ __align__(16) uint8_t s_ws[kExpertsPerCta * kMaxBlk * 32];
+  __shared__ __align__(16) uint8_t s_ws[kEPC * kMaxBlk * 32];
   __shared__ __align__(8) uint64_t s_bar;
   const uint32_t crank = cluster_ctarank();
   const int t = blockIdx.x / n_split;
@@ -415,8 +417,8 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
     return;
   }
   const int nb = a.H >> 5;
-  const int e_begin = int(crank) * kExpertsPerCta;
-  const int n_e = min(kExpertsPerCta, a.E - e_begin);
+  const int e_begin = int(crank) * kEPC;
+  const int n_e = min(kEPC, a.E - e_begin);
   const uint32_t w_bytes = uint32_t(n_e) * uint32_t(a.H >> 1);
 
   // router rows first: their loads should not queue behind the weight
@@ -498,8 +500,10 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
       xs[j] = s_xsc[b];
     }
   }
-  constexpr int kU = 4;
   constexpr int kWarps = kClusterThreads / 32;
+  constexpr int kU = kEPC / kWarps;  // experts per warp
+  static_assert(kU == 2 || kU == 4, "experts per warp");
+  constexpr int kLog = kU == 4 ? 2 : 1;
   double acc[kU];
 #pragma unroll
   for (int u = 0; u < kU; ++u) {
@@ -537,8 +541,9 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
     }
   }
   cluster_wait_acquire();  // the leader has started (its shared memory exists)
-  if ((lane & 7) == 0) {
-    const int el = warp + (lane >> 3) * kWarps;
+  // after kLog halving steps lane l holds value l >> (5 - kLog)
+  if ((lane & ((32 >> kLog) - 1)) == 0) {
+    const int el = warp + (lane >> (5 - kLog)) * kWarps;
     if (have_w && el < n_e) st_cluster_f32(&s_logit[e_begin + el], 0, float(acc[0]));
   }
   cluster_arrive_release();
@@ -837,12 +842,13 @@ static cudaError_t launch_route_batch(const RouteArgs& a, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
-template <int kMaxBlk>
-static cudaError_t launch_route_cluster(const RouteArgs& a, cudaStream_t stream) {
-  const int n_split = (a.E + kExpertsPerCta - 1) / kExpertsPerCta;  // <= 8
-  const size_t smem = size_t(kExpertsPerCta) * (a.H >> 1);
+template <int kMaxBlk, int kEPC>
+static cudaError_t launch_route_cluster_n(const RouteArgs& a, cudaStream_t stream) {
+  const int n_split = (a.E + kEPC - 1) / kEPC;  // <= 8
+  const size_t smem = size_t(kEPC) * (a.H >> 1);
   {
-    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(route_cluster_kernel<kMaxBlk>), smem);
+    cudaError_t e =
+        ensure_dynamic_smem(reinterpret_cast<const void*>(route_cluster_kernel<kMaxBlk, kEPC>), smem);
     if (e != cudaSuccess) return e;
   }
   cudaLaunchConfig_t cfg{};
@@ -858,7 +864,15 @@ static cudaError_t launch_route_cluster(const RouteArgs& a, cudaStream_t stream)
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, route_cluster_kernel<kMaxBlk>, a, n_split);
+  return cudaLaunchKernelEx(&cfg, route_cluster_kernel<kMaxBlk, kEPC>, a, n_split);
+}
+
+template <int kMaxBlk>
+static cudaError_t launch_route_cluster(const RouteArgs& a, cudaStream_t stream) {
+  // small batches: 8-CTA clusters halve each CTA's router rows (the latency
+  // of a few tokens); at T = 32/64 the 4-CTA clusters measured faster
+  return a.E <= 8 * 16 && a.T <= 16 ? launch_route_cluster_n<kMaxBlk, 16>(a, stream)
+                                    : launch_route_cluster_n<kMaxBlk, kExpertsPerCta>(a, stream);
 }
 
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t stream) {
