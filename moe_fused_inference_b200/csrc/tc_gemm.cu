@@ -192,6 +192,169 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Persistent form for N a multiple of 4 (the dense projections at prefill
+// sizes; weight rows past N read as zeros through the tensor map and their
+// columns are not stored): one CTA per SM walks tiles of 128 x 128 (consecutive tiles share
+// the weight tile: m inner, n outer), 5-stage ring, three rotating
+// 128-column accumulators, so a tile's epilogue overlaps the next tiles'
+// MMAs.  The epilogue takes the tile's 128 columns into registers, releases
+// the accumulator, and stores through a per-warp shared-memory transpose so
+// every store instruction writes whole 128-byte row segments.
+// ---------------------------------------------------------------------------
+constexpr int kPBN = 128;
+constexpr int kPStagesG = 5;
+constexpr int kPStageG = kABytes + kBM * kBK / 2 + 2 * 1024;  // A 16 KB, B 16 KB, SFA 1 KB, SFB 1 KB
+constexpr int kPAccG = 3;
+constexpr uint32_t kPTmemSFG = kPAccG * 128;                  // + 16 per ring slot
+static_assert(kPTmemSFG + 16 * kPStagesG <= 512, "scale columns exceed the allocation");
+constexpr int kPOutStageG = 32 * 32 * 4;                       // per epilogue warp
+
+size_t tc_gemm_p_smem_bytes() {
+  return 1024 + size_t(kPStagesG) * kPStageG + 4 * size_t(kPOutStageG) +
+         8 * (2 * kPStagesG + 2 * kPAccG) + 16;
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    tc_gemm_p_kernel(const __grid_constant__ CUtensorMap tma_a,
+                     const __grid_constant__ CUtensorMap tma_b, TcGemmArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* out_stage = ring + size_t(kPStagesG) * kPStageG;
+  uint64_t* full = reinterpret_cast<uint64_t*>(out_stage + 4 * kPOutStageG);
+  uint64_t* empty = full + kPStagesG;
+  uint64_t* acc_full = empty + kPStagesG;
+  uint64_t* acc_empty = acc_full + kPAccG;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + kPAccG);
+  constexpr int kOffB = kABytes, kOffSFA = kABytes + kBM * kBK / 2, kOffSFB = kOffSFA + 1024;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int k_tiles = (p.Kp + kBK - 1) / kBK;
+  const int n_m = (p.M + kBM - 1) / kBM, n_n = (p.N + kPBN - 1) / kPBN;
+  const int n_tiles = n_m * n_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPStagesG; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < kPAccG; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      prefetch_tmap(&tma_a);
+      prefetch_tmap(&tma_b);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+        const int m = t % n_m, n = t / n_m;
+        for (int kt = 0; kt < k_tiles; ++kt, ++it) {
+          const int s = int(it % kPStagesG);
+          if (!mbar_wait(&empty[s], ((it / kPStagesG) & 1) ^ 1, p.err, 1)) { ok = false; break; }
+          uint8_t* st = ring + size_t(s) * kPStageG;
+          mbar_expect_tx(&full[s], kPStageG);
+          tma_load_2d(st, &tma_a, kt * (kBK / 2), m * kBM, &full[s]);
+          tma_load_2d(st + kOffB, &tma_b, kt * (kBK / 2), n * kPBN, &full[s]);
+          bulk_load(st + kOffSFA, p.sfa + (size_t(m) * p.kc_pad + 2 * kt) * 512, 1024, &full[s]);
+          bulk_load(st + kOffSFB, p.sfb + (size_t(n) * p.kc_pad + 2 * kt) * 512, 1024, &full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      uint32_t it = 0, ti = 0;
+      bool ok = true;
+      const uint32_t idesc0 = make_idesc_mxf4(kBM, kPBN, 0, 0);
+      const uint32_t idesc2 = make_idesc_mxf4(kBM, kPBN, 2, 2);
+      for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++ti) {
+        const uint32_t buf = ti % kPAccG;
+        if (!mbar_wait(&acc_empty[buf], ((ti / kPAccG) & 1) ^ 1, p.err, 2)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + buf * 128;
+        for (int kt = 0; kt < k_tiles; ++kt, ++it) {
+          const int s = int(it % kPStagesG);
+          if (!mbar_wait(&full[s], (it / kPStagesG) & 1, p.err, 2)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t base = smem_u32(ring + size_t(s) * kPStageG);
+          const uint32_t sfa = tmem + kPTmemSFG + 16 * s, sfb = sfa + 8;
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            tmem_cp_sf(sfa + 4 * c, make_sdesc(base + kOffSFA + c * 512, 0, 128, kLayoutNone));
+            tmem_cp_sf(sfb + 4 * c, make_sdesc(base + kOffSFB + c * 512, 0, 128, kLayoutNone));
+          }
+#pragma unroll
+          for (int kb = 0; kb < 4; ++kb) {
+            const int c = kb >> 1;
+            const uint32_t byte = uint32_t(kb & 1) * 2;
+            mma_mxf4(d, make_sdesc(base + kb * 32, 16, 1024, kLayoutSW128),
+                     make_sdesc(base + kOffB + kb * 32, 16, 1024, kLayoutSW128),
+                     byte ? idesc2 : idesc0, (kt | kb) != 0 ? 1u : 0u,
+                     (sfa + 4 * c) | (byte << 30), (sfb + 4 * c) | (byte << 30));
+          }
+          tc_commit(&empty[s]);
+        }
+        if (ok) tc_commit(&acc_full[buf]);
+      }
+    }
+  } else {
+    const int quad = warp & 3;
+    uint4* stg = reinterpret_cast<uint4*>(out_stage + (warp - 2) * kPOutStageG);
+    uint32_t ti = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++ti) {
+      const int m = t % n_m, n = t / n_m;
+      const uint32_t buf = ti % kPAccG;
+      if (!mbar_wait(&acc_full[buf], (ti / kPAccG) & 1, p.err, 3)) break;
+      tc_fence_after();
+      uint32_t r[4][32];
+      const uint32_t ta = tmem + (uint32_t(quad * 32) << 16) + buf * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(ta + c * 32, r[c]);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      // lane l holds row row0 + l; 16-byte chunk q of row l sits at q ^ (l & 7)
+      const int row0 = m * kBM + quad * 32;
+      const int sub = lane >> 3, ch = lane & 7;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          stg[lane * 8 + (q ^ (lane & 7))] =
+              make_uint4(r[c][4 * q], r[c][4 * q + 1], r[c][4 * q + 2], r[c][4 * q + 3]);
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int rr = 4 * i + sub;
+          const int row = row0 + rr;
+          const int col = n * kPBN + c * 32 + ch * 4;
+          const uint4 v = stg[rr * 8 + (ch ^ (rr & 7))];
+          if (row < p.M && col < p.N)
+            *reinterpret_cast<uint4*>(p.y + (long long)row * p.ldy + col) = v;
+        }
+        __syncwarp();
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Row-major E8M0 codes (R, nb) -> 512-byte atoms.  Atom (rb, kc) holds rows
 // rb*128 .. rb*128+127 and K blocks kc*4 .. kc*4+3; inside it byte
 // (r % 32)*16 + ((r % 128) / 32)*4 + (k % 4).  This is the layout that one
@@ -271,6 +434,19 @@ cudaError_t launch_tc_gemm(const uint8_t* a, const uint8_t* sfa_atoms, const uin
   p.M = M; p.N = N; p.Kp = Kp;
   p.kc_pad = 2 * ((Kp + kBK - 1) / kBK);
   p.sfa = sfa_atoms; p.sfb = sfb_atoms; p.y = y; p.ldy = ldy; p.err = err;
+  if (N % 4 == 0 && ldy % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
+    CUtensorMap tb2;
+    if (!make_tmap(&tb2, b, uint64_t(Kp / 2), uint64_t(N), kPBN)) return cudaErrorInvalidValue;
+    const size_t smem2 = tc_gemm_p_smem_bytes();
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(tc_gemm_p_kernel), smem2);
+    if (e != cudaSuccess) return e;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int tiles = (M + kBM - 1) / kBM * ((N + kPBN - 1) / kPBN);
+    tc_gemm_p_kernel<<<tiles < sms ? tiles : sms, kGemmThreads, smem2, stream>>>(ta, tb2, p);
+    return cudaGetLastError();
+  }
   dim3 grid((N + kBN - 1) / kBN, (M + kBM - 1) / kBM);
   tc_gemm_mxf4_kernel<<<grid, kGemmThreads, smem, stream>>>(ta, tb, p);
   return cudaGetLastError();

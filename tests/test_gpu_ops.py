@@ -56,7 +56,11 @@ def test_forward_mxfp4_linear(M, N, K):
                                    (1, 4096, 2048), (2, 2048, 2048), (64, 128, 2048),
                                    # the streaming GEMV (M <= 8, K % 512 == 0): partial last
                                    # tile, two-stage ring at K = 4096, several tiles per CTA
-                                   (7, 999, 2048), (8, 1000, 4096), (3, 20000, 2048)])
+                                   (7, 999, 2048), (8, 1000, 4096), (3, 20000, 2048),
+                                   # the persistent prefill GEMM (N % 4 == 0): one partial
+                                   # K tile; several tiles per CTA with every accumulator
+                                   # reused; a partial last weight tile
+                                   (300, 384, 100), (4700, 2048, 256), (200, 1000, 512)])
 def test_lin_pq(M, N, K):
     rng = np.random.default_rng(1 + M + N + K)
     wp, wc, twp, twc = make_w(rng, N, K)
