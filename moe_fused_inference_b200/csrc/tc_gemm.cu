@@ -202,7 +202,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // every store instruction writes whole 128-byte row segments.
 // ---------------------------------------------------------------------------
 constexpr int kPBN = 128;
-constexpr int kPStagesG = 5;
+#ifndef MFI_PG_STAGES
+#define MFI_PG_STAGES 5
+#endif
+constexpr int kPStagesG = MFI_PG_STAGES;
 constexpr int kPStageG = kABytes + kBM * kBK / 2 + 2 * 1024;  // A 16 KB, B 16 KB, SFA 1 KB, SFB 1 KB
 constexpr int kPAccG = 3;
 constexpr uint32_t kPTmemSFG = kPAccG * 128;                  // + 16 per ring slot
