@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // Persistent form for N a multiple of 4 (the dense projections at prefill
 // sizes; weight rows past N read as zeros through the tensor map and their
 // columns are not stored): one CTA per SM walks tiles of 128 x 128 (consecutive tiles share
-// the weight tile: m inner, n outer), 5-stage ring, three rotating
+// the weight tile: m inner, n outer), 6-stage ring (226 KB of shared memory), three rotating
 // 128-column accumulators, so a tile's epilogue overlaps the next tiles'
 // MMAs.  The epilogue takes the tile's 128 columns into registers, releases
 // the accumulator, and stores through a per-warp shared-memory transpose so
@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // ---------------------------------------------------------------------------
 constexpr int kPBN = 128;
 #ifndef MFI_PG_STAGES
-#define MFI_PG_STAGES 5
+#define MFI_PG_STAGES 6
 #endif
 constexpr int kPStagesG = MFI_PG_STAGES;
 constexpr int kPStageG = kABytes + kBM * kBK / 2 + 2 * 1024;  // A 16 KB, B 16 KB, SFA 1 KB, SFB 1 KB
