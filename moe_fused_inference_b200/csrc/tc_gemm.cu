@@ -272,6 +272,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           bulk_load(st + kOffSFB, p.sfb + (size_t(n) * p.kc_pad + 2 * kt) * 512, 1024, &full[s]);
         }
       }
+      if (!ok) {
+        // drain our own copies before the CTA can exit
+        for (uint32_t j = (it > uint32_t(kPStagesG) ? it - kPStagesG : 0); j < it; ++j)
+          mbar_wait(&full[j % kPStagesG], (j / kPStagesG) & 1, nullptr, 0);
+      }
     }
   } else if (warp == 1) {
     if (elect_one()) {
