@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Benchmark of the MXFP4 grouped-MoE expert path on B200.
 
-Workload (the headline metric's configuration): one
+Headline (the metric's configuration): one
 Qwen3-30B-A3B-shaped MoE layer (H = 2048, 128 experts, top-8, Mi = 768,
 SwiGLU experts, MXFP4 weights N(0, 0.02) quantised on the device) at decode
 size T tokens per GPU (default 64), bf16 N(0, 1) activations quantised on the
@@ -12,19 +12,36 @@ MoE layers, each with its own weights (48 x 320.9 MB = 15.4 GB resident), so
 consecutive layer calls never find their weights in the 126 MB L2.  ``value``
 is MoE-layer token throughput: tokens x layer calls / second, over all GPUs.
 
+The same single-GPU line also carries every other configuration of the path:
+  decode_sweep   T in {1, 8, 32, 64}: per-layer time, per-stage times, the
+                 expert kernel's and the whole layer's HBM roofline fraction;
+  prefill        BASELINE config 3: T in {2048, 16384} with Zipf(1.2)-skewed
+                 routing (FP4 tensor fraction, HBM fraction, per-stage times)
+                 and the dense q/k/v/o mxfp4_linear GEMMs at T = 16384;
+  dropin         the reference's own call sequence, unchanged
+                 (runtime/model_runner_v2.py:185-207: prequant -> lin_pq router
+                 -> host softmax/top-k -> .tolist() -> host pointer tables ->
+                 moe_gateup -> moe_down -> moe_combine) through the drop-in
+                 fp4_ext module, with its kernel-only HBM roofline;
+  cpu_baseline   the reference's CPU dequantise-then-matmul layer
+                 (runtime/model_runner.py:99-132, ported in oracle/moe_ref.py)
+                 at T = 64 and at config 1's T = 4.
+
 Arms:
   default            this library, inputs resident in HBM (``value``) and end to
                      end through ``MoELayer.forward`` with pinned host buffers
                      (``e2e``: H2D of the step's activations, D2H of its outputs);
-  --impl reference   the reference's CPU dequantise-then-matmul path
-                     (runtime/model_runner.py:99-132, ported in oracle/moe_ref.py)
-                     on the host cores, same metric and config, rank 0 only.
+  --impl reference   the reference's CPU dequantise-then-matmul path on the host
+                     cores, same metric and config, rank 0 only.
 
 Multi-GPU (torchrun, N ranks): expert parallelism (BASELINE config 5's
 sharding) — each rank holds 128/N experts of every layer and the full router,
-routes its own T tokens, and dispatch / combine are NCCL all-to-alls over
-NVLink (moe_fused_inference_b200/ep.py).  Per-GPU tokens stay at T (weak
-scaling); the step is timed on the device and reduced with a max over ranks.
+routes its own T tokens, and the token exchange runs over peer memory: the
+router stores each token's row straight into the owning ranks' receive
+buffers over NVLink and the experts store their weighted sums straight back
+(the default, ``--ep-transport p2p``), or two NCCL all-to-alls
+(``--ep-transport nccl``).  Per-GPU tokens stay at T (weak scaling); the step
+is timed on the device and reduced with a max over ranks.
 """
 
 from __future__ import annotations
@@ -35,6 +52,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import torch
@@ -46,6 +64,8 @@ H, MI, E, TOPK = 2048, 768, 128, 8
 N_LAYERS = 48
 EXPERT_BYTES = 3 * (MI * H // 2 + MI * H // 32)  # 2,506,752 B packed gate+up+down
 ROUTER_BYTES = E * (H // 2 + H // 32)            # 139,264 B (MXFP4 router)
+FLOP_TOKEN = TOPK * (2 * H * 2 * MI + 2 * MI * H) + 2 * H * E  # experts + router
+FP4_PEAK = 9000.0  # dense MXFP4 tensor TFLOP/s, nominal (no measured FP4 figure on this pool)
 
 
 def parse():
@@ -57,9 +77,12 @@ def parse():
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="distinct MoE layers per step (48 = the model; fewer for profiling)")
     ap.add_argument("--workload", choices=["decode", "prefill", "linear"], default="decode",
-                    help="decode (BASELINE config 2, the headline), prefill (config 3: "
-                         "T = 16384 by default, Zipf(1.2)-skewed routing) or linear (the "
-                         "static decode projections and lm_head through lin_pq)")
+                    help="decode (BASELINE config 2, the headline, with every other "
+                         "configuration in the same line), prefill (config 3 alone: T = 16384 "
+                         "by default, Zipf(1.2)-skewed routing) or linear (the static decode "
+                         "projections and lm_head through lin_pq)")
+    ap.add_argument("--headline-only", action="store_true",
+                    help="decode: skip the sweep, prefill, drop-in and T=4 blocks")
     ap.add_argument("--zipf-alpha", type=float, default=0.5,
                     help="prefill: scale of the Zipf(1.2) per-expert logit bias")
     ap.add_argument("--ep-zipf", action="store_true",
@@ -71,8 +94,8 @@ def parse():
     ap.add_argument("--no-graph", action="store_true",
                     help="time plain launches instead of a captured CUDA graph")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-sample-s", type=float, default=15.0,
-                    help="seconds of CPU work for the cpu_baseline sample")
+    ap.add_argument("--cpu-sample-s", type=float, default=12.0,
+                    help="seconds of CPU work for each cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -110,7 +133,8 @@ def max_over_ranks(v: float, world: int) -> float:
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle sampling during the timed region."""
+    """nvidia-smi clocks/throttle sampling during the timed region (samples
+    go to a temporary file that is removed afterwards)."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -119,11 +143,11 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+        fd, self.path = tempfile.mkstemp(prefix=f"mfi_clocks_gpu{gpu_index}_", suffix=".csv")
+        os.close(fd)
 
     def start(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
@@ -141,6 +165,7 @@ class ClockSampler:
 
     def stop(self):
         if self.proc is None:
+            self._remove()
             return None
         self.proc.terminate()
         try:
@@ -157,6 +182,7 @@ class ClockSampler:
                 rows.append((float(p[1]), float(p[2]), float(p[3]), p[5:9]))
             except ValueError:
                 continue
+        self._remove()
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -164,6 +190,12 @@ class ClockSampler:
         loaded = [r for r in rows if r[2] > 200.0] or rows
         return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": rows[0][1],
                 "reasons": reasons, "samples": len(rows), "samples_under_load": len(loaded)}
+
+    def _remove(self):
+        try:
+            os.remove(self.path)
+        except OSError:
+            pass
 
 
 def measured_peaks():
@@ -182,6 +214,12 @@ def committed_traffic():
         except Exception:
             return None
     return None
+
+
+def decode_layer_bytes(uniq_per_layer: float, T: int) -> float:
+    """Algorithmic HBM bytes of one decode layer call: every expert with
+    tokens once, the MXFP4 router, bf16 in, fp32 out, ids and weights."""
+    return uniq_per_layer * EXPERT_BYTES + ROUTER_BYTES + T * H * 2 + T * H * 4 + T * TOPK * 8
 
 
 # ---------------------------------------------------------------------------
@@ -222,7 +260,7 @@ def time_cpu_layer(layer, T, seconds=None, calls=None):
         layer.forward(x)
         n += 1
         el = time.perf_counter() - t0
-        if (calls is not None and n >= calls) or (calls is None and (el >= seconds or n >= 1000)):
+        if (calls is not None and n >= calls) or (calls is None and (el >= seconds or n >= 2000)):
             break
     return T * n / el, n, el / n
 
@@ -242,7 +280,6 @@ def run_reference(args, world, rank):
     per_call = time.perf_counter() - t0
     steps = max(1, min(args.steps, int(120.0 / max(per_call, 1e-6))))
     tok_s, n, per = time_cpu_layer(layer, T, calls=steps)
-    cores = torch.get_num_threads()
     line = {
         "impl": "reference", "metric": "MXFP4 MoE layer tokens/s (decode)", "value": tok_s,
         "unit": "tokens/s", "n_gpus": args.gpus, "steps": n, "warmup": args.warmup,
@@ -250,7 +287,8 @@ def run_reference(args, world, rank):
         "vs_baseline": None, "dtype": "bf16 (dequantised MXFP4 weights)", "data": "synthetic",
         "config": {"workload": f"decode MoE layer, T={T} tokens, H=2048, E=128, top-8, Mi=768",
                    "step": "one MoE layer call on the host CPU", "l2": "n/a (CPU)"},
-        "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": "port",
+        "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": torch.get_num_threads(),
+                         "cpu_count": os.cpu_count(), "kind": "port",
                          "sample": f"{n} layer calls x T={T} tokens, torch CPU bf16 "
                                    "(runtime/model_runner.py:99-132 ported)"},
         "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -260,9 +298,10 @@ def run_reference(args, world, rank):
 
 
 # ---------------------------------------------------------------------------
-def timed_region(args, world, dev, stream, step):
-    """Clock-sampled, barrier-bracketed device timing of args.steps calls of
-    step(); returns (max-over-ranks ms, clocks)."""
+def timed_region(args, world, dev, stream, step, steps=None):
+    """Clock-sampled, barrier-bracketed device timing of `steps` (default
+    args.steps) calls of step(); returns (max-over-ranks ms, clocks)."""
+    steps = args.steps if steps is None else steps
     sampler = ClockSampler(dev.index if dev.index is not None else 0)
     sampler.start()
     barrier(world)
@@ -270,13 +309,25 @@ def timed_region(args, world, dev, stream, step):
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
-    for _ in range(args.steps):
+    for _ in range(steps):
         step()
     t1.record(stream)
     torch.cuda.synchronize(dev)
     barrier(world)
     clocks = sampler.stop()
     return max_over_ranks(t0.elapsed_time(t1), world), clocks
+
+
+def event_time(dev, stream, step, steps):
+    """Device time (ms) of `steps` calls of step() between two events."""
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1)
 
 
 def capture(dev, stream, fn, warm):
@@ -295,103 +346,289 @@ def capture(dev, stream, fn, warm):
     return graph
 
 
-def cpu_baseline(args, T, weights):
-    cpu_layer = make_cpu_layer(weights)
+def cpu_baseline(args, T, cpu_layer):
     tok_s, n, _ = time_cpu_layer(cpu_layer, T, seconds=args.cpu_sample_s)
-    return {"value": tok_s, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+    return {"value": tok_s, "unit": "tokens/s", "cores": torch.get_num_threads(),
+            "cpu_count": os.cpu_count(), "kind": "port",
             "sample": f"{n} layer calls x T={T} tokens, torch CPU bf16 with layer 0's weights "
                       "dequantised (runtime/model_runner.py:99-132 ported)"}
 
 
-def run_prefill(args, world, rank, local):
-    """one prefill-sized MoE layer call per layer (T tokens,
-    default 16384) with Zipf(1.2)-skewed routing; FLOP rate of the layer
-    against the dense FP4 tensor peak.  Single GPU; under torchrun every rank
-    runs its own copy (weak scaling)."""
-    from moe_fused_inference_b200.layer import MoELayer, random_layer_weights
-    from oracle import mxfp4 as mx
+# ---------------------------------------------------------------------------
+class DecodePoint:
+    """The decode step at T tokens: NL layer calls of the fused layer with
+    distinct weights, captured in one CUDA graph, plus a second graph that
+    records the library's stage events for the per-kernel breakdown."""
 
-    dev = torch.device("cuda", local if world > 1 else 0)
-    T = args.tokens if args.tokens != 64 else 16384
-    NL = args.layers if args.layers != N_LAYERS else 4
-    bias = torch.from_numpy(mx.zipf_bias(E, args.zipf_alpha, seed=3))
-    layers = [MoELayer(random_layer_weights(E, H, MI, 0.02, seed=l, device=dev), TOPK,
-                       logit_bias=bias) for l in range(NL)]
-    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    def __init__(self, layers, T, dev, stream, seed=7, graph=True):
+        self.layers, self.T, self.dev, self.stream = layers, T, dev, stream
+        NL = len(layers)
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.X = torch.randn((NL, T, H), generator=g, device=dev).bfloat16()
+        self.out = torch.empty((NL, T, H), dtype=torch.float32, device=dev)
+        self.topi = torch.empty((NL, T, TOPK), dtype=torch.int32, device=dev)
+        self.topw = torch.empty((NL, T, TOPK), dtype=torch.float32, device=dev)
+        self.evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(NL)]
+        for row in self.evs:
+            for e in row:
+                e.record(stream)  # creates the event handles before the library records them
+        self.graph = self.graph_ev = None
+        self.use_graph = graph
+
+    def step(self, with_events=False):
+        for l, layer in enumerate(self.layers):
+            layer(self.X[l], out=self.out[l], topi=self.topi[l], topw=self.topw[l],
+                  events=self.evs[l] if with_events else None)
+
+    def prepare(self, warmup):
+        for _ in range(warmup):
+            self.step()
+        torch.cuda.synchronize(self.dev)
+        # The timed graph has no stage events (each event node costs the
+        # timeline ~2-3 us); the graph with the stage events is replayed once
+        # afterwards for the per-kernel breakdown.
+        if self.use_graph:
+            self.graph = capture(self.dev, self.stream, self.step, 1)
+            self.graph_ev = capture(self.dev, self.stream, lambda: self.step(True), 0)
+            for _ in range(warmup):
+                self.graph.replay()
+            torch.cuda.synchronize(self.dev)
+
+    def run(self):
+        (self.graph.replay if self.graph is not None else self.step)()
+
+    def breakdown(self):
+        """Per-step stage times (ms, summed over the layers) and unique experts
+        per layer, from one replay of the stage-event graph."""
+        if self.graph_ev is not None:
+            self.graph_ev.replay()
+        else:
+            self.step(True)
+        torch.cuda.synchronize(self.dev)
+        NL = len(self.layers)
+        stage = [0.0] * 5
+        for l in range(NL):
+            for i in range(5):
+                stage[i] += self.evs[l][i].elapsed_time(self.evs[l][i + 1])
+        uniq = sum(int(torch.unique(self.topi[l]).numel()) for l in range(NL)) / NL
+        return stage, uniq
+
+    def release(self):
+        self.graph = self.graph_ev = None
+
+
+def decode_summary(pt: DecodePoint, ms_per_step: float, peak: float) -> dict:
+    """Per-layer time, stage times and the HBM roofline of one decode point."""
+    NL = len(pt.layers)
+    stage, uniq = pt.breakdown()
+    gemm_ms = stage[2] + stage[3]
+    w_bytes = uniq * EXPERT_BYTES
+    layer_bytes = decode_layer_bytes(uniq, pt.T)
+    us_layer = ms_per_step / NL * 1e3
+    exp_gbs = w_bytes / (gemm_ms / NL / 1e3) / 1e9
+    lay_gbs = layer_bytes / (us_layer / 1e6) / 1e9
+    return {"tokens_per_s": pt.T * NL / (ms_per_step / 1e3), "us_per_layer": us_layer,
+            "unique_experts_per_layer": uniq,
+            "stage_us_per_layer": {"route": stage[0] / NL * 1e3, "experts": gemm_ms / NL * 1e3,
+                                   "combine": stage[4] / NL * 1e3},
+            "experts_kernel": {"bytes": w_bytes, "GBps": exp_gbs, "frac": exp_gbs / peak},
+            "layer": {"bytes": layer_bytes, "GBps": lay_gbs, "frac": lay_gbs / peak}}
+
+
+# ---------------------------------------------------------------------------
+def prefill_point(T, NL, dev, stream, zipf_alpha, steps, warmup, seed_base=100, layer_weights=None):
+    """BASELINE config 3 at T tokens: NL prefill layer calls (distinct weights,
+    Zipf(1.2)-skewed routing), plain launches; returns the summary dict."""
+    from moe_fused_inference_b200.layer import MoELayer, random_layer_weights
+    from moe_fused_inference_b200.synthetic import zipf_bias
+
+    bias = torch.from_numpy(zipf_bias(E, zipf_alpha, seed=3))
+    if layer_weights is None:
+        layer_weights = [random_layer_weights(E, H, MI, 0.02, seed=seed_base + l, device=dev)
+                         for l in range(NL)]
+    layers = [MoELayer(w, TOPK, logit_bias=bias) for w in layer_weights[:NL]]
+    g = torch.Generator(device=dev).manual_seed(7)
     X = torch.randn((NL, T, H), generator=g, device=dev).bfloat16()
     out = torch.empty((NL, T, H), dtype=torch.float32, device=dev)
     topi = torch.empty((NL, T, TOPK), dtype=torch.int32, device=dev)
     topw = torch.empty((NL, T, TOPK), dtype=torch.float32, device=dev)
-    stream = torch.cuda.current_stream(dev)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(NL)]
 
-    def step():
+    def step(with_events=False):
+        # T * top_k > 4096: mfi_moe_layer takes the prefill path by itself
         for l in range(NL):
-            layers[l](X[l], out=out[l], topi=topi[l], topw=topw[l])
+            layers[l](X[l], out=out[l], topi=topi[l], topw=topw[l],
+                      events=evs[l] if with_events else None)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
+    ms = event_time(dev, stream, step, steps)
+    ms_per_layer = ms / steps / NL
+    step(True)
     torch.cuda.synchronize(dev)
-    ms, clocks = timed_region(args, world, dev, stream, step)
-    ms_per_step = ms / args.steps
-    flop_tok = TOPK * (2 * H * 2 * MI + 2 * MI * H) + 2 * H * E   # experts + router
-    flops = flop_tok * T * NL
-    tflops = flops / (ms_per_step / 1e3) / 1e12
+    names = ["route", "scatter", "experts", "combine"]
+    st = {n: 0.0 for n in names}
+    for l in range(NL):
+        t = [evs[l][i].elapsed_time(evs[l][i + 1]) for i in range(5)]
+        st["route"] += t[0]
+        st["scatter"] += t[1]
+        st["experts"] += t[2] + t[3]
+        st["combine"] += t[4]
     counts = torch.bincount(topi[0].flatten().long(), minlength=E).float()
-    fp4_peak = 9000.0  # dense MXFP4 tensor peak, nominal (no measured FP4 figure on this pool)
-    # algorithmic bytes of one layer call: every expert with tokens once, the
-    # MXFP4 router, bf16 in, fp32 out, ids and weights
+    flops = FLOP_TOKEN * T
+    tflops = flops / (ms_per_layer / 1e3) / 1e12
+    exp_flops = TOPK * (2 * H * 2 * MI + 2 * MI * H) * T
+    exp_ms = st["experts"] / NL
+    hbm_peak, hbm_kind = measured_peaks()
     hbm_bytes = (int((counts > 0).sum()) * EXPERT_BYTES + ROUTER_BYTES + T * H * 2 + T * H * 4
                  + T * TOPK * 8)
-    hbm_gbs = hbm_bytes / (ms_per_step / NL / 1e3) / 1e9
-    hbm_peak, hbm_kind = measured_peaks()
+    hbm_gbs = hbm_bytes / (ms_per_layer / 1e3) / 1e9
+    res = {"tokens_per_s": T / (ms_per_layer / 1e3), "us_per_layer": ms_per_layer * 1e3,
+           "flops_per_layer": flops, "tflops": tflops, "frac": tflops / FP4_PEAK,
+           "stage_us_per_layer": {k: v / NL * 1e3 for k, v in st.items()},
+           "experts_kernel": {"us": exp_ms * 1e3, "tflops": exp_flops / (exp_ms / 1e3) / 1e12,
+                              "frac": exp_flops / (exp_ms / 1e3) / 1e12 / FP4_PEAK},
+           "hbm": {"bytes_per_layer": hbm_bytes, "GBps": hbm_gbs, "frac": hbm_gbs / hbm_peak,
+                   "peak_kind": hbm_kind},
+           "expert_load_max_over_mean": float(counts.max() / counts.mean()),
+           "experts_with_tokens": int((counts > 0).sum()),
+           "layers": NL, "steps": steps}
+    del layers, X, out, topi, topw
+    torch.cuda.empty_cache()
+    return res
 
-    # ---- dense mxfp4_linear of the attention projections at T tokens (config 3):
-    # lin_pq on pre-quantised activations (the GEMM incl. its scale re-layout)
+
+def dense_projections(T, dev, stream, seed=5):
+    """Dense mxfp4_linear of the attention projections at T tokens (config 3)
+    through lin_pq on pre-quantised activations."""
     from moe_fused_inference_b200 import fp4_ext
     from moe_fused_inference_b200.layer import quantize_rows
+
     dec = fp4_ext.get_decode_ext()
+    g = torch.Generator(device=dev).manual_seed(seed)
     dense = {}
-    del X, out
-    torch.cuda.empty_cache()
     for name, (n_out, k_in) in {"q": (4096, 2048), "k": (512, 2048), "v": (512, 2048),
                                 "o": (2048, 4096)}.items():
         wq, wsc = quantize_rows((torch.randn((n_out, k_in), generator=g, device=dev) * 0.02).bfloat16())
         xq, xsc = quantize_rows(torch.randn((T, k_in), generator=g, device=dev).bfloat16())
         for _ in range(2):
             dec.lin_pq(xq, xsc, wq, wsc, T, n_out, k_in)
-        torch.cuda.synchronize(dev)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(5):
-            dec.lin_pq(xq, xsc, wq, wsc, T, n_out, k_in)
-        e1.record(stream)
-        torch.cuda.synchronize(dev)
-        us = e0.elapsed_time(e1) / 5 * 1e3
-        dense[name] = {"us": us, "tflops": 2.0 * T * n_out * k_in / us / 1e6}
+        ms = event_time(dev, stream, lambda: dec.lin_pq(xq, xsc, wq, wsc, T, n_out, k_in), 5)
+        us = ms / 5 * 1e3
+        tf = 2.0 * T * n_out * k_in / us / 1e6
+        dense[name] = {"us": us, "tflops": tf, "frac": tf / FP4_PEAK}
         del wq, wsc, xq, xsc
+    torch.cuda.empty_cache()
+    return dense
+
+
+def dropin_point(layers, T, dev, stream, steps, warmup, peak):
+    """The reference's decode MoE block through the drop-in operators, with
+    its host steps unchanged (runtime/model_runner_v2.py:185-207 for T = 1,
+    :266-290 for T = M): prequant, lin_pq router, softmax/top-k/renormalise in
+    torch, .tolist(), per-token pointer lists, moe_gateup, moe_down,
+    moe_combine.  Returns the whole chain's time and the gate/up + down
+    kernels' HBM roofline (CUDA events around them)."""
+    from moe_fused_inference_b200 import fp4_ext
+    import torch.nn.functional as F
+
+    dext = fp4_ext.get_decode_ext()
+    NL = len(layers)
+    # per-expert tensors, as the reference WeightStore hands them out
+    # (runtime/weight_store.py:283-285)
+    views = []
+    for L in layers:
+        w = L.w
+        views.append({e: {"gate": (w.gate_wp[e], w.gate_sc[e]), "up": (w.up_wp[e], w.up_sc[e]),
+                          "down": (w.down_wp[e], w.down_sc[e])} for e in range(E)})
+    g = torch.Generator(device=dev).manual_seed(17)
+    X = torch.randn((NL, T, H), generator=g, device=dev).bfloat16()
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(NL)]
+    uniq = [0] * NL
+    outs = [None] * NL
+
+    def step(with_events=False):
+        for l in range(NL):
+            w = layers[l].w
+            hq, hs = dext.prequant(X[l])
+            gate = dext.lin_pq(hq, hs, w.router_wp, w.router_sc, T, E, H)
+            rp = F.softmax(gate.float(), -1)
+            tv, ti = torch.topk(rp, TOPK, dim=-1)
+            tv = tv / tv.sum(-1, keepdim=True)
+            ids = ti.reshape(-1).tolist()
+            ex = views[l]
+            gu_tab, gsu_tab, dw_tab, ds_tab = [], [], [], []
+            for m in range(T):
+                sel = ids[m * TOPK:(m + 1) * TOPK]
+                gu_tab += [ex[e]["gate"][0] for e in sel] + [ex[e]["up"][0] for e in sel]
+                gsu_tab += [ex[e]["gate"][1] for e in sel] + [ex[e]["up"][1] for e in sel]
+                dw_tab += [ex[e]["down"][0] for e in sel]
+                ds_tab += [ex[e]["down"][1] for e in sel]
+            if with_events:
+                kev[l][0].record(stream)
+            guv = dext.moe_gateup(hq, hs, gu_tab, gsu_tab, TOPK, T, MI, H)
+            ydv = dext.moe_down(guv, dw_tab, ds_tab, TOPK, T, H, MI)
+            if with_events:
+                kev[l][1].record(stream)
+                uniq[l] = len(set(ids))
+            outs[l] = dext.moe_combine(ydv, tv.reshape(T, TOPK).float(), T)
+
+    for _ in range(warmup):
+        step()
+    ms = event_time(dev, stream, step, steps)
+    ms_per_layer = ms / steps / NL
+    step(True)
+    torch.cuda.synchronize(dev)
+    k_ms = sum(a.elapsed_time(b) for a, b in kev) / NL
+    u = sum(uniq) / NL
+    k_gbs = u * EXPERT_BYTES / (k_ms / 1e3) / 1e9
+    lay_gbs = decode_layer_bytes(u, T) / (ms_per_layer / 1e3) / 1e9
+    return {"tokens_per_s": T / (ms_per_layer / 1e3), "us_per_layer": ms_per_layer * 1e3,
+            "unique_experts_per_layer": u,
+            "gateup_down_kernels": {"us_per_layer": k_ms * 1e3, "GBps": k_gbs, "frac": k_gbs / peak},
+            "layer": {"GBps": lay_gbs, "frac": lay_gbs / peak},
+            "note": "host steps (.tolist(), pointer lists) inside the timed chain, as the "
+                    "reference runner runs them"}
+
+
+# ---------------------------------------------------------------------------
+def run_prefill(args, world, rank, local):
+    """--workload prefill: BASELINE config 3 alone (T tokens, default 16384,
+    Zipf(1.2)-skewed routing) with its own JSON line.  Under torchrun every
+    rank runs its own copy (weak scaling)."""
+    dev = torch.device("cuda", local if world > 1 else 0)
+    T = args.tokens if args.tokens != 64 else 16384
+    NL = args.layers if args.layers != N_LAYERS else 4
+    stream = torch.cuda.current_stream(dev)
+    sampler = ClockSampler(dev.index)
+    sampler.start()
+    barrier(world)
+    pf = prefill_point(T, NL, dev, stream, args.zipf_alpha, args.steps, args.warmup)
+    barrier(world)
+    clocks = sampler.stop()
+    ms_layer = max_over_ranks(pf["us_per_layer"] / 1e3, world)
+    dense = dense_projections(T, dev, stream)
     if rank != 0:
         return
     line = {
-        "metric": "MXFP4 MoE layer tokens/s (prefill)", "value": T * NL * args.steps * world / (ms / 1e3),
+        "metric": "MXFP4 MoE layer tokens/s (prefill)", "value": T * world / (ms_layer / 1e3),
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": ms_layer * NL, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "mxfp4 (e2m1 x e2m1, fp32 accumulate)",
         "data": "synthetic (random-init weights N(0,0.02), activations N(0,1), seeded)",
         "config": {"workload": f"prefill MoE layer, T={T} tokens, H=2048, E=128, top-8, Mi=768, "
                                f"Zipf(1.2) logit bias alpha={args.zipf_alpha}",
                    "step": f"{NL} MoE layers with distinct weights, plain launches",
-                   "expert_load_max_over_mean": float(counts.max() / counts.mean()),
-                   "experts_with_tokens": int((counts > 0).sum())},
+                   "expert_load_max_over_mean": pf["expert_load_max_over_mean"],
+                   "experts_with_tokens": pf["experts_with_tokens"]},
         "gpu_launches": 5 * NL * args.steps,  # quantise, route, scatter, experts, combine
-        "roofline": {"bound": "tensor", "achieved": tflops, "peak": fp4_peak, "unit": "TFLOP/s",
-                     "frac": tflops / fp4_peak, "peak_kind": "nominal dense FP4 (no measured FP4 peak)",
-                     "flops_per_layer": flop_tok * T,
-                     "dense_projections": {k: {"us": v["us"], "tflops": v["tflops"],
-                                               "frac": v["tflops"] / fp4_peak}
-                                           for k, v in dense.items()},
-                     # the other roof: at small T the weights, not the math, set the time
-                     "hbm": {"bytes_per_layer": hbm_bytes, "achieved": hbm_gbs, "peak": hbm_peak,
-                             "unit": "GB/s", "frac": hbm_gbs / hbm_peak, "peak_kind": hbm_kind}},
+        "roofline": {"bound": "tensor", "achieved": pf["tflops"], "peak": FP4_PEAK,
+                     "unit": "TFLOP/s", "frac": pf["frac"],
+                     "peak_kind": "nominal dense FP4 (no measured FP4 peak)",
+                     "flops_per_layer": pf["flops_per_layer"], "experts_kernel": pf["experts_kernel"],
+                     "stage_us_per_layer": pf["stage_us_per_layer"], "dense_projections": dense,
+                     "hbm": pf["hbm"]},
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
@@ -430,14 +667,8 @@ def run_linear(args, world, rank, local):
             graph = capture(dev, stream, calls, 1)
             for _ in range(max(args.warmup, 1)):
                 graph.replay()
-            torch.cuda.synchronize(dev)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            for _ in range(args.steps):
-                graph.replay()
-            e1.record(stream)
-            torch.cuda.synchronize(dev)
-            us = e0.elapsed_time(e1) / (args.steps * reps) * 1e3
+            ms = event_time(dev, stream, graph.replay, args.steps)
+            us = ms / (args.steps * reps) * 1e3
             res[f"{name}_T{T}"] = {"us": us, "GBps": w_bytes / us / 1e3,
                                    "frac": w_bytes / us / 1e3 / peak}
             del graph
@@ -475,75 +706,31 @@ def run_ours(args, world, rank, local):
     T, NL = args.tokens, args.layers
     layers = [MoELayer(random_layer_weights(E, H, MI, 0.02, seed=l, device=dev), TOPK)
               for l in range(NL)]
-    g = torch.Generator(device=dev).manual_seed(7)
-    X = torch.randn((NL, T, H), generator=g, device=dev).bfloat16()
-    out = torch.empty((NL, T, H), dtype=torch.float32, device=dev)
-    topi = torch.empty((NL, T, TOPK), dtype=torch.int32, device=dev)
-    topw = torch.empty((NL, T, TOPK), dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(NL)]
-    for row in evs:
-        for e in row:
-            e.record(stream)  # creates the event handles before the library records them
+    peak, peak_kind = measured_peaks()
 
-    def step(with_events=False):
-        for l in range(NL):
-            layers[l](X[l], out=out[l], topi=topi[l], topw=topw[l],
-                      events=evs[l] if with_events else None)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize(dev)
-
-    # One step (NL layer calls) is captured in a CUDA graph and replayed:
-    # decode serving runs graphs, and replay removes the host's per-launch cost
-    # from the device-side measurement.  The timed graph has no stage events
-    # (each event node costs the timeline ~2-3 us); a second graph with the
-    # stage events is replayed once afterwards for the per-kernel breakdown.
-    graph = graph_ev = None
-    if not args.no_graph:
-        graph = capture(dev, stream, step, 1)
-        graph_ev = capture(dev, stream, lambda: step(True), 0)
-        for _ in range(args.warmup):
-            graph.replay()
-        torch.cuda.synchronize(dev)
-
-    ms, clocks = timed_region(args, world, dev, stream, graph.replay if graph else step)
+    # ---- headline: decode at T, one CUDA graph per step (decode serving runs
+    # graphs; replay removes the host's per-launch cost from the measurement)
+    head = DecodePoint(layers, T, dev, stream, graph=not args.no_graph)
+    head.prepare(args.warmup)
+    ms, clocks = timed_region(args, world, dev, stream, head.run)
     ms_per_step = ms / args.steps
     tokens = T * NL * args.steps
     value = tokens / (ms / 1e3)
-
-    # ---- per-stage times (stage events, after the timed region) ----
-    if graph_ev is not None:
-        graph_ev.replay()
-    else:
-        step(True)
-    torch.cuda.synchronize(dev)
-    stage = [0.0] * 5
-    for l in range(NL):
-        for i in range(5):
-            stage[i] += evs[l][i].elapsed_time(evs[l][i + 1])
-    uniq = sum(int(torch.unique(topi[l]).numel()) for l in range(NL))
-
-    # ---- roofline of the dominant kernel (tensor-core expert GEMMs: gate/up + down) ----
-    peak, peak_kind = measured_peaks()
-    gemm_ms = stage[2] + stage[3]  # per step, summed over the NL layer calls
-    w_bytes = uniq * EXPERT_BYTES  # per step
-    achieved = w_bytes / (gemm_ms / 1e3) / 1e9
-    layer_bytes = (uniq * EXPERT_BYTES + NL * (ROUTER_BYTES + T * H * 2 + T * H * 4 + T * TOPK * 8))
+    hs = decode_summary(head, ms_per_step, peak)
+    head.release()
     traffic = committed_traffic()
 
-    del graph, graph_ev
     # ---- e2e through the public API with host buffers (plain per-call launches) ----
-    Xh = X.cpu().pin_memory()
+    Xh = head.X.cpu().pin_memory()
     Oh = torch.empty((NL, T, H), dtype=torch.float32).pin_memory()
-    Xd = torch.empty_like(X)
+    Xd = torch.empty_like(head.X)
 
     def e2e_step():
         Xd.copy_(Xh, non_blocking=True)
         for l in range(NL):
-            layers[l](Xd[l], out=out[l], topi=topi[l], topw=topw[l])
-        Oh.copy_(out, non_blocking=True)
+            layers[l](Xd[l], out=head.out[l], topi=head.topi[l], topw=head.topw[l])
+        Oh.copy_(head.out, non_blocking=True)
 
     e2e_ms, _ = timed_region(args, world, dev, stream, e2e_step)
     e2e_value = tokens / (e2e_ms / 1e3)
@@ -561,27 +748,57 @@ def run_ours(args, world, rank, local):
                    "global_batch": T, "parallelism": "single GPU",
                    "l2": f"inputs larger than L2: {NL} distinct layer weight sets "
                          f"({NL * E * EXPERT_BYTES / 1e9:.1f} GB) per step",
-                   "unique_experts_per_layer": uniq / NL},
+                   "unique_experts_per_layer": hs["unique_experts_per_layer"]},
         "gpu_launches": 3 * NL * args.steps,  # route (+quantise), experts (gate/up + down), combine
         "roofline": {"bound": "hbm", "kernel": "moe_experts_kernel (gate/up + down, one launch)",
-                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": peak_kind,
-                     "algorithmic_bytes_per_step": w_bytes,
-                     "algorithmic_bytes_per_layer_call": w_bytes / NL,
+                     "achieved": hs["experts_kernel"]["GBps"], "peak": peak, "unit": "GB/s",
+                     "frac": hs["experts_kernel"]["frac"], "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_layer_call": hs["experts_kernel"]["bytes"],
+                     "algorithmic_bytes_per_step": hs["experts_kernel"]["bytes"] * NL,
                      "traffic": (traffic or {}).get("bytes_per_layer_call"),
                      "traffic_source": (traffic or {}).get("source"),
-                     "layer": {"achieved": layer_bytes / (ms_per_step / 1e3) / 1e9,
-                               "frac": layer_bytes / (ms_per_step / 1e3) / 1e9 / peak,
-                               "stage_ms_per_step": {"route": stage[0],
-                                                     "experts": stage[2] + stage[3],
-                                                     "combine": stage[4]}}},
+                     "layer": {"achieved": hs["layer"]["GBps"], "frac": hs["layer"]["frac"],
+                               "stage_us_per_layer": hs["stage_us_per_layer"]}},
         "e2e": {"value": e2e_value, "unit": "tokens/s",
                 "h2d_bytes_per_step": int(Xh.numel() * Xh.element_size()),
                 "d2h_bytes_per_step": int(Oh.numel() * Oh.element_size())},
         "clocks": clocks,
     }
+    del Xh, Oh, Xd, head
+    torch.cuda.empty_cache()
+
+    if not args.headline_only:
+        # ---- decode sweep (config 2's other batch sizes) ----
+        sweep = {str(T): hs}
+        for t in (1, 8, 32):
+            if t == T:
+                continue
+            pt = DecodePoint(layers, t, dev, stream, seed=70 + t, graph=not args.no_graph)
+            pt.prepare(args.warmup)
+            pms = event_time(dev, stream, pt.run, args.steps) / args.steps
+            sweep[str(t)] = decode_summary(pt, pms, peak)
+            pt.release()
+            del pt
+        line["decode_sweep"] = {k: sweep[k] for k in sorted(sweep, key=int)}
+        # ---- the reference's drop-in call sequence (unchanged callers) ----
+        line["dropin"] = {f"T{t}": dropin_point(layers, t, dev, stream, max(args.steps // 4, 3),
+                                                 2, peak) for t in (1, 16)}
+        torch.cuda.empty_cache()
+        # ---- prefill (config 3) on 4 of the decode weight sets ----
+        pf = {}
+        for t in (2048, 16384):
+            pf[f"T{t}"] = prefill_point(t, 4, dev, stream, args.zipf_alpha,
+                                        steps=5 if t > 4096 else 10, warmup=2,
+                                        layer_weights=[L.w for L in layers[:4]])
+        pf["dense_projections_T16384"] = dense_projections(16384, dev, stream)
+        pf["peak_kind"] = "nominal dense FP4 9000 TFLOP/s (no measured FP4 peak)"
+        line["prefill"] = pf
+
     if not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args, T, layers[0].w)
+        cpu_layer = make_cpu_layer(layers[0].w)
+        line["cpu_baseline"] = cpu_baseline(args, T, cpu_layer)
+        if not args.headline_only:
+            line["cpu_baseline"]["config1_T4"] = cpu_baseline(args, 4, cpu_layer)
     print(json.dumps(line), flush=True)
 
 
@@ -594,8 +811,8 @@ def run_ep(args, world, rank, local):
     T, NL = args.tokens, args.layers
     bias = None
     if args.ep_zipf:
-        from oracle import mxfp4 as mx
-        bias = torch.from_numpy(mx.zipf_bias(E, args.zipf_alpha, seed=3)).to(dev)
+        from moe_fused_inference_b200.synthetic import zipf_bias
+        bias = torch.from_numpy(zipf_bias(E, args.zipf_alpha, seed=3)).to(dev)
     layers = [EPMoELayer(random_shard(E, world, rank, H, MI, 0.02, seed=l, device=dev), TOPK, T,
                          transport=args.ep_transport, logit_bias=bias)
               for l in range(NL)]
@@ -639,34 +856,45 @@ def run_ep(args, world, rank, local):
     tokens = T * NL * args.steps * world
     value = tokens / (ms / 1e3)
 
-    # ---- expert-compute time per step (events around the local expert part) ----
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(NL)]
+    # ---- per-stage device times of one step (events between the calls) ----
     import torch.distributed as dist
     from moe_fused_inference_b200.ep import ep_row_bytes
+    stage_names = (["route_dispatch", "experts_return", "unpack_wait"] if args.ep_transport == "p2p"
+                   else ["route_pack", "a2a_dispatch", "experts", "a2a_return", "unpack"])
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(stage_names) + 1)]
+           for _ in range(NL)]
     recvs = []
+    barrier(world)
     for l in range(NL):
         L = layers[l]
+        ev = evs[l]
+        ev[0].record(stream)
         if L.transport == "p2p":
             L.p2p_dispatch(X[l])
-            evs[l][0].record(stream)
+            ev[1].record(stream)
             L.p2p_experts()  # includes the wait for the peers' dispatch
-            evs[l][1].record(stream)
+            ev[2].record(stream)
             L.p2p_finish(T, out[l])
+            ev[3].record(stream)
             rv = torch.empty((world, T + 1, ep_row_bytes(H, TOPK)), dtype=torch.uint8, device=dev)
             L.xch.copy_recv_to(rv)
             recvs.append(rv)
         else:
             L.dispatch_prepare(X[l])
+            ev[1].record(stream)
             dist.all_to_all_single(L.recv.view(-1), L.send.view(-1))
-            evs[l][0].record(stream)
+            ev[2].record(stream)
             L.compute()
-            evs[l][1].record(stream)
+            ev[3].record(stream)
             dist.all_to_all_single(L.ret_back.view(-1), L.ret.view(-1))
+            ev[4].record(stream)
             L.finish(T, out[l])
+            ev[5].record(stream)
             recvs.append(L.recv)
     torch.cuda.synchronize(dev)
-    experts_ms = sum(a.elapsed_time(b) for a, b in evs)
+    stage_ms = [sum(evs[l][i].elapsed_time(evs[l][i + 1]) for l in range(NL))
+                for i in range(len(stage_names))]
+    experts_ms = stage_ms[1] if args.ep_transport == "p2p" else stage_ms[2]
     # unique local experts touched per layer on this rank
     uniq = 0
     rows_recv = 0
@@ -683,8 +911,8 @@ def run_ep(args, world, rank, local):
     w_bytes = uniq * EXPERT_BYTES
     peak, peak_kind = measured_peaks()
     achieved = w_bytes / (experts_ms / 1e3) / 1e9
-    stats = torch.tensor([achieved, experts_ms, rows_recv / NL, uniq / NL], dtype=torch.float64,
-                         device=dev)
+    stats = torch.tensor([achieved, experts_ms, rows_recv / NL, uniq / NL] + stage_ms,
+                         dtype=torch.float64, device=dev)
     allstats = [torch.zeros_like(stats) for _ in range(world)]
     dist.all_gather(allstats, stats)
     allstats = torch.stack(allstats).cpu()
@@ -717,6 +945,8 @@ def run_ep(args, world, rank, local):
     if rank != 0:
         return
     worst = int(torch.argmin(allstats[:, 0]))
+    per_rank_stages = {n: [float(v) / NL * 1e3 for v in allstats[:, 4 + i]]
+                       for i, n in enumerate(stage_names)}
     line = {
         "metric": "MXFP4 MoE layer tokens/s (decode)", "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
@@ -747,6 +977,9 @@ def run_ep(args, world, rank, local):
                      "frac": float(allstats[worst, 0]) / peak, "peak_kind": peak_kind,
                      "rank": worst, "experts_ms_per_step": float(allstats[worst, 1]),
                      "traffic": None},
+        # one eager step with events between the calls (plain launches; each
+        # call's time includes its waits on the other ranks)
+        "stage_us_per_layer": per_rank_stages,
         "e2e": {"value": e2e_value, "unit": "tokens/s",
                 "h2d_bytes_per_step": int(Xh.numel() * Xh.element_size()),
                 "d2h_bytes_per_step": int(Oh.numel() * Oh.element_size())},

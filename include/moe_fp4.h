@@ -46,10 +46,17 @@ const char* mfi_last_error(void);
 /* Library ABI version (bumped when a signature changes). */
 int mfi_version(void);
 
-/* Device error flag of the current device: 0 while healthy; non-zero after a
- * kernel's bounded wait (2 s) timed out and the kernel returned early (1 load
- * producer, 2 MMA issuer, 3 epilogue).  Synchronous; clear != 0 resets it.
- * Returns -1 if the flag cannot be read. */
+/* Device error flag of the current device: 0 while healthy, else the code of
+ * the first failure any kernel reported since it was last cleared — a bounded
+ * wait (2 s) that timed out, after which that kernel's CTA stopped early and
+ * its outputs are incomplete (1 load producer, 2 MMA issuer, 3 epilogue,
+ * 4 down item waiting for its h rows, 6 router rows, 7 missing dispatch from
+ * a peer, 8 missing return from a peer), or invalid data (4 expert id out of
+ * range, 5 expert region overflow: a repeated id or counters not zeroed,
+ * 9 a received exchange block whose row count lies outside [0, capacity],
+ * treated as empty).
+ * The flag only reports: a set flag does not stop later calls.  Synchronous;
+ * clear != 0 resets it.  Returns -1 if the flag cannot be read. */
 int mfi_device_error(int clear);
 
 /* ------------------------------------------------------------------------
@@ -107,7 +114,9 @@ int mfi_mxfp4_linear(const void* x, int dtype, int ld_x, const uint8_t* wp, cons
  * arguments and results as mfi_mxfp4_linear minus the workspace.  Shapes with
  * mfi_linear_workspace_bytes(M, N, Kp) > 4 MiB are rejected with
  * MFI_ERR_WORKSPACE.  The first call on each device looks up the array's
- * device address and should happen before any stream capture.  All calls on
+ * device address and should happen before any stream capture; the address is
+ * kept for the process, so after cudaDeviceReset() on a device this entry
+ * point must not be called there again.  All calls on
  * a device share the array (it keeps the last call's contents; nothing needs
  * to start at zero), so calls that overlap on the GPU race: serialise them.
  * Allocates nothing (no cudaMalloc, cudaFree or allocating library call). */
@@ -206,12 +215,13 @@ int mfi_moe_layer(const mfi_moe_weights* w, const void* x_bf16, int T, float* ou
 
 /* As mfi_moe_layer, recording six caller-created cudaEvent_t (passed as void*)
  * on the stream at the stage boundaries, for per-kernel timing:
- * tensor-core shapes: [0] start, [1] after quantise + route (which also
- * writes each token's row into its experts' regions), [2] = [1], [3] = [4]
- * after the expert GEMMs (gate/up, SwiGLU requant and down run as one
- * persistent launch), [5] after the combine; other
- * shapes: [2] after the gate/up GEMV, [3] after SwiGLU requantisation, [4]
- * after the down GEMV. */
+ * tensor-core decode shapes: [0] start, [1] after quantise + route (which
+ * also writes each token's row into its experts' regions), [2] = [1],
+ * [3] = [4] after the expert GEMMs (gate/up, SwiGLU requant and down run as
+ * one persistent launch), [5] after the combine; the prefill path: [0]
+ * start, [1] after quantise + route, [2] after the row scatter, [3] = [4]
+ * after the expert GEMMs, [5] after the combine; other shapes: [2] after the
+ * gate/up GEMV, [3] after SwiGLU requantisation, [4] after the down GEMV. */
 int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float* out,
                      int32_t* topi, float* topw, float* logits, void* workspace,
                      size_t workspace_bytes, void* const* events, int n_events, void* stream);

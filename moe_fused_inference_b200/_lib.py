@@ -89,6 +89,47 @@ class MfiError(RuntimeError):
     """A libmoe_fp4 call returned a non-zero status."""
 
 
+class MfiDeviceError(MfiError):
+    """A kernel of the library reported a failure through the device error flag."""
+
+
+# Codes of the device error flag (mfi_device_error): the first failure of any
+# kernel on the device since the flag was last cleared.
+DEVICE_ERRORS = {
+    1: "a load producer's bounded wait timed out",
+    2: "an MMA issuer's bounded wait timed out",
+    3: "an epilogue's bounded wait timed out",
+    4: "a down item's wait for its h rows timed out, or an expert id was out of range",
+    5: "an expert region overflowed: duplicate expert ids or a workspace whose counters "
+       "were not initialised",
+    6: "the router rows did not arrive in time",
+    7: "a peer rank's dispatch did not arrive in time",
+    8: "a peer rank's return did not arrive in time",
+    9: "a received exchange block's row count was outside [0, capacity] (treated as empty)",
+}
+
+# MFI_CHECK_DEVICE=1: every checked call synchronises the device and raises
+# MfiDeviceError if the flag is set (a debugging aid: it serialises the host
+# with the GPU after every operator).
+_CHECK_DEVICE = os.environ.get("MFI_CHECK_DEVICE", "0") == "1"
+
+
+def device_error(clear: bool = True) -> int:
+    """Read (and by default clear) the device error flag of the current
+    device; synchronous.  0 means no kernel has reported a failure."""
+    v = int(load().mfi_device_error(1 if clear else 0))
+    if v < 0:
+        raise MfiError("mfi_device_error: the flag could not be read")
+    return v
+
+
+def check_device(what: str) -> None:
+    """Raise MfiDeviceError (and clear the flag) if a kernel reported a failure."""
+    v = device_error(clear=True)
+    if v:
+        raise MfiDeviceError(f"{what}: device error {v}: {DEVICE_ERRORS.get(v, 'unknown code')}")
+
+
 def load():
     """Load (once) and return the ctypes handle; raise if the library is absent."""
     global _lib
@@ -114,3 +155,5 @@ def check(status: int, what: str) -> None:
     if status != 0:
         msg = load().mfi_last_error().decode(errors="replace")
         raise MfiError(f"{what}: {msg} (status {status})")
+    if _CHECK_DEVICE:
+        check_device(what)

@@ -419,18 +419,31 @@ bool use_prefill(int T, int H, int Mi, int k) {
   return layer_uses_tc(H, Mi) && (long long)T * k > kDecodeMaxPairs;
 }
 
+// events (optional, 6 cudaEvent_t): [0] start, [1] after quantise + route,
+// [2] after the scatter, [3] = [4] after the expert GEMMs, [5] after the combine.
 int run_prefill(const mfi_moe_weights* w, const void* x_bf16, int T, float* out, int32_t* topi,
                 float* topw, float* logits, void* workspace, size_t workspace_bytes,
-                cudaStream_t st) {
+                cudaStream_t st, void* const* events = nullptr) {
   const int E = w->n_experts, H = w->hidden, Mi = w->inter, k = w->top_k;
+  auto rec = [&](int i) -> int {
+    if (!events) return MFI_OK;
+    // while the stream is being captured an external record becomes an event node
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(st, &cs);
+    const unsigned flags = cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : 0u;
+    return cuda_status(cudaEventRecordWithFlags(reinterpret_cast<cudaEvent_t>(events[i]), st, flags),
+                       "moe_layer event record");
+  };
   if (!layer_uses_tc(H, Mi))
     return fail(MFI_ERR_ARG, "the prefill path needs hidden and inter to be multiples of 256");
   if ((long long)T * k > mfi::kPrefillMaxPairs) return fail(MFI_ERR_ARG, "T * top_k must be <= 262144");
   if (bad_ptr(w->prepared)) return fail(MFI_ERR_ARG, "weights.prepared is null (mfi_moe_prepare)");
   PrefillScratch s = carve_prefill(workspace, T, H, Mi, E, k);
   if (workspace_bytes < s.bytes) return fail(MFI_ERR_WORKSPACE, "workspace too small for the prefill layer");
-  int rc = cuda_status(cudaMemsetAsync(s.counts, 0, sizeof(int) * s.zero_words, st),
-                       "moe_layer prefill memset");
+  int rc = rec(0);
+  if (rc != MFI_OK) return rc;
+  rc = cuda_status(cudaMemsetAsync(s.counts, 0, sizeof(int) * s.zero_words, st),
+                   "moe_layer prefill memset");
   if (rc != MFI_OK) return rc;
   mfi::RouteArgs ra{};
   ra.x = x_bf16; ra.xq = s.xq; ra.xsc = s.xsc; ra.wr = w->router_wp; ra.sr = w->router_sc;
@@ -443,10 +456,12 @@ int run_prefill(const mfi_moe_weights* w, const void* x_bf16, int T, float* out,
   ra.logit_bias = w->logit_bias;
   ra.err = mfi::device_error_flag();
   rc = cuda_status(mfi::launch_route(ra, st), "moe_layer prefill route launch");
+  if (rc == MFI_OK) rc = rec(1);
   if (rc != MFI_OK) return rc;
   rc = cuda_status(mfi::launch_prefill_scatter(s.xq, s.xsc, topi, s.slot_pos, s.counts, T, E, k, H,
                                                s.perm, s.xp, s.xa, st),
                    "moe_layer prefill scatter launch");
+  if (rc == MFI_OK) rc = rec(2);
   if (rc != MFI_OK) return rc;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -458,12 +473,16 @@ int run_prefill(const mfi_moe_weights* w, const void* x_bf16, int T, float* out,
   L.xp = s.xp; L.xa = s.xa; L.hp = s.hp; L.ha = s.ha;
   L.yd = s.yd;
   L.err = mfi::device_error_flag(); L.queue = s.queue; L.gu_done = s.gu_done; L.ready = s.ready;
-  L.pdl = true;
+  L.pdl = events == nullptr;  // an event record between the kernels breaks the overlap anyway
   rc = cuda_status(mfi::launch_moe_prefill(L, st), "moe_layer prefill experts launch");
+  if (rc == MFI_OK) rc = rec(3);
+  if (rc == MFI_OK) rc = rec(4);
   if (rc != MFI_OK) return rc;
   // the decode combine's arithmetic on bf16 rows
-  return cuda_status(mfi::launch_combine_bf16(s.yd, topw, k, out, T, H, st, true),
-                     "moe_layer prefill combine launch");
+  rc = cuda_status(mfi::launch_combine_bf16(s.yd, topw, k, out, T, H, st, events == nullptr),
+                   "moe_layer prefill combine launch");
+  if (rc == MFI_OK) rc = rec(5);
+  return rc;
 }
 
 int layer_common_checks(const mfi_moe_weights* w, int T) {
@@ -569,20 +588,8 @@ int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float*
     if ((reinterpret_cast<uintptr_t>(x_bf16) & 15) != 0 ||
         (reinterpret_cast<uintptr_t>(w->router_wp) & 15) != 0)
       return fail(MFI_ERR_ARG, "x and router_wp must be 16-byte aligned");
-    cudaStream_t stp = as_stream(stream);
-    auto rec = [&](int i) -> int {
-      if (!events) return MFI_OK;
-      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-      cudaStreamIsCapturing(stp, &cs);
-      const unsigned flags = cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : 0u;
-      return cuda_status(cudaEventRecordWithFlags(reinterpret_cast<cudaEvent_t>(events[i]), stp, flags),
-                         "moe_layer event record");
-    };
-    int rc = rec(0);
-    if (rc != MFI_OK) return rc;
-    rc = run_prefill(w, x_bf16, T, out, topi, topw, logits, workspace, workspace_bytes, stp);
-    for (int i = 1; rc == MFI_OK && i < 6; ++i) rc = rec(i);
-    return rc;
+    return run_prefill(w, x_bf16, T, out, topi, topw, logits, workspace, workspace_bytes,
+                       as_stream(stream), events);
   }
   if (workspace_bytes < mfi_moe_layer_workspace_bytes(T, H, Mi, E, k))
     return fail(MFI_ERR_WORKSPACE, "workspace too small for moe_layer");
@@ -857,6 +864,7 @@ int mfi_ep_mask_recv(uint8_t* recv, int n_ranks, int capacity, int hidden, int t
   if ((reinterpret_cast<uintptr_t>(recv) & 15) != 0)
     return fail(MFI_ERR_ARG, "recv must be 16-byte aligned");
   return cuda_status(mfi::launch_ep_mask_recv(n_ranks, capacity, hidden, top_k, recv,
+                                              mfi::device_error_flag(),
                                               as_stream(stream)),
                      "ep_mask_recv launch");
 }

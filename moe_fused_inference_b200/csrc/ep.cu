@@ -121,12 +121,19 @@ __global__ void ep_write_headers_kernel(const int* __restrict__ counts, int n_ra
   if (d < n_ranks) reinterpret_cast<int*>(send + size_t(d) * (C + 1) * L.rb)[0] = counts[d];
 }
 
-__global__ void ep_mask_recv_kernel(int n_ranks, int C, RowLayout L, uint8_t* __restrict__ recv) {
+// A block whose count lies outside [0, C] (a corrupted header) is reported
+// (device error 9) and treated as empty.
+__global__ void ep_mask_recv_kernel(int n_ranks, int C, RowLayout L, uint8_t* __restrict__ recv,
+                                    int* __restrict__ err) {
   const long long rows = (long long)n_ranks * (C + 1);
   for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < rows;
        g += (long long)gridDim.x * blockDim.x) {
     const int s = int(g / (C + 1)), r = int(g % (C + 1));
-    const int count = reinterpret_cast<const int*>(recv + size_t(s) * (C + 1) * L.rb)[0];
+    int count = reinterpret_cast<const int*>(recv + size_t(s) * (C + 1) * L.rb)[0];
+    if (count < 0 || count > C) {
+      if (r == 0 && err) atomicCAS(err, 0, 9);
+      count = 0;
+    }
     if (r == 0 || r - 1 >= count) {
       int* sel = reinterpret_cast<int*>(recv + size_t(g) * L.rb + L.sel_off());
       for (int j = 0; j < L.k; ++j) sel[j] = -1;
@@ -280,8 +287,12 @@ __global__ void __launch_bounds__(128) ep_scatter_wait_kernel(
   const unsigned call = current_call(flags);
   if (threadIdx.x == 0) {
     const bool ok = wait_flags(flags + kFlagDispatch + src, 1, call, err, 7);
-    const int count =
+    int count =
         ok ? *reinterpret_cast<const volatile int*>(recv + size_t(src) * (C + 1) * L.rb) : 0;
+    if (count < 0 || count > C) {  // corrupted header: report, treat the block as empty
+      if (rr == 0) atomicCAS(err, 0, 9);
+      count = 0;
+    }
     s_valid = rr >= 1 && rr - 1 < count;
   }
   __syncthreads();
@@ -466,13 +477,13 @@ cudaError_t launch_ep_pack(const uint8_t* xq, const uint8_t* xsc, const int* top
   return cudaGetLastError();
 }
 
-cudaError_t launch_ep_mask_recv(int n_ranks, int C, int H, int k, uint8_t* recv,
+cudaError_t launch_ep_mask_recv(int n_ranks, int C, int H, int k, uint8_t* recv, int* err,
                                 cudaStream_t stream) {
   RowLayout L{H, k, ep_row_bytes(H, k)};
   const long long rows = (long long)n_ranks * (C + 1);
   int blocks = int((rows + 255) / 256);
   if (blocks < 1) blocks = 1;
-  ep_mask_recv_kernel<<<blocks, 256, 0, stream>>>(n_ranks, C, L, recv);
+  ep_mask_recv_kernel<<<blocks, 256, 0, stream>>>(n_ranks, C, L, recv, err);
   return cudaGetLastError();
 }
 

@@ -99,6 +99,7 @@ __global__ void __launch_bounds__(kLtThreads, 1)
   uint64_t* sfa_empty = sfa_full + 2;            // [2]
   uint64_t* b_bar = sfa_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(b_bar + 1);
+  __shared__ uint64_t drain[1];  // the MMA issuer's error-path drain
   const size_t raw_bytes = size_t(kLtRows) * nb;
   const size_t sfa_bytes = size_t(nks) * 2 * kLtAtom;
 
@@ -121,7 +122,9 @@ __global__ void __launch_bounds__(kLtThreads, 1)
       mbar_init(&sfa_empty[b], 1);
     }
     mbar_init(b_bar, 2);  // the activation TMA + the activation scale atoms
+    mbar_init(drain, 1);
     fence_mbar_init();
+    cta_abort_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kLtTmemCols);
   tc_fence_before();
@@ -138,6 +141,7 @@ __global__ void __launch_bounds__(kLtThreads, 1)
       for (int ks = 0; ks < nks; ++ks) tma_load_2d(s_b + ks * kLtB, &tma_x, ks * 128, 0, b_bar);
       // the raw codes of a tile go out one tile ahead of its weights, so the
       // scale atoms are ready when its first stage lands
+      uint32_t n_raw = 0;  // raw-code copies issued (copy j: buffer j & 1, phase j >> 1)
       auto issue_raw = [&](int t, uint32_t ti) {
         const int ib = int(ti & 1);
         if (!mbar_wait(&raw_empty[ib], ((ti >> 1) & 1) ^ 1, err, 1)) return false;
@@ -145,18 +149,26 @@ __global__ void __launch_bounds__(kLtThreads, 1)
         mbar_expect_tx(&raw_full[ib], uint32_t(rows * nb));
         bulk_load(s_raw + ib * raw_bytes, wsc + size_t(t) * kLtRows * nb, uint32_t(rows * nb),
                   &raw_full[ib]);
+        n_raw = ti + 1;
         return true;
       };
       uint32_t it = 0, ti = 0;
       bool ok = int(blockIdx.x) < n_tiles ? issue_raw(blockIdx.x, 0) : true;
       for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++ti) {
-        if (t + int(gridDim.x) < n_tiles && !issue_raw(t + gridDim.x, ti + 1)) break;
+        if (t + int(gridDim.x) < n_tiles && !issue_raw(t + gridDim.x, ti + 1)) { ok = false; break; }
         for (int ks = 0; ks < nks; ++ks, ++it) {
           const int s = int(it % uint32_t(stages));
           if (!mbar_wait(&empty[s], ((it / stages) & 1) ^ 1, err, 1)) { ok = false; break; }
           mbar_expect_tx(&full[s], kLtA);
           tma_load_2d(ring + s * kLtA, &tma_w, ks * 128, t * kLtRows, &full[s]);
         }
+      }
+      if (!ok) {
+        // drain our own copies before the CTA can exit: the activation rows,
+        // the last two raw-code copies and the ring stages
+        mbar_wait(b_bar, 0, nullptr, 0);
+        drain_ring(raw_full, 2, n_raw);
+        drain_ring(full, uint32_t(stages), it);
       }
     }
   } else if (warp == 6) {
@@ -208,8 +220,8 @@ __global__ void __launch_bounds__(kLtThreads, 1)
       for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++ti) {
         const uint32_t buf = ti % kLtAccBufs;
         const int ib = int(ti & 1);
-        if (!mbar_wait(&acc_empty[buf], ((ti / kLtAccBufs) & 1) ^ 1, err, 2)) break;
-        if (!mbar_wait(&sfa_full[ib], (ti >> 1) & 1, err, 2)) break;
+        if (!mbar_wait(&acc_empty[buf], ((ti / kLtAccBufs) & 1) ^ 1, err, 2)) { ok = false; break; }
+        if (!mbar_wait(&sfa_full[ib], (ti >> 1) & 1, err, 2)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d = tmem + buf * 32;
         const uint32_t atoms = smem_u32(s_sfa + ib * sfa_bytes);
@@ -243,6 +255,7 @@ __global__ void __launch_bounds__(kLtThreads, 1)
         tc_commit(&acc_full[buf]);
         tc_commit(&sfa_empty[ib]);
       }
+      if (!ok) drain_mma(drain);
     }
   } else {
     // ---- epilogue (warps 2-5, TMEM lane quadrant warp % 4) ----------------------

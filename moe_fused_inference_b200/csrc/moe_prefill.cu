@@ -179,6 +179,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
   uint64_t* item_empty = item_full + kPAccBufs;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_empty + kPAccBufs);
   __shared__ int s_item[kPAccBufs];
+  __shared__ uint64_t drain[1];  // the MMA issuer's error-path drain
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_gu = p.inter / 64, tiles_dn = p.hidden / 128;
@@ -196,7 +197,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
       mbar_init(&item_full[b], 1);
       mbar_init(&item_empty[b], 1 + kPGroupWarps);  // the MMA thread + one epilogue group
     }
+    mbar_init(drain, 1);
     fence_mbar_init();
+    cta_abort_init();
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tma_x);
@@ -265,7 +268,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
       int stops = 0;
       for (uint32_t qi = 0; ok; ++qi) {
         const uint32_t slot = qi % kPAccBufs;
-        if (!mbar_wait(&item_empty[slot], ((qi / kPAccBufs) & 1) ^ 1, p.err, 1)) break;
+        if (!mbar_wait(&item_empty[slot], ((qi / kPAccBufs) & 1) ^ 1, p.err, 1)) { ok = false; break; }
         if (item >= n_items) item = -1;
         s_item[slot] = item;
         mbar_arrive(&item_full[slot]);
@@ -292,11 +295,13 @@ __global__ void __launch_bounds__(kPThreads, 1)
             for (uint32_t i = 1;; ++i) {
               __nanosleep(64);
               if (ld_acquire_u32(p.ready + tl) >= tile_slices) break;
-              if ((i & 255u) == 0 && (*reinterpret_cast<volatile int*>(p.err) != 0 ||
-                                      globaltimer_ns() - t0 > kWaitLimitNs)) {
-                atomicCAS(p.err, 0, 4);
-                ok = false;
-                break;
+              if ((i & 255u) == 0) {
+                if (cta_aborted()) { ok = false; break; }
+                if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                  cta_fail(p.err, 4);
+                  ok = false;
+                  break;
+                }
               }
             }
             if (!ok) break;
@@ -319,6 +324,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         item = next;
         next = next2;
       }
+      if (!ok) drain_ring(full, kPStages, it);
     }
   } else if (warp == 1) {
     if (elect_one()) {
@@ -327,7 +333,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
       int stops = 0;
       for (uint32_t acc_it = 0; ok; ++acc_it) {
         const uint32_t buf = acc_it % kPAccBufs;
-        if (!mbar_wait(&item_full[buf], (acc_it / kPAccBufs) & 1, p.err, 2)) break;
+        if (!mbar_wait(&item_full[buf], (acc_it / kPAccBufs) & 1, p.err, 2)) { ok = false; break; }
         const int item = s_item[buf];
         mbar_arrive(&item_empty[buf]);
         if (!mbar_wait(&acc_empty[buf], ((acc_it / kPAccBufs) & 1) ^ 1, p.err, 2)) { ok = false; break; }
@@ -365,6 +371,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         }
         if (ok) tc_commit(&acc_full[buf]);
       }
+      if (!ok) drain_mma(drain);
     }
   } else {
     const int ew = warp - 2;             // 0..15
@@ -407,7 +414,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         bool nan = false;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float h = swiglu_fast(__uint_as_float(g[i]), __uint_as_float(u[i]));
+          const float h = swiglu(__uint_as_float(g[i]), __uint_as_float(u[i]));
           g[i] = __float_as_uint(h);
           am = fmaxf(am, fabsf(h));
           nan |= (h != h);

@@ -133,6 +133,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   uint64_t* item_empty = item_full + kAccBufs;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_empty + kAccBufs);
   __shared__ int s_item[kAccBufs];  // work item of each accumulator slot (-1: no more work)
+  __shared__ uint64_t drain[1];     // the MMA issuer's error-path drain
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_gu = p.inter / 64, tiles_dn = p.hidden / 128;
@@ -151,7 +152,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       mbar_init(&item_full[b], 1);
       mbar_init(&item_empty[b], 5);  // the MMA thread + the 4 epilogue warps
     }
+    mbar_init(drain, 1);
     fence_mbar_init();
+    cta_abort_init();
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tma_x);
@@ -234,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       int item = first_item;
       for (uint32_t qi = 0; ok; ++qi) {
         const uint32_t slot = qi % kAccBufs;
-        if (!mbar_wait(&item_empty[slot], ((qi / kAccBufs) & 1) ^ 1, p.err, 1)) break;
+        if (!mbar_wait(&item_empty[slot], ((qi / kAccBufs) & 1) ^ 1, p.err, 1)) { ok = false; break; }
         if (item >= n_items) item = -1;
         s_item[slot] = item;
         mbar_arrive(&item_full[slot]);
@@ -258,9 +261,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
               __nanosleep(64);
               if (ld_acquire_u32(p.ready + chunk) >= unsigned(tiles_gu)) break;
               if ((i & 255u) == 0) {
-                if (*reinterpret_cast<volatile int*>(p.err) != 0 ||
-                    globaltimer_ns() - t0 > kWaitLimitNs) {
-                  atomicCAS(p.err, 0, 4);
+                if (cta_aborted()) { ok = false; break; }
+                if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                  cta_fail(p.err, 4);
                   ok = false;
                   break;
                 }
@@ -286,6 +289,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         }
         item = next;
       }
+      if (!ok) drain_ring(full, kStages, it);
     }
   } else if (warp == 1) {
     if (elect_one()) {
@@ -293,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       bool ok = true;
       for (uint32_t acc_it = 0; ok; ++acc_it) {
         const uint32_t buf = acc_it % kAccBufs;
-        if (!mbar_wait(&item_full[buf], (acc_it / kAccBufs) & 1, p.err, 2)) break;
+        if (!mbar_wait(&item_full[buf], (acc_it / kAccBufs) & 1, p.err, 2)) { ok = false; break; }
         const int item = s_item[buf];
         mbar_arrive(&item_empty[buf]);
         if (!mbar_wait(&acc_empty[buf], ((acc_it / kAccBufs) & 1) ^ 1, p.err, 2)) { ok = false; break; }
@@ -330,6 +334,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         }
         if (ok) tc_commit(&acc_full[buf]);
       }
+      if (!ok) drain_mma(drain);
     }
   } else {
     const int lane_base = (warp & 3) * 32;
@@ -389,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           if (active && i < q) {
             const float g = sg[(j0 + i) * 33 + n];
             const float u = sg[(64 + j0 + i) * 33 + n];
-            h[i] = swiglu_fast(g, u);
+            h[i] = swiglu(g, u);
             am = fmaxf(am, fabsf(h[i]));
             nan |= (h[i] != h[i]);
           }

@@ -105,13 +105,15 @@ __device__ __forceinline__ void nib8_to_i8(uint32_t w, uint32_t& lo, uint32_t& h
   hi = __byte_perm(ph, nh, 0x3210u | (s >> 16));
 }
 
-// SwiGLU of the fused expert kernels, h = g / (1 + e^-g) * u, evaluated the
-// way the reference's CUDA build evaluates it: src/ext/mxfp4_decode.cu:258
-// is compiled with --use_fast_math (CMakeLists.txt:22), which turns expf into
-// __expf and '/' into __fdividef.  (The standalone moe_down operator keeps
-// IEEE expf and division, like the reference's Python restatement.)
-__device__ __forceinline__ float swiglu_fast(float g, float u) {
-  return __fmul_rn(__fdividef(g, __fadd_rn(1.0f, __expf(-g))), u);
+// SwiGLU, h = (g / (1 + e^-g)) * u in fp32, the one form every kernel of the
+// library uses (the moe_down operator and the fused decode / prefill
+// epilogues).  It is the reference kernel's expression
+// (src/ext/mxfp4_decode.cu:258) as its build compiles it: runtime/fp4_ext.py
+// builds the extension with -O3 and no fast-math flag, so expf is CUDA's
+// expf and '/' a correctly rounded division; nothing in it can be contracted
+// into an FMA.
+__device__ __forceinline__ float swiglu(float g, float u) {
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
 }
 
 // 2^e as float for e in the normal range; ldexpf outside it.

@@ -20,8 +20,15 @@
 //    behind; nothing in it has to start at zero because each call writes
 //    every byte it later reads;
 //  * calls that overlap on the GPU (different streams, or host threads
-//    launching concurrently on one device) race on the array — serialise them.
+//    launching concurrently on one device) race on the array — serialise them;
+//  * the looked-up address is kept for the life of the process: after
+//    cudaDeviceReset() on a device the array lives at a new address, so the
+//    entry point must not be called on that device again.  (Host threads may
+//    make first calls concurrently: the cache is atomic, and two threads that
+//    both look the address up store the same value.)
 #include <cuda_runtime.h>
+
+#include <atomic>
 
 #include "../../include/moe_fp4.h"
 #include "work.cuh"
@@ -36,23 +43,23 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 // the symbol names a host-side stand-in, never a device address, so kernels
 // must be given this address, not the symbol.
 void* scratch_address(int* status) {
-  static void* addr[64] = {nullptr};
+  static std::atomic<void*> addr[64];  // zero-initialised (static storage)
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     *status = MFI_ERR_CUDA;
     return nullptr;
   }
-  if (!addr[dev]) {
-    void* p = nullptr;
+  void* p = addr[dev].load(std::memory_order_acquire);
+  if (!p) {
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) {
       *status = MFI_ERR_CUDA;
       return nullptr;
     }
-    addr[dev] = p;
+    addr[dev].store(p, std::memory_order_release);
   }
   *status = MFI_OK;
-  return addr[dev];
+  return p;
 }
 
 }  // namespace

@@ -110,7 +110,7 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const float* __restri
       if (live && k < K) {
         const float g = gu[row * ld_gu + k];
         const float u = gu[row * ld_gu + K + k];
-        h = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+        h = swiglu(g, u);
       }
       v[i] = h;
     }

@@ -429,6 +429,7 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
   if (threadIdx.x == 0) {
     tc::mbar_init(&s_bar, 1);
     tc::fence_mbar_init();
+    tc::cta_abort_init();
     if (n_e > 0) {
       tc::mbar_expect_tx(&s_bar, w_bytes + (sc_bulk ? sc_bytes : 0u));
       tc::bulk_load(s_w, a.wr + size_t(e_begin) * (a.H >> 1), w_bytes, &s_bar);
@@ -477,6 +478,8 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
 
   // ---- 32 logits: warp w owns local experts w, w+8, w+16, w+24 --------------
   const bool have_w = n_e > 0 && tc::mbar_wait(&s_bar, 0, a.err, 6);
+  // failed: the router rows may still be landing; wait for them before exit
+  if (n_e > 0 && !have_w && threadIdx.x == 0) tc::mbar_wait(&s_bar, 0, nullptr, 0);
   if (warp == 0 && a.pf_bytes) {
     // this token's inputs are in: start streaming the expert weights that the
     // next kernel reads first into L2 (speculative: the routing is not known)
@@ -705,6 +708,7 @@ __global__ void __launch_bounds__(kBatchThreads) route_batch_kernel(RouteArgs a)
   if (threadIdx.x == 0) {
     tc::mbar_init(&s_bar, 1);
     tc::fence_mbar_init();
+    tc::cta_abort_init();
     tc::mbar_expect_tx(&s_bar, w_bytes + (sc_bulk ? sc_bytes : 0u));
     tc::bulk_load(s_w, a.wr, w_bytes, &s_bar);
     if (sc_bulk) tc::bulk_load(s_ws, a.sr, sc_bytes, &s_bar);
@@ -713,6 +717,8 @@ __global__ void __launch_bounds__(kBatchThreads) route_batch_kernel(RouteArgs a)
     for (uint32_t i = threadIdx.x; i < sc_bytes; i += kBatchThreads) s_ws[i] = a.sr[i];
   __syncthreads();
   const bool have_w = tc::mbar_wait(&s_bar, 0, a.err, 6);
+  // failed: the router rows may still be landing; wait for them before exit
+  if (!have_w && threadIdx.x == 0) tc::mbar_wait(&s_bar, 0, nullptr, 0);
   __syncthreads();
 
   const int groups = (a.T + kBatchTok - 1) / kBatchTok;

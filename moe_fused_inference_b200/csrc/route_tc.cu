@@ -315,6 +315,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) route_tc_kernel(RouteArgs a) {
   __shared__ int s_xminc[kRtTile], s_wminc[kRtE];
   __shared__ int s_wspread, s_unscaled, s_xlo, s_xhi, s_wlo, s_whi, s_failed;
   __shared__ int s_cnt[kRtE], s_base[kRtE];
+  __shared__ uint64_t drain[1];  // the MMA issuer's error-path drain
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, t0 = tile * kRtTile;
@@ -330,7 +331,9 @@ __global__ void __launch_bounds__(kRtThreads, 1) route_tc_kernel(RouteArgs a) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], kRtEpiWarps);
     }
+    mbar_init(drain, 1);
     fence_mbar_init();
+    cta_abort_init();
     s_wspread = 0;
     s_unscaled = 0;
     s_xlo = 255;
@@ -407,7 +410,8 @@ __global__ void __launch_bounds__(kRtThreads, 1) route_tc_kernel(RouteArgs a) {
     // ---- producer -------------------------------------------------------------
     if (elect_one()) {
       const uint8_t* x8t = a.x8 + size_t(tile) * nchunk * kRtBlock;
-      for (int c = 0; c < nchunk; ++c) {
+      int c = 0;
+      for (; c < nchunk; ++c) {
         const int s = c % kRtStages;
         if (!mbar_wait(&empty[s], ((c / kRtStages) & 1) ^ 1, a.err, 6)) break;
         uint8_t* st = ring + s * kRtStageBytes;
@@ -415,6 +419,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) route_tc_kernel(RouteArgs a) {
         bulk_load(st, x8t + size_t(c) * kRtBlock, kRtBlock, &full[s]);
         bulk_load(st + kRtBlock, a.r8 + size_t(c) * kRtBlock, kRtBlock, &full[s]);
       }
+      if (c < nchunk) drain_ring(full, kRtStages, uint32_t(c));  // failed: drain our copies
     }
   } else if (warp == 1) {
     // ---- MMA issue --------------------------------------------------------------
@@ -423,7 +428,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) route_tc_kernel(RouteArgs a) {
       bool ok = true;
       for (int c = 0; c < nchunk && ok; ++c) {
         const int s = c % kRtStages;
-        if (!mbar_wait(&full[s], (c / kRtStages) & 1, a.err, 6)) break;
+        if (!mbar_wait(&full[s], (c / kRtStages) & 1, a.err, 6)) { ok = false; break; }
         tc_fence_after();
         const uint32_t base = smem_u32(ring + s * kRtStageBytes);
 #pragma unroll
@@ -446,6 +451,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) route_tc_kernel(RouteArgs a) {
         if (ok) tc_commit(&empty[s]);
       }
       if (ok && fast) tc_commit(&acc_full[0]);
+      if (!ok) drain_mma(drain);
     }
   }
 
@@ -505,7 +511,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) route_tc_kernel(RouteArgs a) {
     for (int j = 0; j < 32; ++j) lg[j] = float(acc[j]);
   }
   tc_fence_before();
-  if (threadIdx.x == 0) s_failed = *reinterpret_cast<volatile int*>(a.err);
+  if (threadIdx.x == 0) s_failed = cta_aborted() ? 1 : 0;
   __syncthreads();  // every MMA has been consumed: the ring is free
   float* s_cv = reinterpret_cast<float*>(ring + kRtOffCv);
   uint8_t* s_ci = ring + kRtOffCi;

@@ -24,6 +24,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
+
 #include "tc_ptx.cuh"
 #include "tmap.cuh"
 #include "work.cuh"
@@ -72,6 +74,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* empty = full + kStages;
   uint64_t* accb = empty + kStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
+  __shared__ uint64_t drain[1];  // the MMA issuer's error-path drain
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tile = blockIdx.x, m_tile = blockIdx.y;
@@ -83,7 +86,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(accb, 1);
+    mbar_init(drain, 1);
     fence_mbar_init();
+    cta_abort_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
   tc_fence_before();
@@ -152,6 +157,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_commit(&empty[s]);
       }
       if (ok) tc_commit(accb);
+      else drain_mma(drain);
     }
   } else {
     const bool ok = mbar_wait(accb, 0, p.err, 3);
@@ -212,10 +218,12 @@ constexpr uint32_t kPTmemSFG = kPAccG * 128;                  // + 16 per ring s
 static_assert(kPTmemSFG + 16 * kPStagesG <= 512, "scale columns exceed the allocation");
 constexpr int kPOutStageG = 32 * 32 * 4;                       // per epilogue warp
 
-size_t tc_gemm_p_smem_bytes() {
+constexpr size_t tc_gemm_p_smem_bytes() {
   return 1024 + size_t(kPStagesG) * kPStageG + 4 * size_t(kPOutStageG) +
          8 * (2 * kPStagesG + 2 * kPAccG) + 16;
 }
+// dynamic shared memory per CTA on sm_100 is at most 227 KB (232,448 B)
+static_assert(tc_gemm_p_smem_bytes() + 64 <= 232448, "ring stages exceed the shared memory of a CTA");
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_gemm_p_kernel(const __grid_constant__ CUtensorMap tma_a,
@@ -229,6 +237,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* acc_full = empty + kPStagesG;
   uint64_t* acc_empty = acc_full + kPAccG;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + kPAccG);
+  __shared__ uint64_t drain[1];  // the MMA issuer's error-path drain
   constexpr int kOffB = kABytes, kOffSFA = kABytes + kBM * kBK / 2, kOffSFB = kOffSFA + 1024;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -245,7 +254,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 4);
     }
+    mbar_init(drain, 1);
     fence_mbar_init();
+    cta_abort_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
   tc_fence_before();
@@ -286,7 +297,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t idesc2 = make_idesc_mxf4(kBM, kPBN, 2, 2);
       for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++ti) {
         const uint32_t buf = ti % kPAccG;
-        if (!mbar_wait(&acc_empty[buf], ((ti / kPAccG) & 1) ^ 1, p.err, 2)) break;
+        if (!mbar_wait(&acc_empty[buf], ((ti / kPAccG) & 1) ^ 1, p.err, 2)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d = tmem + buf * 128;
         for (int kt = 0; kt < k_tiles; ++kt, ++it) {
@@ -313,6 +324,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         if (ok) tc_commit(&acc_full[buf]);
       }
+      if (!ok) drain_mma(drain);
     }
   } else {
     const int quad = warp & 3;
@@ -403,21 +415,25 @@ cudaError_t launch_sf_atoms(const uint8_t* src, long long src_ld, int R, int Kp,
 }
 
 // ---------------------------------------------------------------------------
-// Device-wide error flag: 0 while healthy; a kernel whose bounded wait timed
-// out stores a non-zero code (1 producer, 2 MMA issuer, 3 epilogue).
+// Device-wide error flag: 0 while healthy; the first failure of any kernel
+// stores its code (a bounded wait that timed out, or invalid data).  It only
+// reports to the host (mfi_device_error); a set flag does not stop later
+// kernels (their waits stop on their own CTA's abort word, tc_ptx.cuh).
 __device__ int g_device_error;
 
 int* device_error_flag() {
-  static int* addr[64] = {nullptr};
+  static std::atomic<int*> addr[64];  // zero-initialised; racing first lookups store one value
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return nullptr;
-  if (!addr[dev]) {
+  int* a = addr[dev].load(std::memory_order_acquire);
+  if (!a) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
-    addr[dev] = static_cast<int*>(p);
+    a = static_cast<int*>(p);
+    addr[dev].store(a, std::memory_order_release);
   }
-  return addr[dev];
+  return a;
 }
 
 bool tc_gemm_supported(const void* a, const void* b, int Kp) {

@@ -50,11 +50,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: gives up after kWaitLimitNs, records `code` in *err (first
-// error wins) and returns false.  The caller then skips its remaining work.
-// try_wait suspends in hardware between polls; the clock and the shared error
-// flag (a global load) are only consulted every 1024 polls, so a wait that is
-// satisfied within a few microseconds costs no extra memory traffic.
+// Abort word of the calling CTA (shared memory, one per CTA of every kernel
+// that uses it).  A role of the CTA that gives up a wait raises it, and the
+// CTA's other roles stop at their next wait instead of waiting out the limit
+// as well.  It belongs to this launch only: the device-wide error flag (`err`
+// below) reports to the host and never stops a later call.  Every kernel that
+// waits with mbar_wait clears the word from thread 0 (cta_abort_init) before
+// its first __syncthreads.
+__device__ __forceinline__ volatile int* cta_abort_word() {
+  __shared__ int word;
+  return &word;
+}
+__device__ __forceinline__ void cta_abort_init() { *cta_abort_word() = 0; }
+__device__ __forceinline__ bool cta_aborted() { return *cta_abort_word() != 0; }
+// Record `code` in the device error flag (first error wins) and stop this CTA.
+__device__ __forceinline__ void cta_fail(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+  *cta_abort_word() = 1;
+}
+
+// Bounded wait: gives up after kWaitLimitNs, records `code` (cta_fail) and
+// returns false; it also returns false once another role of the CTA has
+// failed.  The caller then skips its remaining work.  With err == nullptr it
+// is a drain wait (for the CTA's own copies or MMAs still in flight after a
+// failure): it ignores the abort word and only gives up at the limit.
+// try_wait suspends in hardware between polls; the clock and the abort word
+// are only consulted every 1024 polls, so a wait that is satisfied within a
+// few microseconds costs nothing extra.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -62,9 +84,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 1023u) == 0) {
-      if (err && *reinterpret_cast<volatile int*>(err) != 0) return false;  // another role failed
+      if (err && cta_aborted()) return false;  // another role of this CTA failed
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        if (err) atomicCAS(err, 0, code);
+        if (err) cta_fail(err, code);
         return false;
       }
     }
@@ -202,6 +224,22 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
           smem_u32(bar))
       : "memory");
+}
+
+// Error-path drains, so that no copy or MMA of a CTA is still landing in its
+// shared memory or TMEM when the CTA frees them and exits.
+// Producer: the ring stages it filled, [issued - stages, issued), each
+// complete on full[j % stages] in phase j / stages (later stages were never
+// issued, earlier ones completed before their slots were refilled).
+__device__ __forceinline__ void drain_ring(uint64_t* full, uint32_t stages, uint32_t issued) {
+  for (uint32_t j = issued > stages ? issued - stages : 0u; j < issued; ++j)
+    mbar_wait(&full[j % stages], (j / stages) & 1u, nullptr, 0);
+}
+// MMA issuer: commit whatever tcgen05 work it has issued to `bar` (an
+// mbarrier of count 1 used for nothing else) and wait for it.
+__device__ __forceinline__ void drain_mma(uint64_t* bar) {
+  tc_commit(bar);
+  mbar_wait(bar, 0, nullptr, 0);
 }
 
 // 32 lanes x 32 consecutive fp32 columns: thread i of the warp gets row

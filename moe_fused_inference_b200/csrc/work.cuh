@@ -194,7 +194,7 @@ int ep_row_bytes(int H, int k);
 cudaError_t launch_ep_pack(const uint8_t* xq, const uint8_t* xsc, const int* topi,
                            const float* topw, int T, int H, int k, int n_ranks, int e_local, int C,
                            int* counts, uint8_t* send, int* pack_pos, cudaStream_t stream);
-cudaError_t launch_ep_mask_recv(int n_ranks, int C, int H, int k, uint8_t* recv,
+cudaError_t launch_ep_mask_recv(int n_ranks, int C, int H, int k, uint8_t* recv, int* err,
                                 cudaStream_t stream);
 cudaError_t launch_ep_unpack(const float* ret, const int* pack_pos, int T, int n_ranks, int C,
                              int H, float* out, cudaStream_t stream);

@@ -137,6 +137,11 @@ class CpuEPOps:
         out[:] = 0
         for s in range(self.world):
             count = int(np.frombuffer(r[s, 0, :4].tobytes(), np.int32)[0])
+            if not 0 <= count <= self.C:
+                # the library treats such a block as empty and reports device
+                # error 9; on the host the step raises
+                raise RuntimeError(f"received block from rank {s} has row count {count}, "
+                                   f"outside [0, {self.C}]")
             for i in range(count):
                 row = r[s, 1 + i]
                 ids = np.frombuffer(row[sel : sel + 4 * k].tobytes(), np.int32)

@@ -16,6 +16,7 @@ import numpy as np
 import pytest
 import torch
 
+from moe_fused_inference_b200.synthetic import zipf_bias
 from oracle import ep as oep
 from oracle import mxfp4 as mx
 from tests.conftest import cosine, max_rel_err
@@ -338,7 +339,7 @@ def test_ep_p2p_zipf_bias_routes_like_single_gpu():
     from moe_fused_inference_b200.layer import MoELayer
     E, H, Mi, k, world = 128, 2048, 768, 8, 4
     w = _layer_w(E, H, Mi, seed=23)
-    bias = torch.from_numpy(mx.zipf_bias(E, alpha=0.5, seed=3))
+    bias = torch.from_numpy(zipf_bias(E, alpha=0.5, seed=3))
     counts = [64, 40, 64, 9]
     xs = [_x(t, H, 130 + r) for r, t in enumerate(counts)]
     layers, outs = _emulate_p2p(w, xs, world, k, max(counts), logit_bias=bias.cuda())
@@ -355,3 +356,49 @@ def test_ep_p2p_zipf_bias_routes_like_single_gpu():
     finally:
         for L in layers:
             L.close()
+
+
+def test_ep_p2p_missing_peer_times_out():
+    """A virtual rank that never dispatches (two ranks emulated on one GPU,
+    rank 1 launches nothing): rank 0's expert step waits for rank 1's
+    dispatch flag, a flag nothing sets, gives up after its bounded wait (2 s)
+    and treats the block as empty; its unpack likewise gives up on rank 1's
+    return.  Both calls return, the device error flag reads 7 (missing
+    dispatch: the first failure wins over the later 8), and the GPU stays
+    usable: a fresh single-GPU layer afterwards runs clean."""
+    import time
+
+    from moe_fused_inference_b200.ep import EPMoELayer, EPShard
+    from moe_fused_inference_b200.layer import MoELayer
+    E, H, Mi, k, world, C = 128, 2048, 768, 8, 2, 8
+    w = _layer_w(E, H, Mi, seed=31)
+    L = _lib().load()
+    assert L.mfi_device_error(1) == 0
+    layers = [EPMoELayer(EPShard.from_layer(w, r, world), k, C, world=world, rank=r,
+                         transport="p2p", connect=False) for r in range(world)]
+    try:
+        bases = [x.xch.base for x in layers]
+        for x in layers:
+            x.xch.connect(bases)
+        xin = _x(C, H, 150)
+        out = torch.full((C, H), float("nan"), dtype=torch.float32, device="cuda")
+        t0 = time.time()
+        layers[0].p2p_dispatch(xin)
+        layers[0].p2p_experts()
+        layers[0].p2p_finish(C, out)
+        torch.cuda.synchronize()
+        elapsed = time.time() - t0
+        assert L.mfi_device_error(1) == 7
+        assert elapsed < 30.0
+        # rank 0's own experts answered; rank 1's share of each token is missing
+        assert bool(torch.isfinite(out).all())
+    finally:
+        for x in layers:
+            x.close()
+    # the context is still good and the flag was cleared: later calls are not
+    # affected by the failure
+    single = MoELayer(w, top_k=k)
+    o, _, _ = single(xin)
+    torch.cuda.synchronize()
+    assert L.mfi_device_error(1) == 0
+    assert bool(torch.isfinite(o).all())

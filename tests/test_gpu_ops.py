@@ -60,7 +60,10 @@ def test_forward_mxfp4_linear(M, N, K):
                                    # the persistent prefill GEMM (N % 4 == 0): one partial
                                    # K tile; several tiles per CTA with every accumulator
                                    # reused; a partial last weight tile
-                                   (300, 384, 100), (4700, 2048, 256), (200, 1000, 512)])
+                                   (300, 384, 100), (4700, 2048, 256), (200, 1000, 512),
+                                   # the one-tile-per-CTA tensor-core GEMM (M >= 64 and
+                                   # N % 4 != 0): partial weight tiles, rows not a multiple of 4
+                                   (200, 301, 256), (64, 150, 2048)])
 def test_lin_pq(M, N, K):
     rng = np.random.default_rng(1 + M + N + K)
     wp, wc, twp, twc = make_w(rng, N, K)

@@ -17,6 +17,7 @@ import pytest
 import torch
 
 from moe_fused_inference_b200.layer import MoELayer, MoELayerWeights, random_layer_weights
+from moe_fused_inference_b200.synthetic import zipf_bias
 from oracle import mxfp4 as mx
 from tests.conftest import cosine, max_rel_err
 
@@ -68,7 +69,7 @@ def test_prefill_auto_zipf_T2048(qwen_layer):
     """T = 2048 with the Zipf(1.2) logit skew: mfi_moe_layer
     takes the prefill path on its own; some experts get many 128-token tiles,
     some none."""
-    bias = mx.zipf_bias(128, alpha=0.5, seed=3)
+    bias = zipf_bias(128, alpha=0.5, seed=3)
     layer = MoELayer(qwen_layer, top_k=8, logit_bias=torch.from_numpy(bias))
     T = 2048
     x = _x(T, 77)
@@ -137,3 +138,37 @@ def test_prefill_router_ragged_tile_and_wide_scales(qwen_layer, span):
     assert np.array_equal(topi.cpu().numpy(), ref["idx"])
     np.testing.assert_allclose(topw.cpu().numpy(), ref["w"], rtol=2e-6, atol=1e-7)
     assert torch.isfinite(out).all()
+
+
+def test_prefill_zipf_T16384(qwen_layer):
+    """BASELINE config 3's headline prefill shape: T = 16384 tokens with the
+    Zipf(1.2) logit skew through mfi_moe_layer.  A token's routing and output
+    depend only on its own row, so the oracle runs on 2048 of the tokens (every
+    8th, spread over every 128-token tile and every expert's tiles): logits
+    and top-k bit-exact, weights to rounding, output cosine >= 0.999 and max
+    relative error <= 1e-2.  Over all 16384 tokens: no device error, finite
+    output, distinct ids per token, weights summing to 1."""
+    bias = zipf_bias(128, alpha=0.5, seed=3)
+    layer = MoELayer(qwen_layer, top_k=8, logit_bias=torch.from_numpy(bias))
+    T = 16384
+    x = _x(T, 16384)
+    logits = torch.empty((T, 128), dtype=torch.float32, device="cuda")
+    out, topi, topw = layer(x, logits=logits)
+    torch.cuda.synchronize()
+    from moe_fused_inference_b200 import _lib
+    assert _lib.load().mfi_device_error(1) == 0
+    assert bool(torch.isfinite(out).all())
+    ti = topi.cpu().numpy()
+    assert (np.sort(ti, axis=1)[:, 1:] != np.sort(ti, axis=1)[:, :-1]).all()
+    np.testing.assert_allclose(topw.sum(1).cpu().numpy(), 1.0, rtol=0, atol=1e-5)
+    counts = np.bincount(ti.ravel(), minlength=128)
+    assert counts.max() > 4 * counts.mean()  # the skew is real: the hottest expert has many tiles
+    s = slice(0, T, 8)
+    ref = mx.moe_layer(x[s].float().cpu().numpy(), oracle_weights(qwen_layer), topk=8, fast=True,
+                       logit_bias=bias)
+    assert np.array_equal(logits[s].cpu().numpy(), ref["logits"])
+    assert np.array_equal(ti[s], ref["idx"])
+    np.testing.assert_allclose(topw[s].cpu().numpy(), ref["w"], rtol=2e-6, atol=1e-7)
+    o = out[s].cpu().numpy()
+    assert cosine(o, ref["out"]) >= 0.999
+    assert max_rel_err(o, ref["out"]) <= 1e-2

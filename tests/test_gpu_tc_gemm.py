@@ -31,7 +31,9 @@ def make_operands(M, N, K, seed):
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 256), (64, 8, 64), (200, 300, 100), (256, 512, 2048),
                                    (384, 2048, 768), (130, 96, 256), (1024, 4096, 2048),
-                                   (512, 512, 4096)])
+                                   (512, 512, 4096),
+                                   # N % 4 != 0: the one-tile-per-CTA kernel (tc_gemm_mxf4_kernel)
+                                   (200, 301, 256), (64, 150, 2048), (300, 1001, 512)])
 def test_tc_forward(M, N, K):
     x, wp, wc = make_operands(M, N, K, seed=M + N + K)
     xh = torch.from_numpy(x).half().cuda()
@@ -57,3 +59,27 @@ def test_tc_lin_pq_matches_gemv_path():
     ref = mx.mx_gemm_deq64(xq.cpu().numpy(), xs.cpu().numpy(), wp, wc)
     assert max_rel_err(y_tc, ref) <= 1e-4
     assert max_rel_err(y_gv, ref[::17]) <= 1e-4
+
+
+@pytest.mark.parametrize("name,N,K", [("q", 4096, 2048), ("k", 512, 2048), ("o", 2048, 4096)])
+def test_dense_projection_T16384(name, N, K):
+    """BASELINE config 3's dense projections at their full size, T = 16384
+    rows through lin_pq (the persistent tensor-core GEMM; v has k's shape).
+    Every row of y depends only on its own activation row, so the float64
+    oracle is evaluated on a sample of 264 rows spread over all 128-row tiles
+    (every 62nd row, plus the last); the whole output must be finite."""
+    M = 16384
+    g = torch.Generator(device="cuda").manual_seed(3 + N + K)
+    w = (torch.randn((N, K), generator=g, device="cuda") * 0.02).bfloat16()
+    x = torch.randn((M, K), generator=g, device="cuda").bfloat16()
+    dext = fp4_ext.get_decode_ext()
+    wq, wsc = dext.prequant(w)
+    xq, xsc = dext.prequant(x)
+    y = dext.lin_pq(xq, xsc, wq, wsc, M, N, K)
+    torch.cuda.synchronize()
+    assert _lib.load().mfi_device_error(1) == 0
+    assert bool(torch.isfinite(y).all())
+    rows = torch.from_numpy(np.r_[np.arange(0, M, 62), M - 1]).cuda()
+    ref = mx.mx_gemm_deq64(xq[rows].cpu().numpy(), xsc[rows].cpu().numpy(), wq.cpu().numpy(),
+                           wsc.cpu().numpy())
+    assert max_rel_err(y[rows].cpu().numpy(), ref) <= 1e-4
