@@ -453,6 +453,9 @@ def prefill_point(T, NL, dev, stream, zipf_alpha, steps, warmup, seed_base=100, 
     topi = torch.empty((NL, T, TOPK), dtype=torch.int32, device=dev)
     topw = torch.empty((NL, T, TOPK), dtype=torch.float32, device=dev)
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(NL)]
+    for row in evs:
+        for e in row:
+            e.record(stream)  # creates the event handles before the library records them
 
     def step(with_events=False):
         # T * top_k > 4096: mfi_moe_layer takes the prefill path by itself
@@ -543,12 +546,11 @@ def dropin_point(layers, T, dev, stream, steps, warmup, peak):
                           "down": (w.down_wp[e], w.down_sc[e])} for e in range(E)})
     g = torch.Generator(device=dev).manual_seed(17)
     X = torch.randn((NL, T, H), generator=g, device=dev).bfloat16()
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(NL)]
     uniq = [0] * NL
+    tabs = [None] * NL
     outs = [None] * NL
 
-    def step(with_events=False):
+    def step(keep_tables=False):
         for l in range(NL):
             w = layers[l].w
             hq, hs = dext.prequant(X[l])
@@ -565,14 +567,14 @@ def dropin_point(layers, T, dev, stream, steps, warmup, peak):
                 gsu_tab += [ex[e]["gate"][1] for e in sel] + [ex[e]["up"][1] for e in sel]
                 dw_tab += [ex[e]["down"][0] for e in sel]
                 ds_tab += [ex[e]["down"][1] for e in sel]
-            if with_events:
-                kev[l][0].record(stream)
             guv = dext.moe_gateup(hq, hs, gu_tab, gsu_tab, TOPK, T, MI, H)
             ydv = dext.moe_down(guv, dw_tab, ds_tab, TOPK, T, H, MI)
-            if with_events:
-                kev[l][1].record(stream)
-                uniq[l] = len(set(ids))
             outs[l] = dext.moe_combine(ydv, tv.reshape(T, TOPK).float(), T)
+            if keep_tables:
+                uniq[l] = len(set(ids))
+                ptr = lambda ts: torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64,
+                                              device=dev)
+                tabs[l] = (hq, hs, ptr(gu_tab), ptr(gsu_tab), ptr(dw_tab), ptr(ds_tab))
 
     for _ in range(warmup):
         step()
@@ -580,16 +582,66 @@ def dropin_point(layers, T, dev, stream, steps, warmup, peak):
     ms_per_layer = ms / steps / NL
     step(True)
     torch.cuda.synchronize(dev)
-    k_ms = sum(a.elapsed_time(b) for a, b in kev) / NL
+
+    # the operators' kernels alone: the graph-friendly _tab forms with the
+    # same routing's device pointer tables (built above, outside the timing),
+    # all layers captured in one CUDA graph
+    def kernels():
+        for l in range(NL):
+            hq, hs, gt, gs, dt, ds = tabs[l]
+            guv = dext.moe_gateup_tab(hq, hs, gt, gs, TOPK, T, MI, H)
+            dext.moe_down_tab(guv, dt, ds, TOPK, T, H, MI)
+
+    graph = capture(dev, stream, kernels, 1)
+    for _ in range(warmup):
+        graph.replay()
+    k_ms = event_time(dev, stream, graph.replay, steps) / steps / NL
+    del graph
     u = sum(uniq) / NL
     k_gbs = u * EXPERT_BYTES / (k_ms / 1e3) / 1e9
     lay_gbs = decode_layer_bytes(u, T) / (ms_per_layer / 1e3) / 1e9
     return {"tokens_per_s": T / (ms_per_layer / 1e3), "us_per_layer": ms_per_layer * 1e3,
             "unique_experts_per_layer": u,
-            "gateup_down_kernels": {"us_per_layer": k_ms * 1e3, "GBps": k_gbs, "frac": k_gbs / peak},
+            "gateup_down_kernels": {"us_per_layer": k_ms * 1e3, "GBps": k_gbs, "frac": k_gbs / peak,
+                                    "how": "moe_gateup_tab + moe_down_tab of every layer in one "
+                                           "CUDA graph, tables built outside the timing"},
             "layer": {"GBps": lay_gbs, "frac": lay_gbs / peak},
             "note": "host steps (.tolist(), pointer lists) inside the timed chain, as the "
                     "reference runner runs them"}
+
+
+def attn_point(dev, stream, steps, warmup, peak, ctx=4096, M=1, n_caches=48):
+    """FP8-KV decode attention (config 4's attention: 32 query / 4 KV heads,
+    head_dim 128) of M query rows at context `ctx` over n_caches distinct
+    layer caches (n_caches x ctx x 4 x 128 x 2 B, larger than L2), all calls
+    in one CUDA graph.  Bytes per call: the live K and V positions."""
+    from moe_fused_inference_b200 import fp4_ext
+    dext = fp4_ext.get_decode_ext()
+    Hq, Hkv, D = 32, 4, 128
+    max_pos = ctx + M
+    g = torch.Generator(device=dev).manual_seed(23)
+    caches = [(torch.randint(0, 120, (max_pos, Hkv, D), generator=g, device=dev,
+                             dtype=torch.int32).to(torch.uint8),
+               torch.randint(0, 120, (max_pos, Hkv, D), generator=g, device=dev,
+                             dtype=torch.int32).to(torch.uint8)) for _ in range(n_caches)]
+    q = torch.randn((M, Hq, D), generator=g, device=dev).bfloat16()
+    dpos = torch.tensor([ctx - 1], dtype=torch.int32, device=dev)
+    o = torch.empty((M, Hq, D), dtype=torch.float32, device=dev)
+
+    def calls():
+        for kk, vv in caches:
+            o.copy_(dext.attn_decode(q, kk, vv, dpos, None, M))
+
+    graph = capture(dev, stream, calls, 1)
+    for _ in range(warmup):
+        graph.replay()
+    us = event_time(dev, stream, graph.replay, steps) / steps / n_caches * 1e3
+    del graph, caches
+    torch.cuda.empty_cache()
+    kv_bytes = (ctx - 1 + M) * Hkv * D * 2
+    gbs = kv_bytes / us / 1e3
+    return {"us": us, "kv_bytes": kv_bytes, "GBps": gbs, "frac": gbs / peak,
+            "note": "includes a device-to-device copy of o per call (graph-captured)"}
 
 
 # ---------------------------------------------------------------------------
@@ -784,6 +836,9 @@ def run_ours(args, world, rank, local):
         line["dropin"] = {f"T{t}": dropin_point(layers, t, dev, stream, max(args.steps // 4, 3),
                                                  2, peak) for t in (1, 16)}
         torch.cuda.empty_cache()
+        # ---- FP8-KV decode attention (config 4's attention, context 4096) ----
+        line["attn_decode"] = {f"M{m}_ctx4096": attn_point(dev, stream, args.steps, 2, peak, M=m)
+                               for m in (1, 5)}
         # ---- prefill (config 3) on 4 of the decode weight sets ----
         pf = {}
         for t in (2048, 16384):

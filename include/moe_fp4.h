@@ -158,6 +158,42 @@ int mfi_moe_combine(const float* yd, int ystride, const float* w, int E, float* 
                     void* stream);
 
 /* ------------------------------------------------------------------------
+ * FP8 (E4M3) KV cache and single-sequence decode attention (head_dim 128)
+ * ------------------------------------------------------------------------ */
+
+/* KV write: k, v bf16 (M, Hkv, D) -> one byte per element at position
+ * *dpos + m of kvk, kvv (max_pos, Hkv, D); dpos is a device int32 read by the
+ * kernel (graph replay with a moving position), rows past max_pos or a
+ * negative base are skipped.  k_scale = v_scale = NULL: the reference's own
+ * encoder bit for bit (half-away-from-zero mantissa rounding, values below
+ * 2^-6 as round(|x| * 64), saturation to 0x7F).  Per-KV-head fp32 scales
+ * (Hkv each): the standard e4m3fn encoding of x / scale (round to nearest
+ * even, saturating at +-448).  k, v 16-byte, kvk, kvv 8-byte aligned; D a
+ * multiple of 8.
+ * Replaces mxfp4v2::launch_kvwrite_v2 (src/ext/mxfp4_decode.cu:485-490), bound
+ * by kv_write() (src/ext/mxfp4_decode_binding.cpp:161-173). */
+int mfi_kv_write(const void* k, const void* v, uint8_t* kvk, uint8_t* kvv, const int32_t* dpos,
+                 int M, int Hkv, int D, int max_pos, const float* k_scale, const float* v_scale,
+                 void* stream);
+
+/* Decode attention of M query rows of one sequence: q bf16 (M, Hq, D) (RoPE
+ * applied), row m attending to positions [0, *dpos + m] of the FP8 cache
+ * kvk, kvv (max_pos, Hkv, D), query head h reading KV head h / (Hq / Hkv);
+ * o fp32 (M, Hq, D) = softmax(q k^T / sqrt(D)) v with the cache decoded by the
+ * reference's decoder (scales NULL) or as standard e4m3fn times the per-head
+ * scales.  A row with no live position gets zeros.  D must be 128 and
+ * Hq / Hkv <= 16.  The positions are split over the grid; the partial
+ * results need mfi_attn_decode_workspace_bytes() of workspace (16-byte
+ * aligned).
+ * Replaces mxfp4v2::launch_attn_decode_v2 (src/ext/mxfp4_decode.cu:424-437),
+ * bound by attn_decode() (src/ext/mxfp4_decode_binding.cpp:213-230), whose
+ * score buffer `sc` this library does not need. */
+size_t mfi_attn_decode_workspace_bytes(int M, int Hq, int Hkv, int D, int max_pos);
+int mfi_attn_decode(const void* q, const uint8_t* kvk, const uint8_t* kvv, const int32_t* dpos,
+                    float* o, int M, int Hq, int Hkv, int D, int max_pos, const float* k_scale,
+                    const float* v_scale, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * Fused device-routed MoE layer (no reference counterpart as a single call:
  * it fulfils the reference's unimplemented K1/K2/K3 stubs
  * src/kernels/k1_router_topk_sort.cu, k2_mxfp4_grouped_gemm.cu,

@@ -38,6 +38,10 @@ SIGNATURES = {
     "mfi_moe_down_workspace_bytes": (_SZ, [_I, _I, _I]),
     "mfi_moe_down": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _VP, _SZ, _VP]),
     "mfi_moe_combine": (_I, [_VP, _I, _VP, _I, _VP, _I, _I, _VP]),
+    "mfi_kv_write": (_I, [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP, _VP, _VP]),
+    "mfi_attn_decode_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
+    "mfi_attn_decode": (_I, [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _VP, _VP, _VP, _SZ,
+                             _VP]),
     "mfi_moe_prepared_bytes": (_SZ, [_I, _I, _I]),
     "mfi_moe_prepare": (_I, [_VP, _VP, _SZ, _VP]),
     "mfi_moe_layer_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),

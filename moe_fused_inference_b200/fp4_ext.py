@@ -23,10 +23,12 @@ Differences on purpose:
   (src/ext/mxfp4_decode_binding.cpp:44-60);
 * weights shared by several (token, slot) entries are streamed once;
 * the stale call arities used by the reference's own tests and v3 runner
-  (``moe_down`` with 6 arguments, ``moe_combine`` with 2) are accepted and mean
-  M = 1;
-* ``attn_decode`` and ``kv_write`` (FP8-KV attention) are outside this
-  library's MoE path and raise ``NotImplementedError``.
+  (``moe_down`` with 6 arguments, ``moe_combine`` with 2, ``attn_decode`` and
+  ``kv_write`` with 5) are accepted and mean M = 1;
+* ``attn_decode`` does not write the score buffer ``sc`` (the reference
+  leaves raw scores there; no caller reads them) and splits the positions
+  over the grid; ``attn_decode`` / ``kv_write`` take optional per-KV-head
+  FP8 scales (the reference's cache has none).
 """
 
 from __future__ import annotations
@@ -60,16 +62,55 @@ def _require_f32(t: torch.Tensor, name: str) -> None:
            f"expected scalar type Float but found {str(t.dtype).replace('torch.', '')} ({name})")
 
 
+class _PinnedRing:
+    """Reusable pinned staging buffers for pointer-table uploads: allocating
+    pinned memory per call (cudaHostAlloc) costs far more than the copy.  A
+    slot is reused only after the copy that last read it has completed (an
+    event recorded behind the copy), so the host never overwrites a table the
+    GPU has not yet read."""
+
+    SLOTS = 16
+    ENTRIES = 8192
+
+    def __init__(self):
+        self.buf = torch.empty((self.SLOTS, self.ENTRIES), dtype=torch.int64).pin_memory()
+        self.np = self.buf.numpy()
+        self.events = [None] * self.SLOTS
+        self.next = 0
+
+    def upload(self, ptrs, dev: torch.device) -> torch.Tensor:
+        n = len(ptrs)
+        if n > self.ENTRIES:
+            return torch.tensor(ptrs, dtype=torch.int64).to(dev)
+        i = self.next
+        self.next = (i + 1) % self.SLOTS
+        if self.events[i] is not None:
+            self.events[i].synchronize()
+        self.np[i, :n] = ptrs
+        out = torch.empty(n, dtype=torch.int64, device=dev)
+        out.copy_(self.buf[i, :n], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(dev))
+        self.events[i] = ev
+        return out
+
+
+_RING: dict = {}
+
+
 def _ptr_table(ts, dev: torch.device) -> torch.Tensor:
     """Device int64 table of data pointers (reference make_ptr_table,
-    src/ext/mxfp4_decode_binding.cpp:44-60), uploaded asynchronously."""
+    src/ext/mxfp4_decode_binding.cpp:44-60), uploaded asynchronously from a
+    reusable pinned buffer."""
     _check(len(ts) > 0, "empty pointer table")
     ptrs = []
     for t in ts:
         _check(t.is_cuda and t.dtype == torch.uint8, "ptr table entries must be cuda uint8")
         ptrs.append(t.data_ptr())
-    host = torch.tensor(ptrs, dtype=torch.int64).pin_memory()
-    return host.to(dev, non_blocking=True)
+    ring = _RING.get(dev.index)
+    if ring is None:
+        ring = _RING[dev.index] = _PinnedRing()
+    return ring.upload(ptrs, dev)
 
 
 def _workspace(nbytes: int, dev: torch.device) -> torch.Tensor:
@@ -260,14 +301,70 @@ class _DecodeExt:
         return out
 
     @staticmethod
-    def attn_decode(*args, **kwargs):
-        raise NotImplementedError(
-            "attn_decode (FP8-KV decode attention) is not part of this library's MoE path")
+    def attn_decode(q, kvk, kvv, dpos, sc, M=1, k_scale=None, v_scale=None):
+        """o fp32 (M, Hq, D): decode attention of M query rows of one sequence
+        over the layer's FP8 cache kvk/kvv (max_pos, Hkv, D) up to position
+        dpos[0] + m (reference src/ext/mxfp4_decode_binding.cpp:213-230).
+        ``sc`` (the reference's score buffer) is accepted and left untouched;
+        the stale 5-argument call and a 2-D q (Hq, D) mean M = 1.  Optional
+        per-KV-head ``k_scale``/``v_scale`` (fp32 (Hkv,)) select the standard
+        e4m3fn cache format with scales (this library's addition)."""
+        lib = _lib.load()
+        M = int(M)
+        _check(q.is_cuda and kvk.is_cuda and kvv.is_cuda and dpos.is_cuda, "tensors must be cuda")
+        _check(q.dtype == torch.bfloat16, "q must be bfloat16")
+        if q.dim() == 2:
+            q = q.unsqueeze(0)
+        q = q.contiguous()
+        kvk = kvk.view(torch.uint8) if kvk.dtype != torch.uint8 else kvk
+        kvv = kvv.view(torch.uint8) if kvv.dtype != torch.uint8 else kvv
+        _check(kvk.dim() == 3 and kvv.shape == kvk.shape and kvk.is_contiguous()
+               and kvv.is_contiguous(), "kvk/kvv must be contiguous (max_pos, Hkv, D)")
+        _check(dpos.dtype == torch.int32, "dpos must be int32")
+        Hq, D = int(q.shape[1]), int(q.shape[2])
+        max_pos, Hkv = int(kvk.shape[0]), int(kvk.shape[1])
+        _check(q.shape[0] >= M, "q has fewer than M rows")
+        o = torch.empty((M, Hq, D), dtype=torch.float32, device=q.device)
+        ks = vs = 0
+        if k_scale is not None or v_scale is not None:
+            _check(k_scale is not None and v_scale is not None, "give both scales or neither")
+            k_scale = k_scale.to(q.device, torch.float32).contiguous()
+            v_scale = v_scale.to(q.device, torch.float32).contiguous()
+            _check(k_scale.numel() == Hkv and v_scale.numel() == Hkv, "one scale per KV head")
+            ks, vs = k_scale.data_ptr(), v_scale.data_ptr()
+        ws = _workspace(lib.mfi_attn_decode_workspace_bytes(M, Hq, Hkv, D, max_pos), q.device)
+        _lib.check(lib.mfi_attn_decode(_ptr(q), _ptr(kvk), _ptr(kvv), _ptr(dpos), _ptr(o), M, Hq,
+                                       Hkv, D, max_pos, ks, vs, _ptr(ws), ws.numel(),
+                                       _stream(q.device)), "attn_decode")
+        return o
 
     @staticmethod
-    def kv_write(*args, **kwargs):
-        raise NotImplementedError(
-            "kv_write (FP8-KV cache write) is not part of this library's MoE path")
+    def kv_write(k, v, kvk, kvv, dpos, M=1, k_scale=None, v_scale=None):
+        """Write M rows of k, v (bf16 (M, Hkv, D)) into the FP8 cache slices
+        kvk/kvv (max_pos, Hkv, D) at positions dpos[0] + m (reference
+        src/ext/mxfp4_decode_binding.cpp:161-173; the stale 5-argument call
+        means M = 1).  Without scales the bytes are the reference encoder's,
+        bit for bit; with per-KV-head scales, standard e4m3fn of x / scale."""
+        lib = _lib.load()
+        M = int(M)
+        kvk = kvk.view(torch.uint8) if kvk.dtype != torch.uint8 else kvk
+        kvv = kvv.view(torch.uint8) if kvv.dtype != torch.uint8 else kvv
+        _check(k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16, "k and v must be bfloat16")
+        _check(dpos.dtype == torch.int32, "dpos must be int32")
+        _check(kvk.dim() == 3 and kvv.shape == kvk.shape and kvk.is_contiguous()
+               and kvv.is_contiguous(), "kvk/kvv must be contiguous (max_pos, Hkv, D)")
+        k, v = k.contiguous(), v.contiguous()
+        max_pos, Hkv, D = (int(s) for s in kvk.shape)
+        _check(k.numel() >= M * Hkv * D and v.numel() >= M * Hkv * D, "k/v smaller than (M, Hkv, D)")
+        ks = vs = 0
+        if k_scale is not None or v_scale is not None:
+            _check(k_scale is not None and v_scale is not None, "give both scales or neither")
+            k_scale = k_scale.to(k.device, torch.float32).contiguous()
+            v_scale = v_scale.to(k.device, torch.float32).contiguous()
+            _check(k_scale.numel() == Hkv and v_scale.numel() == Hkv, "one scale per KV head")
+            ks, vs = k_scale.data_ptr(), v_scale.data_ptr()
+        _lib.check(lib.mfi_kv_write(_ptr(k), _ptr(v), _ptr(kvk), _ptr(kvv), _ptr(dpos), M, Hkv, D,
+                                    max_pos, ks, vs, _stream(k.device)), "kv_write")
 
 
 _EXT = _LinearExt()

@@ -75,5 +75,9 @@ def test_binding_checks_mirror_reference_messages(lib):
         dext.moe_combine(torch.zeros(8, 4), torch.zeros(7), 2)
     with pytest.raises(RuntimeError, match="yd \\(M\\*E,N\\)"):
         dext.moe_combine(torch.zeros(6, 4), torch.zeros(8), 1)
-    with pytest.raises(NotImplementedError):
-        dext.attn_decode()
+    d = torch.zeros(1, dtype=torch.int32)
+    kv = torch.zeros(16, 4, 128, dtype=torch.uint8)
+    with pytest.raises(RuntimeError, match="tensors must be cuda"):
+        dext.attn_decode(torch.zeros(1, 32, 128, dtype=torch.bfloat16), kv, kv, d, None, 1)
+    with pytest.raises(RuntimeError, match="k and v must be bfloat16"):
+        dext.kv_write(torch.zeros(1, 4, 128), torch.zeros(1, 4, 128), kv, kv, d, 1)
