@@ -53,6 +53,10 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kMaxGroup = 16;    // query heads per KV head
 constexpr int kRowsPerPass = 4;  // query rows held in registers per pass
 constexpr int kKStride = kD + 4; // padded fp32 row of the K tile (conflict-free float4 reads)
+// one split's partial result: D accumulators, then max and sum, padded so
+// every row starts on a 16-byte boundary (the accumulators go out as float4)
+constexpr int kPartStride = kD + 4;
+static_assert((kPartStride * 4) % 16 == 0, "partial rows must stay 16-byte aligned");
 
 // ---- FP8 codecs --------------------------------------------------------------
 // The reference encoder, restated: sign from v < 0; frexp exponent e of |v|;
@@ -159,7 +163,7 @@ struct AttnArgs {
   const int* dpos;
   const float* k_scale;     // (Hkv) or null (reference codec)
   const float* v_scale;
-  float* part;              // [M][Hq][nsplit][D + 2]: acc[D], max, sum
+  float* part;              // [M][Hq][nsplit][kPartStride]: acc[D], max, sum, pad
   float* o;                 // (M, Hq, D)
   int M, Hq, Hkv, max_pos, nsplit, chunk;
   float inv_sqrt_d;
@@ -191,7 +195,7 @@ __global__ void __launch_bounds__(kThreads) attn_partial_kernel(AttnArgs a) {
   // positions a row m may see: [0, base + m]
   const int live_hi = min(base + a.M, a.max_pos);  // exclusive bound over all rows
   const int p_hi = min(p_lo + a.chunk, live_hi);
-  const size_t part_stride = size_t(kD + 2);
+  const size_t part_stride = size_t(kPartStride);
   __syncthreads();
 
   for (int m0 = 0; m0 < a.M; m0 += kRowsPerPass) {
@@ -252,7 +256,10 @@ __global__ void __launch_bounds__(kThreads) attn_partial_kernel(AttnArgs a) {
             s = fmaf(q4.z, k4.z, s);
             s = fmaf(q4.w, k4.w, s);
           }
-          const bool live = pos < p_hi && pos <= base + m0 + r;
+          // a row whose own position lies outside the cache attends to nothing
+          // (the reference skips it), so it merges to zeros
+          const int row_pos = base + m0 + r;
+          const bool live = pos < p_hi && pos <= row_pos && row_pos < a.max_pos && base >= 0;
           const float x = live ? s * qscale : -INFINITY;
           float tmax = x;
 #pragma unroll
@@ -309,17 +316,17 @@ __global__ void __launch_bounds__(kThreads) attn_partial_kernel(AttnArgs a) {
 // position lies outside the cache has no live position and gets zeros.
 __global__ void __launch_bounds__(kD) attn_merge_kernel(AttnArgs a) {
   const int m = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
-  const float* pp = a.part + (size_t(m) * a.Hq + h) * a.nsplit * size_t(kD + 2);
+  const float* pp = a.part + (size_t(m) * a.Hq + h) * a.nsplit * size_t(kPartStride);
   float gmax = -INFINITY;
-  for (int j = 0; j < a.nsplit; ++j) gmax = fmaxf(gmax, pp[j * (kD + 2) + kD]);
+  for (int j = 0; j < a.nsplit; ++j) gmax = fmaxf(gmax, pp[j * kPartStride + kD]);
   float num = 0.0f, den = 0.0f;
   if (gmax != -INFINITY) {
     for (int j = 0; j < a.nsplit; ++j) {
-      const float mj = pp[j * (kD + 2) + kD];
+      const float mj = pp[j * kPartStride + kD];
       if (mj == -INFINITY) continue;
       const float c = expf(mj - gmax);
-      num = fmaf(pp[j * (kD + 2) + d], c, num);
-      den = fmaf(pp[j * (kD + 2) + kD + 1], c, den);
+      num = fmaf(pp[j * kPartStride + d], c, num);
+      den = fmaf(pp[j * kPartStride + kD + 1], c, den);
     }
   }
   a.o[(size_t(m) * a.Hq + h) * kD + d] = den > 0.0f ? num / den : 0.0f;
@@ -372,7 +379,7 @@ extern "C" size_t mfi_attn_decode_workspace_bytes(int M, int Hq, int Hkv, int D,
   if (M <= 0 || Hq <= 0 || Hkv <= 0 || D <= 0 || max_pos <= 0) return 0;
   int nsplit, chunk;
   mfi::split_layout(max_pos, Hkv, nsplit, chunk);
-  return size_t(M) * Hq * nsplit * (D + 2) * sizeof(float);
+  return size_t(M) * Hq * nsplit * mfi::kPartStride * sizeof(float);
 }
 
 extern "C" int mfi_attn_decode(const void* q, const uint8_t* kvk, const uint8_t* kvv,

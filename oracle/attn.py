@@ -34,7 +34,8 @@ import numpy as np
 def e4m3_ref_encode(x) -> np.ndarray:
     x = np.asarray(x, dtype=np.float32)
     sign = np.where(x < 0, 0x80, 0).astype(np.int64)
-    a = np.abs(x).astype(np.float64)
+    with np.errstate(invalid="ignore"):
+        a = np.abs(x).astype(np.float64)
     finite = np.isfinite(a)
     a_f = np.where(finite, a, 1.0)
     m, e = np.frexp(a_f)
