@@ -216,6 +216,15 @@ typedef struct mfi_moe_weights {
   const void* prepared;     /* blocks from mfi_moe_prepare, or NULL       */
   const float* logit_bias;  /* [E] fp32 added to the router logits before
                                top-k (e.g. a synthetic load skew), or NULL */
+  /* RMSNorm fused into the router (the MoE block's post-attention layernorm,
+   * reference runtime/model_runner.py:20-25 called at
+   * runtime/model_runner_v2.py:183): with norm_weight (bf16 [hidden]) set,
+   * x is the residual stream and every token row is normalised before it is
+   * quantised: r = 1 / sqrt(float(ss) / hidden + norm_eps), ss the row's sum
+   * of squares accumulated in fp64, each element bf16(bf16(x * r) * weight).
+   * NULL: x is quantised as given. */
+  const void* norm_weight;
+  float norm_eps;
 } mfi_moe_weights;
 
 /* Tensor-core form of the layer's expert weights.  When hidden and inter are

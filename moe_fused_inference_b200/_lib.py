@@ -85,7 +85,8 @@ class MoEWeights(ctypes.Structure):
         ("gate_wp", _VP), ("gate_sc", _VP), ("up_wp", _VP), ("up_sc", _VP),
         ("down_wp", _VP), ("down_sc", _VP), ("router_wp", _VP), ("router_sc", _VP),
         ("n_experts", _I), ("hidden", _I), ("inter", _I), ("top_k", _I),
-        ("prepared", _VP), ("logit_bias", _VP),
+        ("prepared", _VP), ("logit_bias", _VP), ("norm_weight", _VP),
+        ("norm_eps", ctypes.c_float),
     ]
 
 

@@ -78,7 +78,7 @@ extern "C" {
 
 const char* mfi_last_error(void) { return g_err.c_str(); }
 
-int mfi_version(void) { return 2; }
+int mfi_version(void) { return 3; }  // 3: mfi_moe_weights gained norm_weight / norm_eps
 
 // ---------------------------------------------------------------------------
 int mfi_quantize_rows(const void* x, int dtype, long long ld_x, int half_roundtrip, uint8_t* xq,
@@ -454,6 +454,8 @@ int run_prefill(const mfi_moe_weights* w, const void* x_bf16, int T, float* out,
   ra.x8 = s.x8;
   ra.r8 = s.r8;
   ra.logit_bias = w->logit_bias;
+  ra.norm_w = static_cast<const __nv_bfloat16*>(w->norm_weight);
+  ra.norm_eps = w->norm_eps;
   ra.err = mfi::device_error_flag();
   rc = cuda_status(mfi::launch_route(ra, st), "moe_layer prefill route launch");
   if (rc == MFI_OK) rc = rec(1);
@@ -637,6 +639,8 @@ int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float*
   ra.T_pad = s.T_pad;
   ra.err = mfi::device_error_flag();
   ra.logit_bias = w->logit_bias;
+  ra.norm_w = static_cast<const __nv_bfloat16*>(w->norm_weight);
+  ra.norm_eps = w->norm_eps;
   if (tc && w->prepared && (reinterpret_cast<uintptr_t>(w->prepared) & 15) == 0) {
     // the router issues the gate/up weight prefetch after its own loads
     ra.pf_base = static_cast<const uint8_t*>(w->prepared);
@@ -717,6 +721,8 @@ int mfi_moe_route(const mfi_moe_weights* w, const void* x_bf16, int T, uint8_t* 
   ra.logits = logits; ra.topi = topi; ra.topw = topw;
   ra.err = mfi::device_error_flag();
   ra.logit_bias = w->logit_bias;
+  ra.norm_w = static_cast<const __nv_bfloat16*>(w->norm_weight);
+  ra.norm_eps = w->norm_eps;
   // no work lists, no expert regions: the kernel stops after the routing
   return cuda_status(mfi::launch_route(ra, as_stream(stream)), "moe_route launch");
 }
@@ -1003,6 +1009,8 @@ int mfi_ep_route_dispatch(const mfi_moe_weights* w, const void* x_bf16, int T, i
   ra.topi = topi; ra.topw = topw;
   ra.err = mfi::device_error_flag();
   ra.logit_bias = w->logit_bias;
+  ra.norm_w = static_cast<const __nv_bfloat16*>(w->norm_weight);
+  ra.norm_eps = w->norm_eps;
   ra.ep.table = static_cast<const mfi::EpTable*>(table);
   ra.ep.flags = fl;
   ra.ep.pack_pos = pack_pos;

@@ -38,7 +38,10 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   const int nb = a.H >> 5;
 
   // ---- quantise token t (the reference's prequant, fused) -------------------
-  // one thread per 8 elements, a quad per 32-element block (quant_group8)
+  // one thread per 8 elements, a quad per 32-element block (quant_group8);
+  // with a norm weight every warp first computes the row's RMS factor (the
+  // same value in every warp)
+  const float rms_r = a.norm_w ? warp_rms_inv(a, t, lane) : 1.0f;
   for (int base = warp * 32; base < (a.H >> 3); base += kRouteThreads) {
     const int c8 = base + lane;
     const bool live = c8 < (a.H >> 3);
@@ -53,6 +56,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
         v[2 * i] = f.x;
         v[2 * i + 1] = f.y;
       }
+      if (a.norm_w) rms_apply8(a, c8 * 8, rms_r, v);
     } else {
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[i] = 0.0f;
@@ -443,7 +447,8 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
     for (int e = threadIdx.x; e < a.E; e += kClusterThreads) s_logit[e] = 0.0f;
   cluster_arrive_release();  // every CTA of the cluster has started (and the init is ordered)
 
-  // ---- quantise token t ----------------------------------------------------
+  // ---- quantise token t (RMS-normalised first when a.norm_w is set) --------
+  const float rms_r = a.norm_w ? warp_rms_inv(a, t, lane) : 1.0f;
   for (int base = warp * 32; base < (a.H >> 3); base += kClusterThreads) {
     const int c8 = base + lane;
     const bool live = c8 < (a.H >> 3);
@@ -458,6 +463,7 @@ __global__ void __launch_bounds__(kClusterThreads) route_cluster_kernel(RouteArg
         v[2 * i] = f.x;
         v[2 * i + 1] = f.y;
       }
+      if (a.norm_w) rms_apply8(a, c8 * 8, rms_r, v);
     } else {
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[i] = 0.0f;

@@ -13,10 +13,55 @@ __device__ __forceinline__ bool better(float v, int i, float w, int j) {
   return v > w || (v == w && i < j);
 }
 
-// One warp quantises token t (bf16 row of a.x) into s_xq (H/2 packed bytes)
-// and s_xsc (H/32 E8M0 codes); t < 0 gives an all-zero row (codes 127).
+// RMSNorm of a token row before quantisation — the MoE block's
+// post-attention layernorm (reference runtime/model_runner.py:20-25, called at
+// runtime/model_runner_v2.py:183):
+//   r = 1 / sqrt(float(ss) / H + eps),  ss = sum of x_i^2,
+//   y_i = bf16(bf16(x_i * r) * w_i)
+// (the reference normalises in fp32, casts to the activation type, then
+// multiplies by the bf16 weight).  ss is accumulated in fp64: every square of
+// a bf16 value is exact there, so the sum is exact, whatever the order, for
+// any row whose magnitudes span less than 2^13, and rounded to fp32 once.
+// One warp computes r for row t (every lane returns it).
+__device__ __forceinline__ float warp_rms_inv(const RouteArgs& a, int t, int lane) {
+  const __nv_bfloat16* row = reinterpret_cast<const __nv_bfloat16*>(a.x) + long(t) * a.H;
+  double ss = 0.0;
+  for (int c8 = lane; c8 < (a.H >> 3); c8 += 32) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(row + c8 * 8);
+    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h2[i]);
+      ss += double(f.x) * double(f.x);
+      ss += double(f.y) * double(f.y);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float var = __fdiv_rn(__double2float_rn(ss), float(a.H));
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, a.norm_eps)));
+}
+
+// Elements c .. c+7 of a normalised row (see warp_rms_inv), in place.
+__device__ __forceinline__ void rms_apply8(const RouteArgs& a, int c, float r, float (&v)[8]) {
+  const uint4 wr = *reinterpret_cast<const uint4*>(a.norm_w + c);
+  const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wr);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 w = __bfloat1622float2(w2[i]);
+    const float y0 = __bfloat162float(__float2bfloat16_rn(__fmul_rn(v[2 * i], r)));
+    const float y1 = __bfloat162float(__float2bfloat16_rn(__fmul_rn(v[2 * i + 1], r)));
+    v[2 * i] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(y0, w.x)));
+    v[2 * i + 1] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(y1, w.y)));
+  }
+}
+
+// One warp quantises token t (bf16 row of a.x, RMS-normalised first when
+// a.norm_w is set) into s_xq (H/2 packed bytes) and s_xsc (H/32 E8M0 codes);
+// t < 0 gives an all-zero row (codes 127).
 __device__ __forceinline__ void warp_quant_token(const RouteArgs& a, int t, uint8_t* s_xq,
                                                  uint8_t* s_xsc, int lane) {
+  const float r = (a.norm_w && t >= 0) ? warp_rms_inv(a, t, lane) : 1.0f;
   for (int base = 0; base < (a.H >> 3); base += 32) {
     const int c8 = base + lane;
     const bool live = c8 < (a.H >> 3);
@@ -31,6 +76,7 @@ __device__ __forceinline__ void warp_quant_token(const RouteArgs& a, int t, uint
         v[2 * i] = f.x;
         v[2 * i + 1] = f.y;
       }
+      if (a.norm_w) rms_apply8(a, c8 * 8, r, v);
     } else {
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[i] = 0.0f;

@@ -149,6 +149,8 @@ __global__ void __launch_bounds__(kQxThreads) quant_x8_kernel(RouteArgs a, int n
     // quant_group8: block maximum, NaN -> code 127, nibbles at 2^-e)
     const int t = blockIdx.x * kQxTok + warp;  // < ceil(T/128) * 128
     const int tt = t < a.T ? t : -1;
+    // RMSNorm factor of the row when a norm weight is given (route_common.cuh)
+    const float rms_r = (a.norm_w && tt >= 0) ? warp_rms_inv(a, tt, lane) : 1.0f;
     uint4 packed[kRtMaxBlk / 32];
     int code[kRtMaxBlk / 32];
     int lo = 255, hi = 0;
@@ -168,12 +170,16 @@ __global__ void __launch_bounds__(kQxThreads) quant_x8_kernel(RouteArgs a, int n
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw[q]);
+          float u[8];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const float2 f = __bfloat1622float2(h2[i]);
-            v[q * 8 + 2 * i] = f.x;
-            v[q * 8 + 2 * i + 1] = f.y;
+            u[2 * i] = f.x;
+            u[2 * i + 1] = f.y;
           }
+          if (a.norm_w) rms_apply8(a, b * 32 + q * 8, rms_r, u);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[q * 8 + i] = u[i];
         }
       } else {
 #pragma unroll

@@ -101,6 +101,9 @@ struct RouteArgs {
   unsigned long long pf_bytes;
   EpDispatch ep;       // ep.table == null: no expert-parallel dispatch
   const float* logit_bias;  // [E] added to the logits before top-k, or null
+  // RMSNorm of each token row before quantisation (route_common.cuh), or null
+  const __nv_bfloat16* norm_w;  // [H] bf16 weight
+  float norm_eps;
   // prefill placement: slot_pos[t*k + j] = the pair's position among the
   // tokens of its expert (cursor claim, no row copy)
   int* slot_pos;

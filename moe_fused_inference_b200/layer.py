@@ -135,9 +135,14 @@ def random_layer_weights(n_experts=128, hidden=2048, inter=768, std=0.02, seed=0
 class MoELayer:
     """One device-routed MoE layer call per forward (library entry mfi_moe_layer)."""
 
-    def __init__(self, weights: MoELayerWeights, top_k: int = 8, logit_bias=None):
+    def __init__(self, weights: MoELayerWeights, top_k: int = 8, logit_bias=None,
+                 norm_weight=None, norm_eps: float = 1e-6):
         """``logit_bias``: optional cuda float32 (E,) added to the router logits
-        before top-k (a synthetic load skew; the reference has no such term)."""
+        before top-k (a synthetic load skew; the reference has no such term).
+        ``norm_weight``: optional bf16 (hidden,) RMSNorm weight — the MoE
+        block's post-attention layernorm (runtime/model_runner.py:20-25) fused
+        into the router: forward() then takes the residual stream x and
+        normalises each row before quantising it."""
         weights.validate()
         if not 1 <= top_k <= min(weights.n_experts, 32):
             raise RuntimeError("top_k must be in [1, min(E, 32)]")
@@ -157,6 +162,14 @@ class MoELayer:
                 raise RuntimeError("logit_bias must have shape (E,)")
             self.logit_bias = lb
             self._cw.logit_bias = lb.data_ptr()
+        self.norm_weight = None
+        if norm_weight is not None:
+            nw = norm_weight.to(device=weights.gate_wp.device, dtype=torch.bfloat16).contiguous()
+            if nw.shape != (weights.hidden,):
+                raise RuntimeError("norm_weight must have shape (hidden,)")
+            self.norm_weight = nw
+            self._cw.norm_weight = nw.data_ptr()
+            self._cw.norm_eps = float(norm_eps)
         # tensor-core scale atoms, built once per weight set (mfi_moe_prepare)
         nprep = int(lib.mfi_moe_prepared_bytes(weights.n_experts, weights.hidden, weights.inter))
         self.prepared = None

@@ -21,6 +21,8 @@ Fixtures:
   dequant.npz          mxfp4_reconstruct_gpu(device="cpu") of a packed tensor.
   route_moe.npz        ModelRunner.moe_route + moe_compute(variant="mxfp4") on
                        a small layer (BASELINE config 1 semantics, reduced size).
+  rms_norm.npz         model_runner.rms_norm (runtime/model_runner.py:20-25) on
+                       64 bf16 rows of width 2048 with a bf16 weight.
 """
 
 import hashlib
@@ -148,6 +150,20 @@ def main():
         scores=scores.float().numpy(), out=out.float().numpy(),
         dims=np.array([E, H, MI, T, K]), **packs,
     )
+
+    # ---- 6. rms_norm (the MoE block's post-attention layernorm) ------------
+    from model_runner import rms_norm  # noqa: E402
+    rng = np.random.default_rng(6)
+    rows = rng.standard_normal((64, 2048)).astype(np.float32)
+    rows *= np.power(2.0, rng.integers(-8, 9, size=(64, 1))).astype(np.float32)
+    x = torch.from_numpy(rows).bfloat16()
+    w = torch.from_numpy(1.0 + 0.1 * rng.standard_normal(2048).astype(np.float32)).bfloat16()
+    y = rms_norm(x, w, 1e-6)
+    np.savez_compressed(
+        os.path.join(HERE, "rms_norm.npz"),
+        x=x.view(torch.int16).numpy().astype(np.uint16),
+        w=w.view(torch.int16).numpy().astype(np.uint16),
+        y=y.view(torch.int16).numpy().astype(np.uint16), eps=np.float32(1e-6))
     print("golden fixtures written to", HERE)
 
 

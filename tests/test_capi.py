@@ -43,7 +43,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_workspace_queries_are_pure_host(lib):
-    assert lib.mfi_version() == 2
+    assert lib.mfi_version() == 3
     assert lib.mfi_moe_layer_workspace_bytes(64, 2048, 768, 128, 8) > 64 * 8 * 2048 * 4
     assert lib.mfi_moe_gateup_workspace_bytes(8, 1) >= 16 * (24 + 16)
     assert lib.mfi_linear_workspace_bytes(16, 256, 2048) >= 16 * (1024 + 64)
@@ -81,3 +81,28 @@ def test_binding_checks_mirror_reference_messages(lib):
         dext.attn_decode(torch.zeros(1, 32, 128, dtype=torch.bfloat16), kv, kv, d, None, 1)
     with pytest.raises(RuntimeError, match="k and v must be bfloat16"):
         dext.kv_write(torch.zeros(1, 4, 128), torch.zeros(1, 4, 128), kv, kv, d, 1)
+
+
+def test_weights_struct_layout_matches_header(tmp_path):
+    """The ctypes mirror of mfi_moe_weights (the layer's C-ABI argument) has
+    the header's field offsets and size: a C probe compiled with gcc prints
+    them."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not available")
+    fields = [f for f, _ in _lib.MoEWeights._fields_]
+    src = tmp_path / "probe.c"
+    src.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "moe_fp4.h"\nint main(void) {\n'
+        + "".join(f'  printf("{f} %zu\\n", offsetof(mfi_moe_weights, {f}));\n' for f in fields)
+        + '  printf("sizeof %zu\\n", sizeof(mfi_moe_weights));\n  return 0;\n}\n')
+    exe = tmp_path / "probe"
+    inc = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
+    subprocess.run([gcc, "-I", inc, str(src), "-o", str(exe)], check=True)
+    out = dict(line.split() for line in subprocess.run([str(exe)], check=True, capture_output=True,
+                                                       text=True).stdout.splitlines())
+    for f in fields:
+        assert int(out[f]) == getattr(_lib.MoEWeights, f).offset, f
+    assert int(out["sizeof"]) == ctypes.sizeof(_lib.MoEWeights)

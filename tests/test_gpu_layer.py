@@ -76,3 +76,39 @@ def test_layer_repeatable_and_graph_capturable(qwen_layer):
     graph.replay()
     torch.cuda.synchronize()
     assert torch.equal(o, out1)
+
+
+@pytest.mark.parametrize("T,path", [(1, "decode"), (8, "decode"), (64, "decode"),
+                                    (600, "prefill"), (300, "prefill")])
+def test_layer_fused_rms_norm(qwen_layer, T, path):
+    """RMSNorm fused into the router (the MoE block's post-attention
+    layernorm, runtime/model_runner.py:20-25 at runtime/model_runner_v2.py:183):
+    the layer takes the residual stream; its routing must equal the oracle's
+    on rms_norm_bf16(x) bit for bit and its output meet the layer contract.
+    Covers the decode cluster router (T <= 64), the tensor-core prefill router
+    (T = 600) and the cluster router with the prefill's count-based placement
+    (T = 300)."""
+    g = torch.Generator(device="cuda").manual_seed(300 + T)
+    x = (torch.randn((T, 2048), generator=g, device="cuda") * 3.0).bfloat16()
+    w = (1.0 + 0.1 * torch.randn(2048, generator=g, device="cuda")).bfloat16()
+    layer = MoELayer(qwen_layer, top_k=8, norm_weight=w, norm_eps=1e-6)
+    logits = torch.empty((T, 128), dtype=torch.float32, device="cuda")
+    run = layer.prefill if path == "prefill" else layer.forward
+    out, topi, topw = run(x, logits=logits)
+    torch.cuda.synchronize()
+    from moe_fused_inference_b200 import _lib
+    assert _lib.load().mfi_device_error(1) == 0
+    xn = mx.rms_norm_bf16(x.float().cpu().numpy(), w.float().cpu().numpy(), 1e-6)
+    ref = mx.moe_layer(xn, oracle_weights(qwen_layer), topk=8, fast=T > 64)
+    assert np.array_equal(logits.cpu().numpy(), ref["logits"])
+    assert np.array_equal(topi.cpu().numpy(), ref["idx"])
+    o = out.cpu().numpy()
+    assert cosine(o, ref["out"]) >= 0.999
+    assert max_rel_err(o, ref["out"]) <= 1e-2
+    # the same as normalising first and running the unfused layer
+    plain = MoELayer(qwen_layer, top_k=8)
+    xn_t = torch.from_numpy(xn).bfloat16().cuda()
+    out2, topi2, _ = (plain.prefill if path == "prefill" else plain.forward)(xn_t)
+    torch.cuda.synchronize()
+    assert torch.equal(topi2, topi)
+    assert torch.equal(out2, out)

@@ -176,3 +176,17 @@ def test_torch_cpu_quant_dequant_equals_numpy_oracle():
     ref = mx.dequantize_rows(*mx.quantize_rows(w.float().numpy()), 200)
     got = moe_ref.quant_dequant_bf16(w)
     assert torch.equal(got, torch.from_numpy(ref).bfloat16())
+
+
+def test_rms_norm_oracle_matches_reference(golden):
+    """The fused RMSNorm's restatement against the reference's own
+    model_runner.rms_norm (fixture from tests/golden/make_golden.py, 64 rows
+    of 2048 with magnitudes from 2^-8 to 2^8).  The definitions could differ
+    only through the rounding of the fp32 sum of squares (torch sums in fp32,
+    the library exactly and rounds once); on the fixture every one of the
+    131,072 normalised bf16 values is identical."""
+    from tests.conftest import bf16_bits_to_f32
+    g = golden("rms_norm.npz")
+    x, w, y = bf16_bits_to_f32(g["x"]), bf16_bits_to_f32(g["w"]), bf16_bits_to_f32(g["y"])
+    got = mx.rms_norm_bf16(x, w, float(g["eps"]))
+    assert np.array_equal(got, y)
