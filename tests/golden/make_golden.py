@@ -23,6 +23,10 @@ Fixtures:
                        a small layer (BASELINE config 1 semantics, reduced size).
   rms_norm.npz         model_runner.rms_norm (runtime/model_runner.py:20-25) on
                        64 bf16 rows of width 2048 with a bf16 weight.
+  mirror_ref/          an MXFP4 mirror (safetensors shards, index, manifest)
+                       written by the reference's run_quantization
+                       (quant/quantize_mxfp4.py:175-223) from the seeded mini
+                       checkpoint of mini_checkpoint().
 """
 
 import hashlib
@@ -164,7 +168,45 @@ def main():
         x=x.view(torch.int16).numpy().astype(np.uint16),
         w=w.view(torch.int16).numpy().astype(np.uint16),
         y=y.view(torch.int16).numpy().astype(np.uint16), eps=np.float32(1e-6))
+
+    # ---- 7. an MXFP4 mirror written by the reference's own quantiser -------
+    import shutil
+    import tempfile
+    from safetensors.torch import save_file as save_torch
+    from quantize_mxfp4 import run_quantization  # noqa: E402
+    src = tempfile.mkdtemp(prefix="mfi_mini_ckpt_")
+    save_torch(mini_checkpoint(), os.path.join(src, "model.safetensors"))
+    out = os.path.join(HERE, "mirror_ref")
+    shutil.rmtree(out, ignore_errors=True)
+    run_quantization(src, out, MIRROR_PATTERN, MIRROR_SHARD_GB, True)
+    shutil.rmtree(src)
     print("golden fixtures written to", HERE)
+
+
+# The mirror fixture's inputs: one layer of 4 bf16 experts (K = 100, not a
+# multiple of 32), a fifth expert stored as FP8 with a 128 x 128 block
+# scale_inv (the official checkpoint's form), the router and a norm weight.
+# Shared with the tests, which rebuild the same checkpoint.
+MIRROR_PATTERN = r"(experts\.\d+\.(gate|up|down)_proj|mlp\.gate)\.weight$"
+MIRROR_SHARD_GB = 16e-6  # about 17 KB: several shards and an index
+
+
+def mini_checkpoint():
+    rng = np.random.default_rng(7)
+    t = {}
+    bf = lambda a: torch.from_numpy(a.astype(np.float32)).bfloat16()
+    pre = "model.layers.0.mlp"
+    for e in range(4):
+        t[f"{pre}.experts.{e}.gate_proj.weight"] = bf(rng.standard_normal((64, 100)) * 0.02)
+        t[f"{pre}.experts.{e}.up_proj.weight"] = bf(rng.standard_normal((64, 100)) * 0.02)
+        t[f"{pre}.experts.{e}.down_proj.weight"] = bf(rng.standard_normal((100, 64)) * 0.02)
+    w8 = torch.from_numpy(rng.standard_normal((128, 256)).astype(np.float32) * 8.0)
+    t[f"{pre}.experts.4.gate_proj.weight"] = w8.to(torch.float8_e4m3fn)
+    t[f"{pre}.experts.4.gate_proj.weight_scale_inv"] = torch.from_numpy(
+        (0.001 + 0.01 * rng.random((1, 2))).astype(np.float32))
+    t[f"{pre}.gate.weight"] = bf(rng.standard_normal((4, 100)) * 0.02)
+    t["model.layers.0.post_attention_layernorm.weight"] = bf(1.0 + 0.1 * rng.standard_normal(100))
+    return t
 
 
 if __name__ == "__main__":
