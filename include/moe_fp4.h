@@ -193,6 +193,19 @@ int mfi_attn_decode(const void* q, const uint8_t* kvk, const uint8_t* kvv, const
                     float* o, int M, int Hq, int Hkv, int D, int max_pos, const float* k_scale,
                     const float* v_scale, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The same for n_seq sequences at the same base position in one launch (no
+ * reference counterpart: the reference decodes one sequence per call):
+ * sequence s has q rows [s*M, (s+1)*M) of q (n_seq*M, Hq, D), its cache at
+ * kvk/kvv + s * kv_seq_stride bytes (kv_seq_stride >= max_pos*Hkv*D, a
+ * multiple of 4) and o rows [s*M, (s+1)*M). */
+size_t mfi_attn_decode_batched_workspace_bytes(int n_seq, int M, int Hq, int Hkv, int D,
+                                               int max_pos);
+int mfi_attn_decode_batched(const void* q, const uint8_t* kvk, const uint8_t* kvv,
+                            long long kv_seq_stride, const int32_t* dpos, float* o, int n_seq,
+                            int M, int Hq, int Hkv, int D, int max_pos, const float* k_scale,
+                            const float* v_scale, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
 /* ------------------------------------------------------------------------
  * Fused device-routed MoE layer (no reference counterpart as a single call:
  * it fulfils the reference's unimplemented K1/K2/K3 stubs

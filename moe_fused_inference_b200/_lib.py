@@ -42,6 +42,9 @@ SIGNATURES = {
     "mfi_attn_decode_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
     "mfi_attn_decode": (_I, [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _VP, _VP, _VP, _SZ,
                              _VP]),
+    "mfi_attn_decode_batched_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I, _I]),
+    "mfi_attn_decode_batched": (_I, [_VP, _VP, _VP, _LL, _VP, _VP, _I, _I, _I, _I, _I, _I, _VP,
+                                     _VP, _VP, _SZ, _VP]),
     "mfi_moe_prepared_bytes": (_SZ, [_I, _I, _I]),
     "mfi_moe_prepare": (_I, [_VP, _VP, _SZ, _VP]),
     "mfi_moe_layer_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),

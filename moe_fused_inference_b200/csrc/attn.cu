@@ -167,7 +167,20 @@ struct AttnArgs {
   float* o;                 // (M, Hq, D)
   int M, Hq, Hkv, max_pos, nsplit, chunk;
   float inv_sqrt_d;
+  long long kv_seq_stride;  // bytes between consecutive sequences' caches
 };
+
+// The arguments of sequence `seq` of a batched call: sequence s owns rows
+// [s*M, (s+1)*M) of q, o and the partials, and the cache at s*kv_seq_stride.
+__device__ __forceinline__ AttnArgs for_sequence(AttnArgs a, int seq) {
+  const size_t rows = size_t(seq) * a.M * a.Hq;
+  a.q += rows * kD;
+  a.o += rows * kD;
+  a.part += rows * size_t(a.nsplit) * kPartStride;
+  a.kvk += size_t(seq) * a.kv_seq_stride;
+  a.kvv += size_t(seq) * a.kv_seq_stride;
+  return a;
+}
 
 // dynamic shared memory: decode table, K tile (padded rows), V tile, queries
 constexpr size_t kSmemLut = 256 * sizeof(float);
@@ -176,7 +189,8 @@ constexpr size_t kSmemV = size_t(kTile) * kD * sizeof(float);
 constexpr size_t kSmemQ = size_t(kMaxGroup) * kRowsPerPass * kD * sizeof(float);
 constexpr size_t kAttnSmem = kSmemLut + kSmemK + kSmemV + kSmemQ;
 
-__global__ void __launch_bounds__(kThreads) attn_partial_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(kThreads) attn_partial_kernel(AttnArgs a_all) {
+  const AttnArgs a = for_sequence(a_all, blockIdx.z);
   extern __shared__ __align__(16) float smem_f[];
   float* lut = smem_f;
   float* s_k = lut + 256;
@@ -314,7 +328,8 @@ __global__ void __launch_bounds__(kThreads) attn_partial_kernel(AttnArgs a) {
 // One CTA of D threads per (row, head): o = sum_j acc_j e^(max_j - M) /
 // sum_j sum_j e^(max_j - M), M the largest split maximum.  A row whose base
 // position lies outside the cache has no live position and gets zeros.
-__global__ void __launch_bounds__(kD) attn_merge_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(kD) attn_merge_kernel(AttnArgs a_all) {
+  const AttnArgs a = for_sequence(a_all, blockIdx.z);
   const int m = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const float* pp = a.part + (size_t(m) * a.Hq + h) * a.nsplit * size_t(kPartStride);
   float gmax = -INFINITY;
@@ -334,8 +349,9 @@ __global__ void __launch_bounds__(kD) attn_merge_kernel(AttnArgs a) {
 
 // Split layout from max_pos: about two CTAs per SM over the KV heads, at
 // least one 32-position tile per split.
-void split_layout(int max_pos, int Hkv, int& nsplit, int& chunk) {
-  const int target = (2 * 148 + Hkv - 1) / Hkv;
+void split_layout(int max_pos, int Hkv, int n_seq, int& nsplit, int& chunk) {
+  const int per = Hkv * n_seq;  // CTAs per split
+  const int target = (2 * 148 + per - 1) / per;
   chunk = (max_pos + target - 1) / target;
   chunk = (chunk + kTile - 1) / kTile * kTile;
   if (chunk < kTile) chunk = kTile;
@@ -375,32 +391,45 @@ extern "C" int mfi_kv_write(const void* k, const void* v, uint8_t* kvk, uint8_t*
                           : mfi::set_last_error(MFI_ERR_CUDA, cudaGetErrorString(e));
 }
 
-extern "C" size_t mfi_attn_decode_workspace_bytes(int M, int Hq, int Hkv, int D, int max_pos) {
-  if (M <= 0 || Hq <= 0 || Hkv <= 0 || D <= 0 || max_pos <= 0) return 0;
+extern "C" size_t mfi_attn_decode_batched_workspace_bytes(int n_seq, int M, int Hq, int Hkv,
+                                                         int D, int max_pos) {
+  if (n_seq <= 0 || M <= 0 || Hq <= 0 || Hkv <= 0 || D <= 0 || max_pos <= 0) return 0;
   int nsplit, chunk;
-  mfi::split_layout(max_pos, Hkv, nsplit, chunk);
-  return size_t(M) * Hq * nsplit * mfi::kPartStride * sizeof(float);
+  mfi::split_layout(max_pos, Hkv, n_seq, nsplit, chunk);
+  return size_t(n_seq) * M * Hq * nsplit * mfi::kPartStride * sizeof(float);
 }
 
-extern "C" int mfi_attn_decode(const void* q, const uint8_t* kvk, const uint8_t* kvv,
-                               const int32_t* dpos, float* o, int M, int Hq, int Hkv, int D,
-                               int max_pos, const float* k_scale, const float* v_scale,
-                               void* workspace, size_t workspace_bytes, void* stream) {
+extern "C" size_t mfi_attn_decode_workspace_bytes(int M, int Hq, int Hkv, int D, int max_pos) {
+  return mfi_attn_decode_batched_workspace_bytes(1, M, Hq, Hkv, D, max_pos);
+}
+
+extern "C" int mfi_attn_decode_batched(const void* q, const uint8_t* kvk, const uint8_t* kvv,
+                                       long long kv_seq_stride, const int32_t* dpos, float* o,
+                                       int n_seq, int M, int Hq, int Hkv, int D, int max_pos,
+                                       const float* k_scale, const float* v_scale,
+                                       void* workspace, size_t workspace_bytes, void* stream) {
   int rc = mfi::check_shapes(M, Hq, Hkv, D, max_pos);
   if (rc != MFI_OK) return rc;
+  if (n_seq <= 0 || n_seq > 65535) return mfi::set_last_error(MFI_ERR_ARG, "n_seq must be in [1, 65535]");
   if (!q || !kvk || !kvv || !dpos || !o || !workspace)
     return mfi::set_last_error(MFI_ERR_ARG, "null pointer");
   if ((k_scale == nullptr) != (v_scale == nullptr))
     return mfi::set_last_error(MFI_ERR_ARG, "attn_decode: give both scales or neither");
   if ((reinterpret_cast<uintptr_t>(kvk) & 3) || (reinterpret_cast<uintptr_t>(kvv) & 3) ||
-      (reinterpret_cast<uintptr_t>(o) & 15) || (reinterpret_cast<uintptr_t>(workspace) & 15))
-    return mfi::set_last_error(MFI_ERR_ARG, "attn_decode: kvk, kvv 4-byte, o and workspace 16-byte aligned");
-  if (workspace_bytes < mfi_attn_decode_workspace_bytes(M, Hq, Hkv, D, max_pos))
-    return mfi::set_last_error(MFI_ERR_WORKSPACE, "workspace smaller than mfi_attn_decode_workspace_bytes()");
+      (kv_seq_stride & 3) || (reinterpret_cast<uintptr_t>(o) & 15) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 15))
+    return mfi::set_last_error(MFI_ERR_ARG,
+                               "attn_decode: kvk, kvv and the sequence stride 4-byte, o and the "
+                               "workspace 16-byte aligned");
+  if (n_seq > 1 && kv_seq_stride < (long long)max_pos * Hkv * D)
+    return mfi::set_last_error(MFI_ERR_ARG, "attn_decode: sequence caches overlap");
+  if (workspace_bytes < mfi_attn_decode_batched_workspace_bytes(n_seq, M, Hq, Hkv, D, max_pos))
+    return mfi::set_last_error(MFI_ERR_WORKSPACE, "workspace smaller than the attn_decode workspace query");
   mfi::AttnArgs a{};
   a.q = reinterpret_cast<const __nv_bfloat16*>(q);
   a.kvk = kvk;
   a.kvv = kvv;
+  a.kv_seq_stride = kv_seq_stride;
   a.dpos = dpos;
   a.k_scale = k_scale;
   a.v_scale = v_scale;
@@ -410,18 +439,26 @@ extern "C" int mfi_attn_decode(const void* q, const uint8_t* kvk, const uint8_t*
   a.Hq = Hq;
   a.Hkv = Hkv;
   a.max_pos = max_pos;
-  mfi::split_layout(max_pos, Hkv, a.nsplit, a.chunk);
+  mfi::split_layout(max_pos, Hkv, n_seq, a.nsplit, a.chunk);
   a.inv_sqrt_d = 1.0f / sqrtf(float(D));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   cudaError_t e = mfi::ensure_dynamic_smem(reinterpret_cast<const void*>(mfi::attn_partial_kernel),
                                            mfi::kAttnSmem);
   if (e != cudaSuccess) return mfi::set_last_error(MFI_ERR_CUDA, cudaGetErrorString(e));
-  mfi::attn_partial_kernel<<<dim3(a.nsplit, Hkv), mfi::kThreads, mfi::kAttnSmem, st>>>(a);
+  mfi::attn_partial_kernel<<<dim3(a.nsplit, Hkv, n_seq), mfi::kThreads, mfi::kAttnSmem, st>>>(a);
   e = cudaGetLastError();
   if (e == cudaSuccess) {
-    mfi::attn_merge_kernel<<<dim3(M, Hq), mfi::kD, 0, st>>>(a);
+    mfi::attn_merge_kernel<<<dim3(M, Hq, n_seq), mfi::kD, 0, st>>>(a);
     e = cudaGetLastError();
   }
   return e == cudaSuccess ? MFI_OK
                           : mfi::set_last_error(MFI_ERR_CUDA, cudaGetErrorString(e));
+}
+
+extern "C" int mfi_attn_decode(const void* q, const uint8_t* kvk, const uint8_t* kvv,
+                               const int32_t* dpos, float* o, int M, int Hq, int Hkv, int D,
+                               int max_pos, const float* k_scale, const float* v_scale,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  return mfi_attn_decode_batched(q, kvk, kvv, 0, dpos, o, 1, M, Hq, Hkv, D, max_pos, k_scale,
+                                 v_scale, workspace, workspace_bytes, stream);
 }
