@@ -185,6 +185,28 @@ int mfi_device_error(int clear) {
 }
 
 // ---------------------------------------------------------------------------
+namespace {
+// The grouped GEMM of the drop-in operators over the grouped pointer tables:
+// the tcgen05 kernel when K tiles by 256 and the activations are aligned for
+// 16-byte copies (every Qwen3-MoE expert shape), else the CUDA-core GEMV.
+int grouped_launch(const mfi::GroupDesc* groups, const int* ng, int P,
+                   const mfi::EntryDesc* entries, const uint8_t* xq, const uint8_t* xsc, float* y,
+                   int N, int Kp, cudaStream_t s, const char* what) {
+  const std::string w = std::string(what) + " grouped GEMM launch";
+  if (mfi::grouped_tc_supported(N, Kp) && (reinterpret_cast<uintptr_t>(xq) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(xsc) & 7) == 0) {
+    const long long items = (long long)P * ((N + 127) / 128);
+    return cuda_status(mfi::launch_grouped_tc(groups, ng, items > (1 << 30) ? (1 << 30) : int(items),
+                                              entries, xq, xsc, y, N, Kp,
+                                              mfi::device_error_flag(), s),
+                       w.c_str());
+  }
+  return cuda_status(mfi::launch_grouped_gemv(groups, ng, P, entries, xq, xsc, y, N, Kp,
+                                              kGemvMaxCtas, s),
+                     w.c_str());
+}
+}  // namespace
+
 size_t mfi_moe_gateup_workspace_bytes(int E, int M) {
   const size_t P = size_t(2) * E * M;
   Carve c(nullptr);
@@ -216,9 +238,7 @@ int mfi_moe_gateup(const uint8_t* xq, const uint8_t* xsc, const uint8_t* const* 
                                                 entries, s),
                        "moe_gateup grouping launch");
   if (st != MFI_OK) return st;
-  return cuda_status(mfi::launch_grouped_gemv(groups, ng, int(P), entries, xq, xsc, gu, N, Kp,
-                                              kGemvMaxCtas, s),
-                     "moe_gateup gemv launch");
+  return grouped_launch(groups, ng, int(P), entries, xq, xsc, gu, N, Kp, s, "moe_gateup");
 }
 
 size_t mfi_moe_down_workspace_bytes(int E, int M, int K) {
@@ -259,9 +279,7 @@ int mfi_moe_down(const float* gu, const uint8_t* const* wp_tab, const uint8_t* c
                                             s),
                    "moe_down grouping launch");
   if (st != MFI_OK) return st;
-  return cuda_status(mfi::launch_grouped_gemv(groups, ng, int(P), entries, hq, hsc, yd, N, Kp,
-                                              kGemvMaxCtas, s),
-                     "moe_down gemv launch");
+  return grouped_launch(groups, ng, int(P), entries, hq, hsc, yd, N, Kp, s, "moe_down");
 }
 
 int mfi_moe_combine(const float* yd, int ystride, const float* w, int E, float* out, int M, int N,

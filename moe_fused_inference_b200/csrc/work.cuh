@@ -144,6 +144,13 @@ cudaError_t launch_grouped_gemv(const GroupDesc* groups, const int* n_groups_dev
 cudaError_t launch_dense_gemv(const uint8_t* xq, const uint8_t* xsc, const uint8_t* wp,
                               const uint8_t* wsc, float* y, long long ldy, int M, int N, int Kp,
                               cudaStream_t stream);
+// The grouped tensor-core form of launch_grouped_gemv (grouped_tc.cu): Kp a
+// multiple of 256, xq rows 16-byte and xsc rows 8-byte aligned; max_items
+// bounds (groups' 32-row chunks) x (128-row tiles) for the grid size.
+bool grouped_tc_supported(int N, int Kp);
+cudaError_t launch_grouped_tc(const GroupDesc* groups, const int* n_groups, int max_items,
+                              const EntryDesc* entries, const uint8_t* xq, const uint8_t* xsc,
+                              float* y, int N, int Kp, int* err, cudaStream_t stream);
 cudaError_t launch_build_groups(const uint8_t* const* wp_tab, const uint8_t* const* wsc_tab, int P,
                                 int mode, int E, int N, GroupDesc* groups, int* n_groups,
                                 EntryDesc* entries, cudaStream_t stream);

@@ -198,10 +198,11 @@ class Runner:
         self.kvk = torch.zeros(shape, dtype=torch.uint8, device=dev)
         self.kvv = torch.zeros(shape, dtype=torch.uint8, device=dev)
 
-    def forward(self, ids: torch.Tensor, base: int, last_only: bool = False):
+    def forward(self, ids: torch.Tensor, base: int, last_only: bool = False, trace=None):
         """ids (B, M) at positions base .. base + M - 1 of every sequence;
         returns fp32 logits (B, M, V) (or (B, V) of the last row) and the
-        top-k expert ids of every layer."""
+        top-k expert ids of every layer.  ``trace`` (a list) receives the
+        residual stream after every layer's attention and MoE block."""
         cfg, be, m = self.model.cfg, self.be, self.model
         B, M = ids.shape
         T = B * M
@@ -228,10 +229,14 @@ class Runner:
             of = o.reshape(T, Hq * D).to(torch.bfloat16).contiguous()
             aq, asc = be.prequant(of)
             x = x + be.linear(aq, asc, lw.o, T, H, Hq * D).bfloat16()
+            if trace is not None:
+                trace.append(("attn", L, x.clone()))
             h2 = rms_norm(x, lw.post_norm, cfg.eps)
             moe, topi = be.moe_block(L, h2)
             x = x + moe.bfloat16()
             routing.append(topi)
+            if trace is not None:
+                trace.append(("moe", L, x.clone()))
         if last_only:
             x = x.view(B, M, H)[:, -1]
         xn = rms_norm(x, m.final_norm, cfg.eps)
