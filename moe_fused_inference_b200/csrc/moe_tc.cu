@@ -249,11 +249,30 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         int chunk, tile;
         decode(item, gu, chunk, tile);
         const ChunkDesc cd = chunk_desc(chunk);
+        const int ksn = gu ? ks_gu : ks_dn;
         const uint8_t* wb;
+        // a down item's weight blocks do not depend on the h rows it waits
+        // for: the first ring-full of them goes out before the wait, so their
+        // latency overlaps it (each stage's barrier completes once the h rows
+        // of the stage have landed too)
+        const int pre = gu ? 0 : min(ksn, kStages);
+        int pre_issued = 0;
         if (gu) {
           wb = p.w_gu + (size_t(cd.expert) * tiles_gu + tile) * ks_gu * size_t(kWBlock);
         } else {
           wb = p.w_dn + (size_t(cd.expert) * tiles_dn + tile) * ks_dn * size_t(kWBlock);
+          for (; pre_issued < pre; ++pre_issued) {
+            const uint32_t j = it + uint32_t(pre_issued);
+            const int s = int(j % kStages);
+            if (!mbar_wait(&empty[s], ((j / kStages) & 1) ^ 1, p.err, 1)) { ok = false; break; }
+            mbar_expect_tx(&full[s], kStageBytes);
+            bulk_load_stream(ring + s * kStageBytes, wb + size_t(pre_issued) * kWBlock, kWBlock,
+                             &full[s]);
+          }
+          if (!ok) {
+            it += uint32_t(pre_issued);  // the drain covers the copies already issued
+            break;
+          }
           // the chunk's h rows: published by its tiles_gu gate/up items
           if (ld_acquire_u32(p.ready + chunk) < unsigned(tiles_gu)) {
             const uint64_t t0 = globaltimer_ns();
@@ -269,20 +288,24 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 }
               }
             }
-            if (!ok) break;
+            if (!ok) {
+              it += uint32_t(pre_issued);
+              break;
+            }
           }
           fence_proxy_async_global();
         }
-        const int ksn = gu ? ks_gu : ks_dn;
         const int kc = gu ? kc_gu : kc_dn;
         const uint8_t* sfb = gu ? p.sfb_x : p.hp_atoms;
         const CUtensorMap* tb = gu ? &tma_x : &tma_h;
         for (int ks = 0; ks < ksn; ++ks, ++it) {
           const int s = it % kStages;
-          if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, p.err, 1)) { ok = false; break; }
           uint8_t* st = ring + s * kStageBytes;
-          mbar_expect_tx(&full[s], kStageBytes);
-          bulk_load_stream(st, wb + size_t(ks) * kWBlock, kWBlock, &full[s]);
+          if (ks >= pre_issued) {
+            if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, p.err, 1)) { ok = false; break; }
+            mbar_expect_tx(&full[s], kStageBytes);
+            bulk_load_stream(st, wb + size_t(ks) * kWBlock, kWBlock, &full[s]);
+          }
           tma_load_2d(st + kOffB, tb, ks * 128, cd.row0, &full[s]);
           bulk_load(st + kOffSFB, sfb + (size_t(cd.row0 / kChunk) * kc + 2 * ks) * 512, kSF,
                     &full[s]);
