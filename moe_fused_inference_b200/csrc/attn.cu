@@ -328,21 +328,39 @@ __global__ void __launch_bounds__(kThreads) attn_partial_kernel(AttnArgs a_all) 
 // One CTA of D threads per (row, head): o = sum_j acc_j e^(max_j - M) /
 // sum_j sum_j e^(max_j - M), M the largest split maximum.  A row whose base
 // position lies outside the cache has no live position and gets zeros.
+constexpr int kMaxSplits = 1024;
+
 __global__ void __launch_bounds__(kD) attn_merge_kernel(AttnArgs a_all) {
   const AttnArgs a = for_sequence(a_all, blockIdx.z);
   const int m = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const float* pp = a.part + (size_t(m) * a.Hq + h) * a.nsplit * size_t(kPartStride);
-  float gmax = -INFINITY;
-  for (int j = 0; j < a.nsplit; ++j) gmax = fmaxf(gmax, pp[j * kPartStride + kD]);
+  // every split's (max, sum) staged in shared memory by the whole block, the
+  // largest maximum by a block reduction, then each split's weight
+  // e^(max_j - M); the accumulators are read with independent loads
+  __shared__ float s_c[kMaxSplits], s_den[kMaxSplits];
+  __shared__ float s_red[kD / 32];
+  float lmax = -INFINITY;
+  for (int j = d; j < a.nsplit; j += kD) {
+    s_c[j] = pp[j * kPartStride + kD];
+    s_den[j] = pp[j * kPartStride + kD + 1];
+    lmax = fmaxf(lmax, s_c[j]);
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, off));
+  if ((d & 31) == 0) s_red[d >> 5] = lmax;
+  __syncthreads();
+  float gmax = s_red[0];
+#pragma unroll
+  for (int w = 1; w < kD / 32; ++w) gmax = fmaxf(gmax, s_red[w]);
+  for (int j = d; j < a.nsplit; j += kD)
+    s_c[j] = (gmax == -INFINITY || s_c[j] == -INFINITY) ? 0.0f : expf(s_c[j] - gmax);
+  __syncthreads();
   float num = 0.0f, den = 0.0f;
-  if (gmax != -INFINITY) {
-    for (int j = 0; j < a.nsplit; ++j) {
-      const float mj = pp[j * kPartStride + kD];
-      if (mj == -INFINITY) continue;
-      const float c = expf(mj - gmax);
-      num = fmaf(pp[j * kPartStride + d], c, num);
-      den = fmaf(pp[j * kPartStride + kD + 1], c, den);
-    }
+#pragma unroll 8
+  for (int j = 0; j < a.nsplit; ++j) {
+    const float c = s_c[j];
+    num = fmaf(pp[j * kPartStride + d], c, num);
+    den = fmaf(s_den[j], c, den);
   }
   a.o[(size_t(m) * a.Hq + h) * kD + d] = den > 0.0f ? num / den : 0.0f;
 }

@@ -71,6 +71,10 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
                : "memory");
 }
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
+               : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
@@ -137,12 +141,20 @@ __global__ void __launch_bounds__(kGtThreads, 1) grouped_tc_kernel(GtArgs p) {
 
   if (warp < 4) {
     // ---- producers ------------------------------------------------------------
+    // Every copy of a stage — weight and activation rows, both operands' E8M0
+    // codes — is a cp.async, so no producer ever waits on a global load
+    // inside the loop; an item's descriptors are loaded one item ahead.
     const int t = threadIdx.x;  // 0..127: weight row t of the tile for the codes
-    uint32_t it = 0, arrived = 0;
-    bool ok = true;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+    const int j0 = t >> 3, j1 = 16 + (t >> 3);  // this thread's activation rows
+    struct ItemDesc {
+      const uint8_t* wp;
+      const uint8_t* wsc;
+      int tile, n_live, ar0, ar1, ar_sf;
+    };
+    auto load_item = [&](int item) {
+      ItemDesc d;
       const int cv = s_chunk[item / n_tiles];
-      const int tile = item % n_tiles;
+      d.tile = item % n_tiles;
       const GroupDesc gd = p.groups[cv >> 8];
       const int c0 = (cv & 255) * kGtTok;
       const int cnt = min(kGtTok, gd.count - c0);
@@ -151,14 +163,28 @@ __global__ void __launch_bounds__(kGtThreads, 1) grouped_tc_kernel(GtArgs p) {
       // 10) and read as zeros instead of faulting
       const bool w_ok = ((reinterpret_cast<uintptr_t>(gd.wp) & 15) == 0) &&
                         ((reinterpret_cast<uintptr_t>(gd.wsc) & 7) == 0);
-      if (!w_ok && t == 0 && tile == 0) atomicCAS(p.err, 0, 10);
-      const int n_live = w_ok ? p.N : 0;
-      // activation row of this thread's B rows (rows t / 8 and 16 + t / 8)
-      const int j0 = t >> 3, j1 = 16 + (t >> 3);
-      const int ar0 = j0 < cnt ? p.entries[gd.first + c0 + j0].act_row : -1;
-      const int ar1 = j1 < cnt ? p.entries[gd.first + c0 + j1].act_row : -1;
-      const int ar_sf = t < cnt ? p.entries[gd.first + c0 + t].act_row : -1;
-      const int wrow = tile * kGtRows + t;
+      if (!w_ok && t == 0 && d.tile == 0) atomicCAS(p.err, 0, 10);
+      d.wp = gd.wp;
+      d.wsc = gd.wsc;
+      d.n_live = w_ok ? p.N : 0;
+      d.ar0 = j0 < cnt ? p.entries[gd.first + c0 + j0].act_row : -1;
+      d.ar1 = j1 < cnt ? p.entries[gd.first + c0 + j1].act_row : -1;
+      d.ar_sf = t < cnt ? p.entries[gd.first + c0 + t].act_row : -1;
+      return d;
+    };
+    // the activation atoms' unused words (words 1-3 of each row line) stay zero
+    for (int s = 0; s < kGtStages; ++s) {
+      uint4* sfb = reinterpret_cast<uint4*>(ring + size_t(s) * kGtStage + kGtOffSFB);
+      if (t < 64) sfb[t] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    uint32_t it = 0, arrived = 0;
+    bool ok = true;
+    ItemDesc cur{};
+    if (int(blockIdx.x) < n_items) cur = load_item(blockIdx.x);
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      const ItemDesc d = cur;
+      if (item + int(gridDim.x) < n_items) cur = load_item(item + gridDim.x);
+      const int wrow = d.tile * kGtRows + t;
       for (int ks = 0; ks < nks; ++ks, ++it) {
         const int s = int(it % kGtStages);
         if (!mbar_wait(&empty[s], ((it / kGtStages) & 1) ^ 1, p.err, 1)) { ok = false; break; }
@@ -168,41 +194,39 @@ __global__ void __launch_bounds__(kGtThreads, 1) grouped_tc_kernel(GtArgs p) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int r = (t >> 3) + 16 * i, c = t & 7;
-          const int n = tile * kGtRows + r;
-          const bool live = n < n_live;
+          const int n = d.tile * kGtRows + r;
+          const bool live = n < d.n_live;
           // a dead row is zero-filled; its source address (not read) is the
           // host-checked, 16-byte aligned activation base
-          const uint8_t* src = live ? gd.wp + size_t(n) * (p.Kp / 2) + ks * 128 + c * 16 : p.xq;
+          const uint8_t* src = live ? d.wp + size_t(n) * (p.Kp / 2) + ks * 128 + c * 16 : p.xq;
           cp_async16(sa + r * 128 + ((c ^ (r & 7)) << 4), src, live ? 16u : 0u);
         }
         // B: 32 rows x 8 chunks; thread t copies chunk (t % 8) of rows t/8, 16 + t/8
         {
           const int c = t & 7;
-          const uint8_t* s0 = p.xq + (ar0 >= 0 ? size_t(ar0) * (p.Kp / 2) + ks * 128 + c * 16 : 0);
-          const uint8_t* s1 = p.xq + (ar1 >= 0 ? size_t(ar1) * (p.Kp / 2) + ks * 128 + c * 16 : 0);
-          cp_async16(sb + j0 * 128 + ((c ^ (j0 & 7)) << 4), s0, ar0 >= 0 ? 16u : 0u);
-          cp_async16(sb + j1 * 128 + ((c ^ (j1 & 7)) << 4), s1, ar1 >= 0 ? 16u : 0u);
+          const uint8_t* s0 = p.xq + (d.ar0 >= 0 ? size_t(d.ar0) * (p.Kp / 2) + ks * 128 + c * 16 : 0);
+          const uint8_t* s1 = p.xq + (d.ar1 >= 0 ? size_t(d.ar1) * (p.Kp / 2) + ks * 128 + c * 16 : 0);
+          cp_async16(sb + j0 * 128 + ((c ^ (j0 & 7)) << 4), s0, d.ar0 >= 0 ? 16u : 0u);
+          cp_async16(sb + j1 * 128 + ((c ^ (j1 & 7)) << 4), s1, d.ar1 >= 0 ? 16u : 0u);
         }
-        cp_async_commit();
-        // scale atoms (generic stores, fenced below with the copies): weight
-        // row t -> byte (t%32)*16 + (t/32)*4 + k%4 of atom k/4; activation
-        // row t < 32 -> word 4t of each atom (the other words zero)
+        // scale atoms: weight row t -> byte (t%32)*16 + (t/32)*4 + k%4 of atom
+        // k/4; activation row t < 32 -> word 4t of each atom.  Dead rows get
+        // code 0 (their operand bytes are zero, so the product is zero).
         {
-          uint2 wcodes = make_uint2(0x7F7F7F7Fu, 0x7F7F7F7Fu);
-          if (wrow < n_live)
-            wcodes = *reinterpret_cast<const uint2*>(gd.wsc + size_t(wrow) * nb + ks * 8);
-          uint32_t* sfa = reinterpret_cast<uint32_t*>(st + kGtOffSFA);
-          const int w = ((t & 31) * 16 + (t >> 5) * 4) >> 2;
-          sfa[w] = wcodes.x;
-          sfa[128 + w] = wcodes.y;
+          const uint32_t sfa = smem_u32(st + kGtOffSFA) + (t & 31) * 16 + (t >> 5) * 4;
+          const bool wl = wrow < d.n_live;
+          const uint8_t* wsrc = wl ? d.wsc + size_t(wrow) * nb + ks * 8 : p.xsc;
+          cp_async4(sfa, wsrc, wl ? 4u : 0u);
+          cp_async4(sfa + 512, wsrc + (wl ? 4 : 0), wl ? 4u : 0u);
           if (t < 32) {
-            uint2 xc = make_uint2(0x7F7F7F7Fu, 0x7F7F7F7Fu);
-            if (ar_sf >= 0) xc = *reinterpret_cast<const uint2*>(p.xsc + size_t(ar_sf) * nb + ks * 8);
-            uint4* sfb = reinterpret_cast<uint4*>(st + kGtOffSFB);
-            sfb[t] = make_uint4(xc.x, 0u, 0u, 0u);
-            sfb[32 + t] = make_uint4(xc.y, 0u, 0u, 0u);
+            const uint32_t sfb = smem_u32(st + kGtOffSFB) + t * 16;
+            const bool xl = d.ar_sf >= 0;
+            const uint8_t* xsrc = xl ? p.xsc + size_t(d.ar_sf) * nb + ks * 8 : p.xsc;
+            cp_async4(sfb, xsrc, xl ? 4u : 0u);
+            cp_async4(sfb + 512, xsrc + (xl ? 4 : 0), xl ? 4u : 0u);
           }
         }
+        cp_async_commit();
         if (it >= uint32_t(kGtLag)) {
           cp_async_wait<kGtLag>();
           fence_proxy_async_smem();

@@ -269,6 +269,23 @@ class Runner:
             pos += 1
         return torch.stack(toks, 1), torch.stack(margins, 1)
 
+    def score(self, prompt: torch.Tensor, tokens: torch.Tensor, chunk: int = 64):
+        """Teacher-forced next-token predictions along a given continuation:
+        the prompt, then tokens (B, S) fed as history, in chunks of rows;
+        returns this backend's argmax (B, S) and top-2 margins (B, S) for each
+        position of `tokens` (prediction i sees the prompt and tokens[:, :i])."""
+        self.prefill(prompt, chunk)
+        P = prompt.shape[1] - 1
+        feed = torch.cat([prompt[:, -1:], tokens[:, :-1]], dim=1)
+        am, mg = [], []
+        for s in range(0, feed.shape[1], chunk):
+            logits, _ = self.forward(feed[:, s:s + chunk], P + s)
+            top2 = torch.topk(logits, 2, dim=-1).values
+            am.append(logits.argmax(-1))
+            mg.append(top2[..., 0] - top2[..., 1])
+            del logits
+        return torch.cat(am, 1), torch.cat(mg, 1)
+
     def speculative(self, prompt: torch.Tensor, steps: int, n_gram: int = 7, draft_len: int = 4):
         """Prompt-lookup speculative decoding of one sequence (B = 1), the
         reference's PromptLookup (runtime/spec_decoder.py:22-122): drafts are

@@ -75,27 +75,35 @@ def test_prompt_forward_agrees_layer_by_layer(model, backends):
 
 @pytest.mark.parametrize("batch", [1, 16, 64])
 def test_greedy_decode_against_reference_semantics(model, backends, batch):
+    """The library decodes greedily (128 one-row steps per sequence); the
+    torch arm then scores the same continuation teacher-forced (one batched
+    pass over prompt + generated tokens), so every step compares the two
+    arms' next-token choice on identical history.  Reported: the share of
+    steps where they agree and the first disagreement with both margins."""
     lib, ref = backends
     prompt = synthetic_prompts(batch, PROMPT, model.cfg.vocab, seed=batch)
     max_len = PROMPT + STEPS + 8
     ta, ma = Runner(model, lib, batch, max_len).greedy(prompt, STEPS)
-    tb, mb = Runner(model, ref, batch, max_len).greedy(prompt, STEPS)
     torch.cuda.synchronize()
     from moe_fused_inference_b200 import _lib
     assert _lib.load().mfi_device_error(1) == 0
     assert bool(((ta >= 0) & (ta < model.cfg.vocab)).all())
-    same = (ta == tb)
-    # per sequence: steps identical before the first difference
+    tb, mb = Runner(model, ref, batch, max_len).score(prompt, ta, chunk=128)
+    same = ta == tb
     first = [int((~same[s]).nonzero()[0]) if not bool(same[s].all()) else STEPS
              for s in range(batch)]
     s0 = min(range(batch), key=lambda s: first[s])
-    rep = {"batch": batch, "steps": STEPS, "sequences_identical": sum(f == STEPS for f in first),
-           "mean_identical_prefix": sum(first) / batch, "first_divergence_step": first[s0]}
+    rep = {"batch": batch, "steps": STEPS, "agreeing_steps": float(same.float().mean()),
+           "sequences_identical": sum(f == STEPS for f in first),
+           "first_disagreement_step": first[s0]}
     if first[s0] < STEPS:
         t = first[s0]
         rep.update({"sequence": s0, "library_token": int(ta[s0, t]), "torch_token": int(tb[s0, t]),
                     "library_top2_margin": float(ma[s0, t]), "torch_top2_margin": float(mb[s0, t])})
     print("config4 greedy " + json.dumps(rep))
+    # the arms mostly agree step by step; a disagreement is a near tie in
+    # one of them (a small top-2 margin), not a different computation
+    assert rep["agreeing_steps"] >= 0.5
 
 
 def test_speculative_decode_is_lossless(model, backends):

@@ -52,3 +52,6 @@ def test_runner_greedy_and_speculative_on_cpu():
     spec, forwards, accepted = r.speculative(prompt[:1], 12, n_gram=3)
     assert torch.equal(spec, toks[0])
     assert forwards <= 12
+    # teacher-forced scoring of the greedy continuation reproduces it
+    am, mg = Runner(m, be, 2, 128).score(prompt, toks, chunk=5)
+    assert torch.equal(am, toks) and mg.shape == toks.shape
