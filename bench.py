@@ -857,6 +857,71 @@ def run_ours(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def ep_prefill_point(args, world, rank, dev, T_total=16384, NL=2, steps=5, warmup=2):
+    """BASELINE config 5's prefill: T_total tokens split over the ranks
+    (T_total / world each), NL expert-parallel layers (128/N experts per GPU)
+    with Zipf(1.2)-skewed routing, NCCL all-to-all dispatch and return, the
+    prefill tcgen05 kernels on the received rows.  Device time max over
+    ranks; one extra step with events between the calls gives the stages."""
+    import torch.distributed as dist
+    from moe_fused_inference_b200.ep import EPMoELayer, random_shard
+    from moe_fused_inference_b200.synthetic import zipf_bias
+
+    Tr = T_total // world
+    bias = torch.from_numpy(zipf_bias(E, args.zipf_alpha, seed=3)).to(dev)
+    layers = [EPMoELayer(random_shard(E, world, rank, H, MI, 0.02, seed=200 + l, device=dev),
+                         TOPK, Tr, transport="nccl", logit_bias=bias) for l in range(NL)]
+    g = torch.Generator(device=dev).manual_seed(11 + rank)
+    X = torch.randn((NL, Tr, H), generator=g, device=dev).bfloat16()
+    out = torch.empty((NL, Tr, H), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for l in range(NL):
+            layers[l](X[l], out=out[l])
+
+    for _ in range(warmup):
+        step()
+    barrier(world)
+    ms = max_over_ranks(event_time(dev, stream, step, steps), world)
+    names = ["route_pack", "a2a_dispatch", "experts", "a2a_return", "unpack"]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(NL)]
+    barrier(world)
+    for l in range(NL):
+        L, ev = layers[l], evs[l]
+        ev[0].record(stream)
+        L.dispatch_prepare(X[l])
+        ev[1].record(stream)
+        dist.all_to_all_single(L.recv.view(-1), L.send.view(-1))
+        ev[2].record(stream)
+        L.compute()
+        ev[3].record(stream)
+        dist.all_to_all_single(L.ret_back.view(-1), L.ret.view(-1))
+        ev[4].record(stream)
+        L.finish(Tr, out[l])
+        ev[5].record(stream)
+    torch.cuda.synchronize(dev)
+    st = torch.tensor([sum(evs[l][i].elapsed_time(evs[l][i + 1]) for l in range(NL)) / NL * 1e3
+                       for i in range(5)], dtype=torch.float64, device=dev)
+    allst = [torch.zeros_like(st) for _ in range(world)]
+    dist.all_gather(allst, st)
+    load = torch.bincount(layers[0].topi[:Tr].flatten().long(), minlength=E).to(torch.float64)
+    dist.all_reduce(load)
+    for L in layers:
+        L.close()
+    del layers, X, out
+    torch.cuda.empty_cache()
+    us_layer = ms / steps / NL * 1e3
+    tflops = FLOP_TOKEN * T_total / (us_layer / 1e6) / 1e12
+    return {"tokens_total": T_total, "tokens_per_rank": Tr, "layers": NL, "steps": steps,
+            "us_per_layer": us_layer, "tokens_per_s": T_total / (us_layer / 1e6),
+            "tflops_all_gpus": tflops, "frac_of_nominal_fp4_per_gpu": tflops / world / 9000.0,
+            "stage_us_per_layer": {n: [float(v[i]) for v in allst] for i, n in enumerate(names)},
+            "expert_load_max_over_mean": float(load.max() / load.mean()),
+            "routing": f"Zipf(1.2) logit bias alpha={args.zipf_alpha}",
+            "transport": "NCCL all_to_all_single (fixed-capacity blocks)"}
+
+
 def run_ep(args, world, rank, local):
     """Expert-parallel step over the torchrun ranks (peer-memory exchange fused
     into the kernels, or NCCL all-to-all with --ep-transport nccl)."""
@@ -997,6 +1062,10 @@ def run_ep(args, world, rank, local):
     for L in layers:
         L.close()  # unmap the peers' memory before the process group goes away
     barrier(world)
+    del layers, X, out, Xd
+    torch.cuda.empty_cache()
+    ep_prefill = None if args.headline_only else ep_prefill_point(args, world, rank, dev)
+    barrier(world)
     if rank != 0:
         return
     worst = int(torch.argmin(allstats[:, 0]))
@@ -1040,6 +1109,8 @@ def run_ep(args, world, rank, local):
                 "d2h_bytes_per_step": int(Oh.numel() * Oh.element_size())},
         "clocks": clocks,
     }
+    if ep_prefill is not None:
+        line["ep_prefill"] = ep_prefill
     print(json.dumps(line), flush=True)
 
 

@@ -59,6 +59,16 @@ int mfi_version(void);
  * clear != 0 resets it.  Returns -1 if the flag cannot be read. */
 int mfi_device_error(int clear);
 
+/* Exhaustive self-check of the library's own fp32 arithmetic on the current
+ * device, over all 2^32 bit patterns: the SwiGLU quotient g / (1 + expf(-g))
+ * (computed by Markstein's division) against CUDA's correctly rounded
+ * division, and the E2M1 rounding of |x| read from its bits against the
+ * threshold definition (quant/fp4_format.py:24-46).  Asynchronous on
+ * `stream`; out (device, 4 words, 8-byte aligned) receives the mismatch
+ * counts of the two checks and the smallest mismatching bit pattern of each
+ * (all ones when there is none).  A few milliseconds on a B200. */
+int mfi_selftest_numerics(unsigned long long* out, void* stream);
+
 /* ------------------------------------------------------------------------
  * Quantisers
  * ------------------------------------------------------------------------ */
@@ -319,7 +329,11 @@ int mfi_moe_route(const mfi_moe_weights* w, const void* x_bf16, int T, uint8_t* 
  * -1; an id must not repeat within a row (the device error flag then reads 5;
  * an id >= n_experts reads 4 and is skipped).  Needs hidden and inter to be
  * multiples of 256 and `w->prepared`; router fields are not read.
- * R * top_k <= 16384.  Rows whose slots are all -1 get zeros. */
+ * R * top_k <= 262144.  Up to 16384 pairs the decode kernels run (fp32 rows
+ * of y); beyond, the prefill kernels of mfi_moe_layer (128-row expert tiles,
+ * each expert's output row rounded to bf16 before the combine, as the
+ * reference's prefill does, runtime/model_runner_v2.py:119) — the expert-
+ * parallel prefill.  Rows whose slots are all -1 get zeros. */
 size_t mfi_moe_experts_workspace_bytes(int R, int hidden, int inter, int n_experts, int top_k);
 int mfi_moe_experts(const mfi_moe_weights* w, const uint8_t* xq, long long xq_ld,
                     const uint8_t* xsc, long long xsc_ld, const int32_t* sel, long long sel_ld,

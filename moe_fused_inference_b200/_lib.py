@@ -28,6 +28,7 @@ SIGNATURES = {
     "mfi_prequant": (_I, [_VP, _VP, _VP, _I, _I, _I, _VP]),
     "mfi_quantize_rows": (_I, [_VP, _I, _LL, _I, _VP, _VP, _I, _I, _I, _VP]),
     "mfi_device_error": (_I, [_I]),
+    "mfi_selftest_numerics": (_I, [_VP, _VP]),
     "mfi_lin_pq_workspace_bytes": (_SZ, [_I, _I, _I]),
     "mfi_lin_pq": (_I, [_VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP, _SZ, _VP]),
     "mfi_linear_workspace_bytes": (_SZ, [_I, _I, _I]),

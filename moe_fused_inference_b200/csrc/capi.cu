@@ -478,7 +478,8 @@ int run_prefill(const mfi_moe_weights* w, const void* x_bf16, int T, float* out,
   rc = cuda_status(mfi::launch_route(ra, st), "moe_layer prefill route launch");
   if (rc == MFI_OK) rc = rec(1);
   if (rc != MFI_OK) return rc;
-  rc = cuda_status(mfi::launch_prefill_scatter(s.xq, s.xsc, topi, s.slot_pos, s.counts, T, E, k, H,
+  rc = cuda_status(mfi::launch_prefill_scatter(s.xq, H / 2, s.xsc, H / 32, topi, k, s.slot_pos,
+                                               s.counts, T, E, k, H,
                                                s.perm, s.xp, s.xa, st),
                    "moe_layer prefill scatter launch");
   if (rc == MFI_OK) rc = rec(2);
@@ -779,10 +780,55 @@ ExpertScratch carve_experts(void* ws, int R, int H, int Mi, int E, int k) {
   s.bytes = c.used + 256;
   return s;
 }
+
+// Pre-routed rows whose pairs exceed the decode kernel's 16384 go through the
+// prefill kernel (per-expert regions of 128-row tiles, bf16 rows of y).
+constexpr long long kExpertsDecodeMaxPairs = 16384;
+
+struct ExpertPrefillScratch {
+  int* counts;          // [E] rows per expert
+  int* queue;           // work-item counter
+  unsigned* gu_done;    // finished gate/up items
+  unsigned* ready;      // [max tiles]
+  size_t zero_words;
+  int* slot_pos;        // [R*k]
+  int* perm;
+  uint8_t* xp; uint8_t* xa; uint8_t* hp; uint8_t* ha;
+  __nv_bfloat16* yd;    // (R*k, H)
+  int rows;
+  size_t bytes;
+};
+
+ExpertPrefillScratch carve_experts_prefill(void* ws, int R, int H, int Mi, int E, int k) {
+  Carve c(ws);
+  ExpertPrefillScratch s;
+  const long long P = (long long)R * k;
+  const size_t max_tiles = size_t(E) + size_t(P) / 128 + 1;
+  s.zero_words = size_t(E) + 2 + max_tiles;
+  s.counts = c.take<int>(s.zero_words);
+  s.queue = s.counts + E;
+  s.gu_done = reinterpret_cast<unsigned*>(s.counts + E + 1);
+  s.ready = reinterpret_cast<unsigned*>(s.counts + E + 2);
+  s.slot_pos = c.take<int>(size_t(P));
+  s.rows = int(mfi::prefill_rows(int(P), E));
+  s.perm = c.take<int>(size_t(s.rows));
+  s.xp = c.take<uint8_t>(size_t(s.rows) * (H / 2));
+  s.xa = c.take<uint8_t>(size_t(s.rows) / 128 * (H / 128) * 512);
+  s.hp = c.take<uint8_t>(size_t(s.rows) * (Mi / 2));
+  s.ha = c.take<uint8_t>(size_t(s.rows) / 128 * (Mi / 128) * 512);
+  s.yd = c.take<__nv_bfloat16>(size_t(P) * H);
+  s.bytes = c.used + 256;
+  return s;
+}
+
+bool experts_use_prefill(int R, int k) { return (long long)R * k > kExpertsDecodeMaxPairs; }
 }  // namespace
 
 size_t mfi_moe_experts_workspace_bytes(int R, int hidden, int inter, int n_experts, int top_k) {
   if (R < 0 || hidden <= 0 || inter <= 0 || n_experts <= 0 || top_k <= 0) return 0;
+  if ((long long)R * top_k > mfi::kPrefillMaxPairs) return 0;
+  if (experts_use_prefill(R, top_k))
+    return carve_experts_prefill(nullptr, R, hidden, inter, n_experts, top_k).bytes;
   return carve_experts(nullptr, R, hidden, inter, n_experts, top_k).bytes;
 }
 
@@ -796,7 +842,8 @@ int mfi_moe_experts(const mfi_moe_weights* w, const uint8_t* xq, long long xq_ld
   if (!layer_uses_tc(H, Mi))
     return fail(MFI_ERR_ARG, "moe_experts needs hidden and inter to be multiples of 256");
   if (k <= 0 || k > 32) return fail(MFI_ERR_ARG, "top_k must be in [1, 32]");
-  if (R < 0 || (long long)R * k > 16384) return fail(MFI_ERR_ARG, "rows * top_k must be <= 16384");
+  if (R < 0 || (long long)R * k > mfi::kPrefillMaxPairs)
+    return fail(MFI_ERR_ARG, "rows * top_k must be <= 262144");
   if (R == 0) return MFI_OK;
   if (bad_ptr(xq) || bad_ptr(xsc) || bad_ptr(sel) || bad_ptr(selw) || bad_ptr(out) ||
       bad_ptr(workspace) || bad_ptr(w->prepared))
@@ -810,8 +857,42 @@ int mfi_moe_experts(const mfi_moe_weights* w, const uint8_t* xq, long long xq_ld
                 "xq and out rows must be 16-byte aligned, xsc rows 4-byte aligned");
   if (workspace_bytes < mfi_moe_experts_workspace_bytes(R, H, Mi, E, k))
     return fail(MFI_ERR_WORKSPACE, "workspace too small for moe_experts");
-  ExpertScratch s = carve_experts(workspace, R, H, Mi, E, k);
   cudaStream_t st = as_stream(stream);
+  if (experts_use_prefill(R, k)) {
+    // many rows (expert-parallel prefill): count the pairs per local expert,
+    // place the rows in 128-row tiles, the prefill tcgen05 kernel, then the
+    // masked combine of the bf16 rows
+    if (H % 8 != 0) return fail(MFI_ERR_ARG, "hidden must be a multiple of 8");
+    ExpertPrefillScratch s = carve_experts_prefill(workspace, R, H, Mi, E, k);
+    int rc = cuda_status(cudaMemsetAsync(s.counts, 0, sizeof(int) * s.zero_words, st),
+                         "moe_experts memset");
+    if (rc != MFI_OK) return rc;
+    rc = cuda_status(mfi::launch_prefill_count_sel(sel, sel_ld, R, k, E, s.counts, s.slot_pos,
+                                                   mfi::device_error_flag(), st),
+                     "moe_experts count launch");
+    if (rc != MFI_OK) return rc;
+    rc = cuda_status(mfi::launch_prefill_scatter(xq, xq_ld, xsc, xsc_ld, sel, sel_ld, s.slot_pos,
+                                                 s.counts, R, E, k, H, s.perm, s.xp, s.xa, st),
+                     "moe_experts scatter launch");
+    if (rc != MFI_OK) return rc;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    mfi::PrefillLaunch L{};
+    L.E = E; L.H = H; L.Mi = Mi; L.top_k = k; L.grid = sms;
+    L.prepared = static_cast<const uint8_t*>(w->prepared);
+    L.counts = s.counts; L.perm = s.perm; L.rows = s.rows;
+    L.xp = s.xp; L.xa = s.xa; L.hp = s.hp; L.ha = s.ha;
+    L.yd = s.yd;
+    L.err = mfi::device_error_flag(); L.queue = s.queue; L.gu_done = s.gu_done; L.ready = s.ready;
+    L.pdl = true;
+    rc = cuda_status(mfi::launch_moe_prefill(L, st), "moe_experts prefill launch");
+    if (rc != MFI_OK) return rc;
+    return cuda_status(mfi::launch_combine_sel_bf16(s.yd, sel, sel_ld, selw, selw_ld, R, k, E, H,
+                                                    out, out_ld, st),
+                       "moe_experts combine launch");
+  }
+  ExpertScratch s = carve_experts(workspace, R, H, Mi, E, k);
   int rc = cuda_status(cudaMemsetAsync(s.cursor, 0, sizeof(int) * s.zero_words, st),
                        "moe_experts memset");
   if (rc != MFI_OK) return rc;

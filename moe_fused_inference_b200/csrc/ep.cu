@@ -237,6 +237,49 @@ __global__ void __launch_bounds__(128) combine_sel_kernel(
     *reinterpret_cast<float4*>(out + size_t(m) * out_ld + c4) = ordered_sum4<false>(s_rows, s_w, s_m, c4);
 }
 
+// combine_sel_kernel on bf16 rows: the same slot order and unfused fp32
+// multiply and add, 8 columns per thread.
+__global__ void __launch_bounds__(128) combine_sel_bf16_kernel(
+    const __nv_bfloat16* __restrict__ yd, const int* __restrict__ sel, long long sel_ld,
+    const float* __restrict__ w, long long w_ld, int k, int E, int H, float* __restrict__ out,
+    long long out_ld) {
+  tc::grid_dep_wait();  // yd comes from the previous kernel
+  const int m = blockIdx.x;
+  __shared__ const __nv_bfloat16* s_rows[32];
+  __shared__ float s_w[32];
+  __shared__ int s_m;
+  if (threadIdx.x < 32) {
+    const int j = threadIdx.x;
+    const bool valid = j < k && unsigned(sel[size_t(m) * sel_ld + j]) < unsigned(E);
+    const unsigned mask = __ballot_sync(0xffffffffu, valid);
+    if (valid) {
+      const int pos = __popc(mask & ((1u << j) - 1u));
+      s_rows[pos] = yd + (size_t(m) * k + j) * H;
+      s_w[pos] = w[size_t(m) * w_ld + j];
+    }
+    if (j == 0) s_m = __popc(mask);
+  }
+  __syncthreads();
+  const int n = s_m;
+  for (int c8 = threadIdx.x * 8; c8 < H; c8 += blockDim.x * 8) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int i = 0; i < n; ++i) {
+      const float wi = s_w[i];
+      const uint4 v = *reinterpret_cast<const uint4*>(s_rows[i] + c8);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(h2[q]);
+        acc[2 * q] = __fadd_rn(acc[2 * q], __fmul_rn(wi, f.x));
+        acc[2 * q + 1] = __fadd_rn(acc[2 * q + 1], __fmul_rn(wi, f.y));
+      }
+    }
+    float4* o = reinterpret_cast<float4*>(out + size_t(m) * out_ld + c8);
+    o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Peer-memory exchange: the router writes rows straight into the owning
 // ranks' receive buffers and raises a per-source flag to the call id
@@ -502,6 +545,24 @@ cudaError_t launch_scatter_sel(const uint8_t* xq, long long xq_ld, const uint8_t
   scatter_sel_kernel<<<R, 128, 0, stream>>>(xq, xq_ld, xsc, xsc_ld, sel, sel_ld, R, k, H, E, T_pad,
                                             cursor, perm, xp, xp_atoms, status);
   return cudaGetLastError();
+}
+
+cudaError_t launch_combine_sel_bf16(const __nv_bfloat16* yd, const int* sel, long long sel_ld,
+                                    const float* w, long long w_ld, int R, int k, int E, int H,
+                                    float* out, long long out_ld, cudaStream_t stream) {
+  if (R == 0) return cudaSuccess;
+  if (H % 8 != 0) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(R);
+  cfg.blockDim = dim3(128);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, combine_sel_bf16_kernel, yd, sel, sel_ld, w, w_ld, k, E, H, out,
+                            out_ld);
 }
 
 cudaError_t launch_combine_sel(const float* yd, const int* sel, long long sel_ld, const float* w,

@@ -207,81 +207,131 @@ cudaError_t launch_dense_gemv(const uint8_t* xq, const uint8_t* xsc, const uint8
 //   mode 0 (gate/up): z = m*2E + proj*E + e -> act row m, out row (m*E+e)*2N + proj*N
 //   mode 1 (down):    z = m*E + e           -> act row z, out row z*N
 // One CTA of 1024 threads; P <= 4096 (the table is staged in shared memory).
+// Every step is spread over the block: each entry finds its group's first
+// entry (its lead) and its rank among the group's entries by one pass over
+// the entries before it, and the group numbering and the group offsets are
+// block-wide prefix sums.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(1024) build_groups_kernel(
+constexpr int kBgThreads = 1024;
+
+// Exclusive prefix sum of v[0..n) in place (n <= 4 * kBgThreads), returns the
+// total.  Each thread sums four consecutive elements, warps scan by shuffles,
+// the 32 warp totals are scanned by warp 0.
+__device__ int block_exclusive_scan(int* v, int n, int* s_warp) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  int a[4], sum = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int k = 4 * t + i;
+    a[i] = k < n ? v[k] : 0;
+    sum += a[i];
+  }
+  int inc = sum;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, inc, off);
+    if (lane >= off) inc += u;
+  }
+  if (lane == 31) s_warp[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    int w = s_warp[lane];
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, w, off);
+      if (lane >= off) w += u;
+    }
+    s_warp[lane] = w;  // inclusive
+  }
+  __syncthreads();
+  int run = inc - sum + (warp > 0 ? s_warp[warp - 1] : 0);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int k = 4 * t + i;
+    if (k < n) v[k] = run;
+    run += a[i];
+  }
+  const int total = s_warp[31];
+  __syncthreads();
+  return total;
+}
+
+__global__ void __launch_bounds__(kBgThreads) build_groups_kernel(
     const uint8_t* const* __restrict__ wp_tab, const uint8_t* const* __restrict__ wsc_tab, int P,
     int mode, int E, int N, GroupDesc* __restrict__ groups, int* __restrict__ n_groups,
     EntryDesc* __restrict__ entries) {
   extern __shared__ __align__(16) unsigned char shraw[];
-  const uint8_t** s_wp = reinterpret_cast<const uint8_t**>(shraw);          // P
-  const uint8_t** s_ws = s_wp + P;                                            // P
-  int* lead = reinterpret_cast<int*>(s_ws + P);                               // P
-  int* gidx = lead + P;     // P: group index of a lead entry
-  int* cnt = lead + 2 * P;  // P: entries per group (by group index)
-  int* first = lead + 3 * P;
+  const uint8_t** s_wp = reinterpret_cast<const uint8_t**>(shraw);  // P
+  const uint8_t** s_ws = s_wp + P;                                    // P
+  int* lead = reinterpret_cast<int*>(s_ws + P);  // P: first entry of the entry's group
+  int* rank = lead + P;                          // P: place among its group's entries
+  int* gidx = lead + 2 * P;                      // P: is-lead flags, then group index of a lead
+  int* cnt = lead + 3 * P;                       // P: entries per group, then group offsets
+  __shared__ int s_warp[32];
   for (int z = threadIdx.x; z < P; z += blockDim.x) {
     s_wp[z] = wp_tab[z];
     s_ws[z] = wsc_tab[z];
+    cnt[z] = 0;
   }
   __syncthreads();
   for (int z = threadIdx.x; z < P; z += blockDim.x) {
     const uint8_t* a = s_wp[z];
     const uint8_t* b = s_ws[z];
-    int l = z;
-    for (int j = 0; j < z; ++j)
-      if (s_wp[j] == a && s_ws[j] == b) { l = j; break; }
+    int l = z, r = 0;
+    for (int j = 0; j < z; ++j) {
+      const bool same = s_wp[j] == a && s_ws[j] == b;
+      if (same && l == z) l = j;
+      r += same;
+    }
     lead[z] = l;
+    rank[z] = r;
+    gidx[z] = l == z;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int ng = 0;
-    for (int z = 0; z < P; ++z) {
-      if (lead[z] == z) { gidx[z] = ng; cnt[ng] = 0; ++ng; }
+  const int ng = block_exclusive_scan(gidx, P, s_warp);  // gidx[lead] = its group's index
+  for (int z = threadIdx.x; z < P; z += blockDim.x) atomicAdd(&cnt[gidx[lead[z]]], 1);
+  __syncthreads();
+  block_exclusive_scan(cnt, ng, s_warp);  // cnt[g] = first entry of group g
+  for (int z = threadIdx.x; z < P; z += blockDim.x) {
+    if (lead[z] == z) {
+      const int g = gidx[z];
+      GroupDesc gd;
+      gd.wp = s_wp[z];
+      gd.wsc = s_ws[z];
+      gd.first = cnt[g];
+      gd.count = (g + 1 < ng ? cnt[g + 1] : P) - cnt[g];
+      groups[g] = gd;
     }
-    for (int z = 0; z < P; ++z) cnt[gidx[lead[z]]]++;
-    int acc = 0;
-    for (int g = 0; g < ng; ++g) { first[g] = acc; acc += cnt[g]; cnt[g] = 0; }
-    for (int z = 0; z < P; ++z) {
-      const int g = gidx[lead[z]];
-      const int pos = first[g] + cnt[g]++;
-      EntryDesc ed;
-      ed.pad = 0;
-      if (mode == 0) {
-        const int m = z / (2 * E), pair = z % (2 * E), proj = pair / E, e = pair % E;
-        ed.act_row = m;
-        ed.out_off = (long long)(m * E + e) * 2 * N + (long long)proj * N;
-      } else {
-        ed.act_row = z;
-        ed.out_off = (long long)z * N;
-      }
-      entries[pos] = ed;
-    }
-    for (int z = 0; z < P; ++z) {
-      if (lead[z] == z) {
-        const int g = gidx[z];
-        GroupDesc gd;
-        gd.wp = s_wp[z];
-        gd.wsc = s_ws[z];
-        gd.first = first[g];
-        gd.count = cnt[g];
-        groups[g] = gd;
-      }
-    }
-    *n_groups = ng;
   }
+  for (int z = threadIdx.x; z < P; z += blockDim.x) {
+    const int g = gidx[lead[z]];
+    EntryDesc ed;
+    ed.pad = 0;
+    if (mode == 0) {
+      const int m = z / (2 * E), pair = z % (2 * E), proj = pair / E, e = pair % E;
+      ed.act_row = m;
+      ed.out_off = (long long)(m * E + e) * 2 * N + (long long)proj * N;
+    } else {
+      ed.act_row = z;
+      ed.out_off = (long long)z * N;
+    }
+    entries[cnt[g] + rank[z]] = ed;
+  }
+  if (threadIdx.x == 0) *n_groups = ng;
 }
 
 cudaError_t launch_build_groups(const uint8_t* const* wp_tab, const uint8_t* const* wsc_tab, int P,
                                 int mode, int E, int N, GroupDesc* groups, int* n_groups,
                                 EntryDesc* entries, cudaStream_t stream) {
+  if (P <= 0 || P > 4 * kBgThreads) return cudaErrorInvalidValue;
   const size_t smem = size_t(P) * (2 * sizeof(void*) + 4 * sizeof(int));
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(build_groups_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
   }
-  build_groups_kernel<<<1, 1024, smem, stream>>>(wp_tab, wsc_tab, P, mode, E, N, groups, n_groups,
-                                                 entries);
+  build_groups_kernel<<<1, kBgThreads, smem, stream>>>(wp_tab, wsc_tab, P, mode, E, N, groups,
+                                                        n_groups, entries);
   return cudaGetLastError();
 }
 

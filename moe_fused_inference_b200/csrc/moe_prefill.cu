@@ -126,11 +126,14 @@ __device__ int expert_bases(const int* s_cnt, int E, int* s_base) {
 }
 
 // One CTA per kScTok tokens: copy each token's quantised row and scale atoms
-// to its k expert rows (the expert bases are computed once per CTA).
+// to its k expert rows (the expert bases are computed once per CTA).  Row t's
+// expert list is topi[t * sel_ld + j]; entries outside [0, E) (slots of
+// received rows that name no local expert) are skipped.
 constexpr int kScTok = 4;
 constexpr int kScThreads = 256;
 __global__ void __launch_bounds__(kScThreads) prefill_scatter_kernel(
-    const uint8_t* __restrict__ xq, const uint8_t* __restrict__ xsc, const int* __restrict__ topi,
+    const uint8_t* __restrict__ xq, long long xq_ld, const uint8_t* __restrict__ xsc,
+    long long xsc_ld, const int* __restrict__ topi, long long sel_ld,
     const int* __restrict__ slot_pos, const int* __restrict__ counts, int T, int E, int k, int H,
     int* __restrict__ perm, uint8_t* __restrict__ xp, uint8_t* __restrict__ xa) {
   const int tok0 = blockIdx.x * kScTok;
@@ -143,25 +146,49 @@ __global__ void __launch_bounds__(kScThreads) prefill_scatter_kernel(
   if (threadIdx.x < 32) expert_bases(s_cnt, E, s_base);
   __syncthreads();
   for (int p = threadIdx.x; p < nt * k; p += blockDim.x) {
-    const long pair = long(tok0) * k + p;
-    const int row = s_base[topi[pair]] + slot_pos[pair];
+    const int t = tok0 + p / k, j = p % k;
+    const long pair = long(t) * k + j;
+    const int e = topi[size_t(t) * sel_ld + j];
+    int row = -1;
+    if (unsigned(e) < unsigned(E)) {
+      row = s_base[e] + slot_pos[pair];
+      perm[row] = int(pair);
+    }
     s_row[p] = row;
-    perm[row] = int(pair);
   }
   __syncthreads();
   const int q16 = H / 32, kc = H / 128;
   for (int p = threadIdx.x; p < nt * k * q16; p += blockDim.x) {
     const int pj = p / q16, c = p - pj * q16;  // pair (token i = pj / k), 16-byte chunk c
+    if (s_row[pj] < 0) continue;
     reinterpret_cast<uint4*>(xp + size_t(s_row[pj]) * (H / 2))[c] =
-        reinterpret_cast<const uint4*>(xq + size_t(tok0 + pj / k) * (H / 2))[c];
+        reinterpret_cast<const uint4*>(xq + size_t(tok0 + pj / k) * xq_ld)[c];
   }
   for (int p = threadIdx.x; p < nt * k * kc; p += blockDim.x) {
     const int pj = p / kc, c = p - pj * kc;
     const int row = s_row[pj];
+    if (row < 0) continue;
     *reinterpret_cast<uint32_t*>(xa + (size_t(row / kPTile) * kc + c) * 512 + (row % 32) * 16 +
                                  ((row % kPTile) / 32) * 4) =
-        reinterpret_cast<const uint32_t*>(xsc + size_t(tok0 + pj / k) * (H / 32))[c];
+        reinterpret_cast<const uint32_t*>(xsc + size_t(tok0 + pj / k) * xsc_ld)[c];
   }
+}
+
+// Positions of pre-routed (row, slot) pairs among their expert's rows, for
+// rows that arrive already routed (expert parallelism): slot_pos[r * k + j] =
+// the count of expert sel[r][j] before it (atomic claim, so the order of the
+// rows inside a region varies between runs; every row's result does not
+// depend on it).  Slots naming no local expert (outside [0, E)) are skipped;
+// ids >= E are reported as error 4.
+__global__ void __launch_bounds__(256) prefill_count_sel_kernel(
+    const int* __restrict__ sel, long long sel_ld, int R, int k, int E, int* __restrict__ counts,
+    int* __restrict__ slot_pos, int* __restrict__ status) {
+  const long i = long(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= long(R) * k) return;
+  const int r = int(i / k), j = int(i % k);
+  const int e = sel[size_t(r) * sel_ld + j];
+  if (e >= E) atomicCAS(status, 0, 4);
+  slot_pos[i] = unsigned(e) < unsigned(E) ? atomicAdd(counts + e, 1) : -1;
 }
 
 __global__ void __launch_bounds__(kPThreads, 1)
@@ -403,28 +430,40 @@ __global__ void __launch_bounds__(kPThreads, 1)
         // columns 0-63: gate outputs tile*64 + c, 64-127: the same up outputs;
         // this warp takes h block `half` (outputs half*32 .. +31) whole, so
         // the block maximum needs no exchange with another warp
-        uint32_t g[32], u[32];
-        tmem_ld_32x32b_x32(tbase + half * 32, g);
-        tmem_ld_32x32b_x32(tbase + 64 + half * 32, u);
-        tmem_ld_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        // h goes through this warp's staging tile in shared memory (lane l
+        // keeps its 32 values in its own 128-byte row, element i at word
+        // i ^ l, so neither pass has bank conflicts), and gate / up come in
+        // loads of 4 columns: the SwiGLU pass and the quantisation pass then
+        // each hold only a few values, and the warp stays within the 96
+        // registers a thread of this 18-warp block has, without spilling
+        float* hs = reinterpret_cast<float*>(out_stage + ew * kPOutStage) + lane * 32;
         float am = 0.0f;
         bool nan = false;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float h = swiglu(__uint_as_float(g[i]), __uint_as_float(u[i]));
-          g[i] = __float_as_uint(h);
-          am = fmaxf(am, fabsf(h));
-          nan |= (h != h);
+        for (int q = 0; q < 8; ++q) {
+          uint32_t gq[4], u[4];
+          tmem_ld_32x32b_x4(tbase + half * 32 + q * 4, gq);
+          tmem_ld_32x32b_x4(tbase + 64 + half * 32 + q * 4, u);
+          tmem_ld_wait();
+          if (q == 7) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float h = swiglu(__uint_as_float(gq[i]), __uint_as_float(u[i]));
+            hs[(q * 4 + i) ^ lane] = h;
+            am = fmaxf(am, fabsf(h));
+            nan |= (h != h);
+          }
         }
         // a NaN anywhere in the block gives code 127, like quant_group8
         const BlockScale bs = block_scale(nan ? __uint_as_float(0x7fc00000u) : am);
         uint32_t w[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-          w[i >> 3] |= quant_nibble(__uint_as_float(g[i]), bs.inv) << (4 * (i & 7));
+          w[i >> 3] |= quant_nibble(hs[i ^ lane], bs.inv) << (4 * (i & 7));
         if (valid) {
           *reinterpret_cast<uint4*>(p.hp + size_t(row) * (p.inter / 2) + tile * 32 + half * 16) =
               make_uint4(w[0], w[1], w[2], w[3]);
@@ -504,13 +543,24 @@ size_t prefill_rows(int pairs, int E) {
   return (size_t(pairs) + kPTile - 1) / kPTile * kPTile + active * kPTile;
 }
 
-cudaError_t launch_prefill_scatter(const uint8_t* xq, const uint8_t* xsc, const int* topi,
+cudaError_t launch_prefill_scatter(const uint8_t* xq, long long xq_ld, const uint8_t* xsc,
+                                   long long xsc_ld, const int* topi, long long sel_ld,
                                    const int* slot_pos, const int* counts, int T, int E, int k,
                                    int H, int* perm, uint8_t* xp, uint8_t* xa,
                                    cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
   prefill_scatter_kernel<<<(T + kScTok - 1) / kScTok, kScThreads, 0, stream>>>(
-      xq, xsc, topi, slot_pos, counts, T, E, k, H, perm, xp, xa);
+      xq, xq_ld, xsc, xsc_ld, topi, sel_ld, slot_pos, counts, T, E, k, H, perm, xp, xa);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_count_sel(const int* sel, long long sel_ld, int R, int k, int E,
+                                     int* counts, int* slot_pos, int* status,
+                                     cudaStream_t stream) {
+  const long n = long(R) * k;
+  if (n == 0) return cudaSuccess;
+  prefill_count_sel_kernel<<<unsigned((n + 255) / 256), 256, 0, stream>>>(sel, sel_ld, R, k, E,
+                                                                           counts, slot_pos, status);
   return cudaGetLastError();
 }
 

@@ -36,18 +36,18 @@ __device__ __forceinline__ float load_elem(const void* p, long i, int dtype) {
 }
 
 // Nearest E2M1 magnitude index of |x| (x already divided by the block scale),
-// ties toward the larger magnitude, clamp at 6 (index 7).
+// ties toward the larger magnitude, clamp at 6 (index 7); NaN gives 7, as in
+// the reference.  Read from the bits of a = |x|: at a >= 1 the grid {1, 1.5,
+// 2, 3, 4, 6} keeps one mantissa bit, so adding half of that bit's weight
+// (bit 21) and keeping exponent + top mantissa bit (bits >> 22) rounds half
+// up, and 1.0 (bits >> 22 = 254) is index 2; below 1 the grid is {0, .5, 1}
+// with midpoints .25 and .75.  Infinities and NaNs (exponent field 255) land
+// above index 7 and clamp to it.
 __device__ __forceinline__ uint32_t e2m1_mag(float a) {
-  uint32_t c = 0;
-  c += (a >= 0.25f);
-  c += (a >= 0.75f);
-  c += (a >= 1.25f);
-  c += (a >= 1.75f);
-  c += (a >= 2.5f);
-  c += (a >= 3.5f);
-  c += (a >= 5.0f);
-  // NaN compares false everywhere; the reference maps it to magnitude 7.
-  return (a != a) ? 7u : c;
+  const uint32_t b = __float_as_uint(a) & 0x7FFFFFFFu;
+  const uint32_t hi = min(((b + 0x200000u) >> 22) - 252u, 7u);
+  const uint32_t lo = uint32_t(b >= 0x3E800000u) + uint32_t(b >= 0x3F400000u);  // .25, .75
+  return b >= 0x3F800000u ? hi : lo;
 }
 
 // Unclamped block exponent e (see header).  amax must be >= 0 or NaN.
@@ -105,15 +105,53 @@ __device__ __forceinline__ void nib8_to_i8(uint32_t w, uint32_t& lo, uint32_t& h
   hi = __byte_perm(ph, nh, 0x3210u | (s >> 16));
 }
 
+// Correctly rounded a / b by Markstein's method (P. Markstein, "Computation
+// of elementary functions on the IBM RISC System/6000 processor", IBM J. Res.
+// Dev. 34(1), 1990): an approximate reciprocal y0, one Newton step
+// y1 = y0 + y0 (1 - b y0), the quotient q0 = a y1, its exact remainder
+// r = a - b q0 (one FMA) and the correction q0 + r y1, which is a / b rounded
+// to nearest even as long as b, 1/b, a and the quotient are normal numbers.
+__device__ __forceinline__ float div_markstein(float a, float b) {
+  float y0;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y0) : "f"(b));
+  const float e = __fmaf_rn(-b, y0, 1.0f);
+  const float y1 = __fmaf_rn(y0, e, y0);
+  const float q0 = __fmul_rn(a, y1);
+  const float r = __fmaf_rn(-b, q0, a);
+  return __fmaf_rn(r, y1, q0);
+}
+
+// g / b for b = 1 + expf(-g) where the plain Markstein division does not
+// apply (|g| < 2^-100 or > 80, infinities, NaN); the exact IEEE quotient.
+static __device__ __noinline__ float swiglu_quotient_edge(float g, float b) {
+  if (g != g || b != b) return __uint_as_float(0x7FFFFFFFu);
+  if (isinf(g)) return b == 1.0f ? g : __uint_as_float(0x7FFFFFFFu);  // +inf / 1, -inf / inf
+  if (isinf(b)) return copysignf(0.0f, g);  // g < -88.7: e^-g overflows
+  if (b == 1.0f) return g;                  // g > 80: e^-g is below half an ulp of 1
+  if (b == 2.0f) return __fmul_rn(g, 0.5f); // |g| < 2^-100 (zeros, subnormals)
+  // -88.7 < g < -80: b is up to 2^128 and 1/b may be subnormal, the quotient
+  // is normal: divide by b 2^-32 and scale back (both exact powers of two)
+  return __fmul_rn(div_markstein(g, __fmul_rn(b, 0x1p-32f)), 0x1p-32f);
+}
+
 // SwiGLU, h = (g / (1 + e^-g)) * u in fp32, the one form every kernel of the
 // library uses (the moe_down operator and the fused decode / prefill
 // epilogues).  It is the reference kernel's expression
 // (src/ext/mxfp4_decode.cu:258) as its build compiles it: runtime/fp4_ext.py
 // builds the extension with -O3 and no fast-math flag, so expf is CUDA's
 // expf and '/' a correctly rounded division; nothing in it can be contracted
-// into an FMA.
+// into an FMA.  The division is div_markstein, which for |g| in [2^-100, 80]
+// (b in [1, 1 + e^80], quotient normal) is the correctly rounded quotient;
+// the rest goes to swiglu_quotient_edge.  mfi_selftest_numerics compares the
+// quotient with CUDA's __fdiv_rn for all 2^32 values of g.
+__device__ __forceinline__ float swiglu_quotient(float g) {
+  const float b = __fadd_rn(1.0f, expf(-g));
+  const float ag = fabsf(g);
+  if (ag >= 0x1p-100f && ag <= 80.0f) return div_markstein(g, b);
+  return swiglu_quotient_edge(g, b);
+}
 __device__ __forceinline__ float swiglu(float g, float u) {
-  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+  return __fmul_rn(swiglu_quotient(g), u);
 }
 
 // 2^e as float for e in the normal range; ldexpf outside it.

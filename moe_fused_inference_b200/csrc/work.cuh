@@ -212,6 +212,10 @@ cudaError_t launch_scatter_sel(const uint8_t* xq, long long xq_ld, const uint8_t
                                long long xsc_ld, const int* sel, long long sel_ld, int R, int k,
                                int H, int E, int T_pad, int* cursor, int* perm, uint8_t* xp,
                                uint8_t* xp_atoms, int* status, cudaStream_t stream);
+// combine_sel on bf16 rows (the prefill kernel's y).
+cudaError_t launch_combine_sel_bf16(const __nv_bfloat16* yd, const int* sel, long long sel_ld,
+                                    const float* w, long long w_ld, int R, int k, int E, int H,
+                                    float* out, long long out_ld, cudaStream_t stream);
 cudaError_t launch_combine_sel(const float* yd, const int* sel, long long sel_ld, const float* w,
                                long long w_ld, int R, int k, int E, int H, float* out,
                                long long out_ld, cudaStream_t stream);
@@ -231,10 +235,18 @@ struct PrefillLaunch {
   bool pdl;
 };
 size_t prefill_rows(int pairs, int E);
-cudaError_t launch_prefill_scatter(const uint8_t* xq, const uint8_t* xsc, const int* topi,
+// Rows t < T with expert lists topi[t * sel_ld + j] (entries outside [0, E)
+// skipped) into the per-expert regions; xq / xsc rows at strides xq_ld /
+// xsc_ld bytes.
+cudaError_t launch_prefill_scatter(const uint8_t* xq, long long xq_ld, const uint8_t* xsc,
+                                   long long xsc_ld, const int* topi, long long sel_ld,
                                    const int* slot_pos, const int* counts, int T, int E, int k,
                                    int H, int* perm, uint8_t* xp, uint8_t* xa,
                                    cudaStream_t stream);
+// Per-expert counts and slot positions of pre-routed rows (counts zeroed).
+cudaError_t launch_prefill_count_sel(const int* sel, long long sel_ld, int R, int k, int E,
+                                     int* counts, int* slot_pos, int* status,
+                                     cudaStream_t stream);
 cudaError_t launch_moe_prefill(const PrefillLaunch& L, cudaStream_t stream);
 
 // Peer-memory exchange (ep.cu).

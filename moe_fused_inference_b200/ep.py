@@ -123,6 +123,10 @@ def random_shard(n_experts: int, world: int, rank: int, hidden: int = 2048, inte
                    dwp.view(el, H, Mi // 2), dsc.view(el, H, Mi // 32), rwp, rsc)
 
 
+# mfi_ep_experts_return: world * (capacity + 1) * top_k (row, slot) pairs at most
+P2P_MAX_PAIRS = 16384
+
+
 def ep_row_bytes(hidden: int, top_k: int) -> int:
     """Bytes of one exchanged row (mfi_ep_row_bytes)."""
     b = hidden // 2 + hidden // 32 + 16 + 8 * top_k
@@ -349,10 +353,19 @@ class EPMoELayer:
         self.topw = torch.empty((C, top_k), dtype=torch.float32, device=dev)
         self.counts = torch.zeros(n, dtype=torch.int32, device=dev)
         self.pack_pos = torch.empty((C, n), dtype=torch.int32, device=dev)
+        # the peer-memory transport runs the decode expert kernels (at most
+        # 16384 (row, slot) pairs per rank); larger exchanges (prefill) take
+        # the all-to-all transport, whose expert step switches to the prefill
+        # kernels
+        p2p_fits = n * (C + 1) * top_k <= P2P_MAX_PAIRS
         if transport is None:
-            transport = "nccl" if ops is not None or not torch.device(dev).type == "cuda" else "p2p"
+            transport = ("nccl" if ops is not None or not torch.device(dev).type == "cuda"
+                         or not p2p_fits else "p2p")
         if transport not in ("p2p", "nccl"):
             raise RuntimeError("transport must be 'p2p' or 'nccl'")
+        if transport == "p2p" and not p2p_fits:
+            raise RuntimeError(f"the p2p transport holds at most {P2P_MAX_PAIRS} (row, slot) pairs "
+                               f"per rank: world * (capacity + 1) * top_k = {n * (C + 1) * top_k}")
         self.transport = transport
         self.xch = None
         if transport == "p2p":

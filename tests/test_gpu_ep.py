@@ -88,6 +88,58 @@ def test_ep_emulated_matches_single_gpu(world, counts):
         assert cosine(a, b) >= 0.999999
 
 
+@pytest.mark.parametrize("world,counts,zipf", [(2, [1100, 700], False), (4, [600, 0, 2100, 900], True),
+                                               (8, [2048] * 8, True)])
+def test_ep_prefill_emulated_matches_single_gpu(world, counts, zipf):
+    """Expert-parallel prefill (BASELINE config 5 at its per-rank sizes): more
+    than 16384 (row, slot) pairs per rank, so the expert step runs the prefill
+    tcgen05 kernels on the received rows, with ragged per-rank token counts
+    (one rank empty) and Zipf-skewed routing.  Every rank here has more than
+    512 tokens, so the single-GPU layer takes its prefill path too: the expert
+    outputs are the same bf16 rows and only the combine's summation order
+    (local slots, then ranks) differs."""
+    from moe_fused_inference_b200.ep import EPMoELayer, EPShard
+    from moe_fused_inference_b200.layer import MoELayer
+    E, H, Mi, k = 128, 2048, 768, 8
+    w = _layer_w(E, H, Mi, seed=9)
+    bias = torch.from_numpy(zipf_bias(E, 0.5, seed=3)).cuda() if zipf else None
+    C = max(counts)
+    xs = [_x(t, H, 80 + r) for r, t in enumerate(counts)]
+    layers = [EPMoELayer(EPShard.from_layer(w, r, world), k, C, world=world, rank=r,
+                         logit_bias=bias) for r in range(world)]
+    assert all(L.transport == "nccl" for L in layers)  # too large for the peer-memory transport
+    for L, x in zip(layers, xs):
+        L.dispatch_prepare(x)
+    for d in range(world):
+        for s in range(world):
+            layers[d].recv[s].copy_(layers[s].send[d])
+    for L in layers:
+        L.compute()
+    for s in range(world):
+        for d in range(world):
+            layers[s].ret_back[d].copy_(layers[d].ret[s])
+    outs = []
+    for L, x in zip(layers, xs):
+        out = torch.empty((x.shape[0], H), dtype=torch.float32, device="cuda")
+        L.finish(x.shape[0], out)
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert _lib().load().mfi_device_error(1) == 0
+    single = MoELayer(w, top_k=k, logit_bias=bias)
+    for r, x in enumerate(xs):
+        if x.shape[0] == 0:
+            continue
+        ref, topi, topw = single(x)
+        torch.cuda.synchronize()
+        assert torch.equal(layers[r].topi[: x.shape[0]], topi)
+        assert torch.equal(layers[r].topw[: x.shape[0]], topw)
+        a, b = outs[r].cpu().numpy(), ref.cpu().numpy()
+        assert max_rel_err(a, b) <= 1e-5
+        assert cosine(a, b) >= 0.999999
+    for L in layers:
+        L.close()
+
+
 def _emulate_p2p(w, xs, world, k, capacity, calls=1, logit_bias=None):
     """The peer-memory transport over `world` virtual ranks on one GPU: every
     rank's block is an allocation of this process, so the peer table holds
@@ -280,8 +332,9 @@ def test_experts_rejects_bad_args():
     st = lib.mfi_moe_experts(ctypes.byref(cw), 0, 256, 0, 16, 0, 4, 0, 4, 4, 0, 512, 0, 0, 0)
     assert st == 1 and b"multiples of 256" in lib.mfi_last_error()
     cw.inter = 256
-    st = lib.mfi_moe_experts(ctypes.byref(cw), 0, 256, 0, 16, 0, 4, 0, 4, 5000, 0, 512, 0, 0, 0)
-    assert st == 1 and b"16384" in lib.mfi_last_error()
+    # past the prefill kernels' 262144 (row, slot) pairs
+    st = lib.mfi_moe_experts(ctypes.byref(cw), 0, 256, 0, 16, 0, 4, 0, 4, 70000, 0, 512, 0, 0, 0)
+    assert st == 1 and b"262144" in lib.mfi_last_error()
 
 
 def _free_port():

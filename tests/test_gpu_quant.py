@@ -82,3 +82,18 @@ def test_weight_quantizer_large_matrix():
     p, c = quantize_rows(w.cuda())
     rp, rc = mx.quantize_rows(w.float().numpy())
     assert np.array_equal(p.cpu().numpy(), rp) and np.array_equal(c.cpu().numpy(), rc)
+
+
+def test_selftest_numerics_all_fp32_patterns():
+    """The library's own SwiGLU quotient (Markstein's division) equals CUDA's
+    correctly rounded g / (1 + expf(-g)) — the reference build's arithmetic,
+    src/ext/mxfp4_decode.cu:258 — and its bit-level E2M1 rounding equals the
+    threshold definition, on all 2^32 fp32 bit patterns."""
+    from moe_fused_inference_b200 import _lib
+    out = torch.zeros(4, dtype=torch.int64, device="cuda")
+    lib = _lib.load()
+    assert lib.mfi_selftest_numerics(out.data_ptr(), None) == 0, lib.mfi_last_error()
+    torch.cuda.synchronize()
+    bad_q, bad_m, first_q, first_m = out.tolist()
+    assert bad_q == 0, f"{bad_q} quotient mismatches, first at bits {first_q & 0xFFFFFFFF:#010x}"
+    assert bad_m == 0, f"{bad_m} E2M1 mismatches, first at bits {first_m & 0xFFFFFFFF:#010x}"
