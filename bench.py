@@ -615,8 +615,8 @@ def attn_point(dev, stream, steps, warmup, peak, ctx=4096, M=1, n_caches=48):
     head_dim 128) of M query rows at context `ctx` over n_caches distinct
     layer caches (n_caches x ctx x 4 x 128 x 2 B, larger than L2), all calls
     in one CUDA graph.  Bytes per call: the live K and V positions."""
-    from moe_fused_inference_b200 import fp4_ext
-    dext = fp4_ext.get_decode_ext()
+    from moe_fused_inference_b200 import _lib
+    lib = _lib.load()
     Hq, Hkv, D = 32, 4, 128
     max_pos = ctx + M
     g = torch.Generator(device=dev).manual_seed(23)
@@ -627,10 +627,17 @@ def attn_point(dev, stream, steps, warmup, peak, ctx=4096, M=1, n_caches=48):
     q = torch.randn((M, Hq, D), generator=g, device=dev).bfloat16()
     dpos = torch.tensor([ctx - 1], dtype=torch.int32, device=dev)
     o = torch.empty((M, Hq, D), dtype=torch.float32, device=dev)
-
+    nws = int(lib.mfi_attn_decode_workspace_bytes(M, Hq, Hkv, D, max_pos))
+    ws = torch.empty(nws, dtype=torch.uint8, device=dev)
     def calls():
+        # the reference-codec cache (no scales), through the C entry with a
+        # preallocated output and workspace (as the model runner calls it),
+        # on the stream being captured
+        st = torch.cuda.current_stream(dev).cuda_stream
         for kk, vv in caches:
-            o.copy_(dext.attn_decode(q, kk, vv, dpos, None, M))
+            _lib.check(lib.mfi_attn_decode(q.data_ptr(), kk.data_ptr(), vv.data_ptr(),
+                                           dpos.data_ptr(), o.data_ptr(), M, Hq, Hkv, D, max_pos,
+                                           None, None, ws.data_ptr(), nws, st), "attn_decode")
 
     graph = capture(dev, stream, calls, 1)
     for _ in range(warmup):
@@ -641,7 +648,7 @@ def attn_point(dev, stream, steps, warmup, peak, ctx=4096, M=1, n_caches=48):
     kv_bytes = (ctx - 1 + M) * Hkv * D * 2
     gbs = kv_bytes / us / 1e3
     return {"us": us, "kv_bytes": kv_bytes, "GBps": gbs, "frac": gbs / peak,
-            "note": "includes a device-to-device copy of o per call (graph-captured)"}
+            "note": "mfi_attn_decode (partial + merge kernels), graph-captured"}
 
 
 # ---------------------------------------------------------------------------

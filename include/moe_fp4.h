@@ -318,6 +318,14 @@ int mfi_moe_layer_prefill(const mfi_moe_weights* w, const void* x_bf16, int T, f
  * hidden and top_k of `w` are read. */
 int mfi_moe_route(const mfi_moe_weights* w, const void* x_bf16, int T, uint8_t* xq, uint8_t* xsc,
                   int32_t* topi, float* topw, float* logits, void* stream);
+/* mfi_moe_route with scratch for the tensor-core router that prefill-sized
+ * batches use (T >= 512 tokens, 128 experts); mfi_moe_route_workspace_bytes
+ * gives its size (0 when it does not apply; the workspace, 256-byte aligned,
+ * may then be NULL).  Same results as mfi_moe_route. */
+size_t mfi_moe_route_workspace_bytes(int T, int hidden, int n_experts);
+int mfi_moe_route_ex(const mfi_moe_weights* w, const void* x_bf16, int T, uint8_t* xq,
+                     uint8_t* xsc, int32_t* topi, float* topw, float* logits, void* workspace,
+                     size_t workspace_bytes, void* stream);
 
 /* Expert compute on R pre-quantised, pre-routed rows:
  *   out[r] = sum over j < top_k with sel[r][j] >= 0, in slot order, of

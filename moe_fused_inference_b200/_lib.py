@@ -53,6 +53,8 @@ SIGNATURES = {
     "mfi_moe_layer": (_I, [_VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _SZ, _VP]),
     "mfi_moe_layer_ex": (_I, [_VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _SZ, _VP, _I, _VP]),
     "mfi_moe_route": (_I, [_VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _VP]),
+    "mfi_moe_route_workspace_bytes": (_SZ, [_I, _I, _I]),
+    "mfi_moe_route_ex": (_I, [_VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _VP, _SZ, _VP]),
     "mfi_moe_layer_prefill_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
     "mfi_moe_layer_prefill": (_I, [_VP, _VP, _I, _VP, _VP, _VP, _VP, _VP, _SZ, _VP]),
     "mfi_moe_experts_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),

@@ -11,13 +11,17 @@
 // then one online-softmax pass over every position in one 128-thread block:
 // Hq x M blocks stream the whole cache serially.  Here the positions are
 // split over the grid (flash-decoding):
-//   attn_partial_kernel  CTA (split j, KV head g): decodes a 32-position tile
-//                        of K and V to fp32 in shared memory once and serves
-//                        every query head of the group and every query row
-//                        from it — scores, running max / sum, weighted V —
-//                        writing one partial (max, sum, D accumulators) per
-//                        (row, head, split) to the workspace;
-//   attn_merge_kernel    per (row, head): log-sum-exp merge of the splits.
+//   attn_partial_kernel  CTA (split j, KV head g, sequence): decodes its
+//                        positions tile by tile (128 at a time) to fp16 in
+//                        shared memory once and serves every query head of
+//                        the group and every query row from it on the tensor
+//                        cores (mma.sync m16n8k16: scores Q.K^T, then P.V,
+//                        per warp 16 positions with an online softmax), the
+//                        warps merged in shared memory, one partial (max,
+//                        sum, D accumulators) per (row, head, split) written
+//                        to the workspace;
+//   attn_merge_kernel    per (row, head): log-sum-exp merge of the splits,
+//                        launched with programmatic serialization.
 // Splits are sized from max_pos (the host does not know the device-side base
 // position); CTAs past the live positions write empty partials.
 //
@@ -27,7 +31,8 @@
 //    away from zero, encodes values below 2^-6 as round(a * 64) (0 or 1) and
 //    saturates anything that rounds to 2^8 or more to 0x7F; its decoder
 //    (e4m3_to_f32, :362-371) reads exponent 0 as m * 2^-6 and exponent 15 as
-//    448 * (1 + m/8).  The decode table below restates that decoder.
+//    448 * (1 + m/8).  ref_e4m3x2_f16x2 restates that decoder (bit shift
+//    and one exact fp16 multiply per pair).
 //  * per-KV-head fp32 scales: the standard E4M3 (e4m3fn) encoding of x/scale,
 //    round to nearest even with saturation to +-448 (cvt.rn.satfinite), and
 //    its exact decoding times the scale — the per-head scale the model
@@ -35,11 +40,13 @@
 //    runtime/model_runner_v2.py:39).
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_fp8.h>
 
 #include <cmath>
 
 #include "../../include/moe_fp4.h"
+#include "tc_ptx.cuh"
 #include "tmap.cuh"
 #include "work.cuh"
 
@@ -47,12 +54,7 @@ namespace mfi {
 namespace {
 
 constexpr int kD = 128;          // head dimension (the reference kernels assume 128)
-constexpr int kTile = 32;        // positions per shared-memory tile
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
 constexpr int kMaxGroup = 16;    // query heads per KV head
-constexpr int kRowsPerPass = 4;  // query rows held in registers per pass
-constexpr int kKStride = kD + 4; // padded fp32 row of the K tile (conflict-free float4 reads)
 // one split's partial result: D accumulators, then max and sum, padded so
 // every row starts on a 16-byte boundary (the accumulators go out as float4)
 constexpr int kPartStride = kD + 4;
@@ -94,22 +96,6 @@ __device__ __forceinline__ uint8_t e4m3_ref_encode(float v) {
 __device__ __forceinline__ uint8_t e4m3_std_encode(float v) {
   const __nv_fp8_e4m3 f(v);  // __NV_SATFINITE conversion
   return *reinterpret_cast<const uint8_t*>(&f);
-}
-
-// Decoded value of byte b: the reference's decoder or the standard format.
-__device__ __forceinline__ float e4m3_decode(uint32_t b, bool ref) {
-  const int m = int(b & 7u), e = int((b >> 3) & 15u);
-  float v;
-  if (ref) {
-    if (e == 0) v = float(m) * 0.015625f;                       // m * 2^-6
-    else if (e == 15) v = 448.0f * (float(m) * 0.125f + 1.0f);
-    else v = (float(m) * 0.125f + 1.0f) * __uint_as_float(uint32_t(e - 7 + 127) << 23);
-  } else {
-    if (e == 0) v = float(m) * 0.001953125f;                    // m * 2^-9
-    else if (e == 15 && m == 7) v = __uint_as_float(0x7fc00000u);
-    else v = (float(m) * 0.125f + 1.0f) * __uint_as_float(uint32_t(e - 7 + 127) << 23);
-  }
-  return (b & 0x80u) ? -v : v;
 }
 
 // ---- KV write ----------------------------------------------------------------
@@ -182,197 +168,388 @@ __device__ __forceinline__ AttnArgs for_sequence(AttnArgs a, int seq) {
   return a;
 }
 
-// dynamic shared memory: decode table, K tile (padded rows), V tile, queries
-constexpr size_t kSmemLut = 256 * sizeof(float);
-constexpr size_t kSmemK = size_t(kTile) * kKStride * sizeof(float);
-constexpr size_t kSmemV = size_t(kTile) * kD * sizeof(float);
-constexpr size_t kSmemQ = size_t(kMaxGroup) * kRowsPerPass * kD * sizeof(float);
-constexpr size_t kAttnSmem = kSmemLut + kSmemK + kSmemV + kSmemQ;
+// ---- tensor-core partial kernel ----------------------------------------------
+// CTA (split j, KV head g, sequence s), 8 warps.  Positions [p_lo, p_hi) of the
+// split go through shared memory in tiles of kAT = 128: the FP8 bytes are
+// decoded to fp16 (exact for both codecs: every E4M3 value, the reference's
+// 448 (1 + m/8) and m 2^-6 included, has at most 7 significant bits and lies in
+// the fp16 range) into rows of 256 bytes whose 16-byte chunk c of row r sits at
+// chunk c ^ (r & 7), so that ldmatrix reads 8 rows without bank conflicts.
+// The query vectors of the group (vector v = m * G + h: row m of head g*G + h)
+// are taken 16 at a time as the M = 16 side of mma.m16n8k16:
+//   S (16 vectors x 16 positions) = Q . K^T     per warp: its 16 positions
+//   O (16 vectors x 128 dims)    += P . V       of each tile
+// fp16 operands and fp32 accumulation.  Q (bf16) and P (fp32 in [0, 1]) are
+// split into fp16 high and low parts, x = hi + lo with |x - hi - lo| <= 2^-22 |x|
+// (|q| below 65504), and multiplied twice, so the products are those of fp32
+// operands to about 2^-22; K and V are exact.  Each warp keeps its own running
+// maximum / sum (online softmax over its tiles); the 8 warps are merged in
+// shared memory in warp order and the CTA writes one partial per vector.
+constexpr int kAT = 128;               // positions per tile (16 per warp)
+constexpr int kAWarps = 8;
+constexpr int kAThreads = kAWarps * 32;
+constexpr int kRowBytes = kD * 2;      // one fp16 row
+constexpr size_t kSmK = size_t(kAT) * kRowBytes;     // 32 KB
+constexpr size_t kSmV = kSmK;                        // 32 KB
+// the warps' accumulators for the merge reuse the tiles' memory; rows padded
+// to 136 floats so the fragment stores spread over the banks
+constexpr int kAccStride = kD + 8;
+constexpr size_t kSmAcc = size_t(kAWarps) * 16 * kAccStride * sizeof(float);
+constexpr size_t kSmTiles = kSmK + kSmV > kSmAcc ? kSmK + kSmV : kSmAcc;
+constexpr size_t kSmQ = size_t(16) * kRowBytes;      // 4 KB (x2: hi, lo)
+constexpr size_t kSmML = size_t(kAWarps) * 16 * 2 * sizeof(float);
+constexpr size_t kAttnSmem = kSmTiles + 2 * kSmQ + kSmML;
 
-__global__ void __launch_bounds__(kThreads) attn_partial_kernel(AttnArgs a_all) {
-  const AttnArgs a = for_sequence(a_all, blockIdx.z);
-  extern __shared__ __align__(16) float smem_f[];
-  float* lut = smem_f;
-  float* s_k = lut + 256;
-  float* s_v = s_k + kTile * kKStride;
-  float* s_q = s_v + kTile * kD;
-  const int split = blockIdx.x, g = blockIdx.y;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = a.Hq / a.Hkv;
-  const bool ref = a.k_scale == nullptr;
-  lut[threadIdx.x] = e4m3_decode(threadIdx.x, ref);
-  const float ks = ref ? 1.0f : a.k_scale[g];
-  const float vs = ref ? 1.0f : a.v_scale[g];
-  const float qscale = a.inv_sqrt_d * ks;  // softmax scale and the K scale, per score
-  const int base = *a.dpos;
-  const int p_lo = split * a.chunk;
-  // positions a row m may see: [0, base + m]
-  const int live_hi = min(base + a.M, a.max_pos);  // exclusive bound over all rows
-  const int p_hi = min(p_lo + a.chunk, live_hi);
-  const size_t part_stride = size_t(kPartStride);
-  __syncthreads();
-
-  for (int m0 = 0; m0 < a.M; m0 += kRowsPerPass) {
-    const int mr = min(kRowsPerPass, a.M - m0);
-    // this pass's queries of the group's heads, fp32
-    for (int i = threadIdx.x; i < G * mr * kD; i += kThreads) {
-      const int h = i / (mr * kD), r = (i / kD) % mr, d = i % kD;
-      s_q[(h * kRowsPerPass + r) * kD + d] =
-          __bfloat162float(a.q[(size_t(m0 + r) * a.Hq + g * G + h) * kD + d]);
-    }
-    // per (head of this warp, row): running max, sum and D/32 accumulators
-    // (lane owns dims 4*lane .. 4*lane + 3); warp w serves heads w, w + 8
-    float mx[2][kRowsPerPass], sm[2][kRowsPerPass], acc[2][kRowsPerPass][4];
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh)
-#pragma unroll
-      for (int r = 0; r < kRowsPerPass; ++r) {
-        mx[hh][r] = -INFINITY;
-        sm[hh][r] = 0.0f;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) acc[hh][r][c] = 0.0f;
-      }
-    for (int p0 = p_lo; p0 < p_hi; p0 += kTile) {
-      __syncthreads();  // previous tile consumed; s_q written
-      // decode the tile: 32 positions x 128 bytes of K and of V
-      for (int i = threadIdx.x; i < kTile * (kD / 4); i += kThreads) {
-        const int p = i / (kD / 4), c4 = i % (kD / 4);
-        const int pos = p0 + p;
-        uint32_t kw = 0u, vw = 0u;
-        if (pos < p_hi) {
-          const size_t off = (size_t(pos) * a.Hkv + g) * kD + c4 * 4;
-          kw = *reinterpret_cast<const uint32_t*>(a.kvk + off);
-          vw = *reinterpret_cast<const uint32_t*>(a.kvv + off);
-        }
-        *reinterpret_cast<float4*>(s_k + p * kKStride + c4 * 4) =
-            make_float4(lut[kw & 255u], lut[(kw >> 8) & 255u], lut[(kw >> 16) & 255u], lut[kw >> 24]);
-        *reinterpret_cast<float4*>(s_v + p * kD + c4 * 4) =
-            make_float4(lut[vw & 255u], lut[(vw >> 8) & 255u], lut[(vw >> 16) & 255u], lut[vw >> 24]);
-      }
-      __syncthreads();
-      const int pos = p0 + lane;  // the position this lane scores
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int h = warp + hh * kWarps;
-        if (h >= G) break;
-#pragma unroll
-        for (int r = 0; r < kRowsPerPass; ++r) {
-          if (r >= mr) break;
-          const float* qv = s_q + (h * kRowsPerPass + r) * kD;
-          const float* kv = s_k + lane * kKStride;
-          float s = 0.0f;
-#pragma unroll 8
-          for (int d = 0; d < kD; d += 4) {
-            const float4 q4 = *reinterpret_cast<const float4*>(qv + d);
-            const float4 k4 = *reinterpret_cast<const float4*>(kv + d);
-            s = fmaf(q4.x, k4.x, s);
-            s = fmaf(q4.y, k4.y, s);
-            s = fmaf(q4.z, k4.z, s);
-            s = fmaf(q4.w, k4.w, s);
-          }
-          // a row whose own position lies outside the cache attends to nothing
-          // (the reference skips it), so it merges to zeros
-          const int row_pos = base + m0 + r;
-          const bool live = pos < p_hi && pos <= row_pos && row_pos < a.max_pos && base >= 0;
-          const float x = live ? s * qscale : -INFINITY;
-          float tmax = x;
-#pragma unroll
-          for (int off = 16; off >= 1; off >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
-          if (tmax == -INFINITY) continue;  // no live position in this tile for the row
-          const float nmax = fmaxf(mx[hh][r], tmax);
-          const float corr = expf(mx[hh][r] - nmax);   // 0 on the first live tile
-          const float w = live ? expf(x - nmax) : 0.0f;
-          float wsum = w;
-#pragma unroll
-          for (int off = 16; off >= 1; off >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, off);
-          sm[hh][r] = sm[hh][r] * corr + wsum;
-          mx[hh][r] = nmax;
-          float a0 = acc[hh][r][0] * corr, a1 = acc[hh][r][1] * corr;
-          float a2 = acc[hh][r][2] * corr, a3 = acc[hh][r][3] * corr;
-#pragma unroll 8
-          for (int p = 0; p < kTile; ++p) {
-            const float wp = __shfl_sync(0xffffffffu, w, p);
-            const float4 v4 = *reinterpret_cast<const float4*>(s_v + p * kD + lane * 4);
-            a0 = fmaf(wp, v4.x, a0);
-            a1 = fmaf(wp, v4.y, a1);
-            a2 = fmaf(wp, v4.z, a2);
-            a3 = fmaf(wp, v4.w, a3);
-          }
-          acc[hh][r][0] = a0;
-          acc[hh][r][1] = a1;
-          acc[hh][r][2] = a2;
-          acc[hh][r][3] = a3;
-        }
-      }
-    }
-    // partials of this split (empty ones too: max -inf, sum 0)
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int h = warp + hh * kWarps;
-      if (h >= G) break;
-      for (int r = 0; r < mr; ++r) {
-        float* pp = a.part + ((size_t(m0 + r) * a.Hq + g * G + h) * a.nsplit + split) * part_stride;
-        *reinterpret_cast<float4*>(pp + lane * 4) =
-            make_float4(acc[hh][r][0] * vs, acc[hh][r][1] * vs, acc[hh][r][2] * vs,
-                        acc[hh][r][3] * vs);
-        if (lane == 0) {
-          pp[kD] = mx[hh][r];
-          pp[kD + 1] = sm[hh][r];
-        }
-      }
-    }
-    __syncthreads();  // s_q is rewritten by the next pass
-  }
+// byte offset of 16-byte chunk c of fp16 row r
+__device__ __forceinline__ uint32_t sw_off(int r, int c) {
+  return uint32_t(r) * kRowBytes + (uint32_t(c ^ (r & 7)) << 4);
 }
 
-// One CTA of D threads per (row, head): o = sum_j acc_j e^(max_j - M) /
-// sum_j sum_j e^(max_j - M), M the largest split maximum.  A row whose base
-// position lies outside the cache has no live position and gets zeros.
-constexpr int kMaxSplits = 1024;
+// Two E4M3 bytes (low byte -> low half) to fp16x2, standard decoding.
+__device__ __forceinline__ uint32_t e4m3x2_f16x2(uint32_t two) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(uint16_t(two & 0xFFFFu)));
+  return r;
+}
 
-__global__ void __launch_bounds__(kD) attn_merge_kernel(AttnArgs a_all) {
+// Two bytes b0 (low) and b1 of the reference codec to fp16x2, branch-free:
+// the 7 magnitude bits shifted into an fp16's exponent and mantissa fields
+// (exponent field = the byte's 4-bit exponent e, mantissa = its 3 bits) read
+// 2^(e-15) (1 + m/8), or m/8 2^-14 at e = 0; one fp16 multiply then gives the
+// reference's value exactly: x 2^8 for 1 <= e <= 14 ((1 + m/8) 2^(e-7)),
+// x 2^11 at e = 0 (m 2^-6), x 448 at e = 15 (448 (1 + m/8)).
+__device__ __forceinline__ uint32_t ref_e4m3x2_f16x2(uint32_t two) {
+  const uint32_t mag = __byte_perm(two & 0x7F7Fu, 0u, 0x4140u) << 7;  // [b0 & 0x7F, b1 & 0x7F] << 7
+  const uint32_t sgn = __byte_perm(two & 0x8080u, 0u, 0x1404u);       // sign bits to 15 and 31
+  const uint32_t ef = mag & 0x3C003C00u;                                // exponent fields
+  const uint32_t is0 = __vcmpeq2(ef, 0u), is15 = __vcmpeq2(ef, 0x3C003C00u);
+  const uint32_t mul = (0x5C005C00u & ~(is0 | is15)) | (0x68006800u & is0) | (0x5F005F00u & is15);
+  const __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&mag),
+                            *reinterpret_cast<const __half2*>(&mul));
+  return *reinterpret_cast<const uint32_t*>(&r) | sgn;
+}
+
+// 16 FP8 bytes -> 16 fp16 values (two 16-byte chunks).
+__device__ __forceinline__ void decode16(const uint4 raw, bool ref, uint4& lo, uint4& hi) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  uint32_t o[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    o[2 * i] = ref ? ref_e4m3x2_f16x2(w[i]) : e4m3x2_f16x2(w[i]);
+    o[2 * i + 1] = ref ? ref_e4m3x2_f16x2(w[i] >> 16) : e4m3x2_f16x2(w[i] >> 16);
+  }
+  lo = make_uint4(o[0], o[1], o[2], o[3]);
+  hi = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+// D (16x8 fp32) += A (16x16 fp16, row) . B (16x8 fp16, col)
+__device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                        uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+// x = hi + lo in fp16, hi = fp16(x), lo = fp16(x - hi)
+__device__ __forceinline__ void split_f16x2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(x0, x1);
+  const float2 hf = __half22float2(h);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = pack_f16x2(x0 - hf.x, x1 - hf.y);
+}
+
+__global__ void __launch_bounds__(kAThreads, 1) attn_partial_kernel(AttnArgs a_all) {
   const AttnArgs a = for_sequence(a_all, blockIdx.z);
-  const int m = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  extern __shared__ __align__(128) uint8_t smem_b[];
+  uint8_t* s_k = smem_b;
+  uint8_t* s_v = s_k + kSmK;
+  uint8_t* s_qh = smem_b + kSmTiles;
+  uint8_t* s_ql = s_qh + kSmQ;
+  float* s_ml = reinterpret_cast<float*>(s_ql + kSmQ);  // [warp][16 rows][max, sum]
+  float* s_acc = reinterpret_cast<float*>(smem_b);      // [warp][16 rows][kD], after the tiles
+  const int split = blockIdx.x, g = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int G = a.Hq / a.Hkv;
+  const int NV = G * a.M;
+  const bool ref = a.k_scale == nullptr;
+  const float ks = ref ? 1.0f : a.k_scale[g];
+  const float vs = ref ? 1.0f : a.v_scale[g];
+  const float qscale = a.inv_sqrt_d * ks;
+  const int base = *a.dpos;
+  const int p_lo = split * a.chunk;
+  const int live_hi = min(base + a.M, a.max_pos);  // exclusive bound over all rows
+  const int p_hi = min(p_lo + a.chunk, live_hi);
+  const uint32_t k_base = tc::smem_u32(s_k), v_base = tc::smem_u32(s_v);
+  const uint32_t qh_base = tc::smem_u32(s_qh), ql_base = tc::smem_u32(s_ql);
+
+  for (int v0 = 0; v0 < NV; v0 += 16) {
+    // the 16 query vectors of this pass as fp16 hi / lo rows (zero rows past NV)
+    for (int i = threadIdx.x; i < 16 * (kD / 8); i += kAThreads) {
+      const int r = i / (kD / 8), c = i % (kD / 8);  // row, 16-byte chunk (8 dims)
+      const int v = v0 + r;
+      uint32_t hi[4] = {0u, 0u, 0u, 0u}, lo[4] = {0u, 0u, 0u, 0u};
+      if (v < NV) {
+        const int m = v / G, h = v % G;
+        const uint4 qr = *reinterpret_cast<const uint4*>(
+            a.q + (size_t(m) * a.Hq + size_t(g) * G + h) * kD + c * 8);
+        const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&qr);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(q2[j]);
+          split_f16x2(f.x, f.y, hi[j], lo[j]);
+        }
+      }
+      *reinterpret_cast<uint4*>(s_qh + sw_off(r, c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      *reinterpret_cast<uint4*>(s_ql + sw_off(r, c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+    // this thread's two rows of the C fragments: vectors v0 + gid and v0 + gid + 8
+    int row_pos[2];
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int v = v0 + gid + 8 * hr;
+      const int m = v / G;
+      const int rp = base + m;
+      // a row whose own position lies outside the cache attends to nothing
+      row_pos[hr] = (v < NV && base >= 0 && rp < a.max_pos) ? rp : -1;
+    }
+    float mx[2] = {-INFINITY, -INFINITY}, sm[2] = {0.0f, 0.0f};
+    float o[16][4];
+#pragma unroll
+    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+
+    for (int t0 = p_lo; t0 < p_hi; t0 += kAT) {
+      __syncthreads();  // the previous tile is consumed (and the queries written)
+      // decode: 128 positions x 8 raw chunks of 16 bytes, for K and for V
+      {
+        uint4 rk[4], rv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int i = threadIdx.x + u * kAThreads;
+          const int p = i >> 3, c = i & 7;
+          const int pos = t0 + p;
+          rk[u] = rv[u] = make_uint4(0u, 0u, 0u, 0u);
+          if (pos < p_hi) {
+            const size_t off = (size_t(pos) * a.Hkv + g) * kD + c * 16;
+            rk[u] = __ldg(reinterpret_cast<const uint4*>(a.kvk + off));
+            rv[u] = __ldg(reinterpret_cast<const uint4*>(a.kvv + off));
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int i = threadIdx.x + u * kAThreads;
+          const int p = i >> 3, c = i & 7;
+          uint4 lo, hi;
+          decode16(rk[u], ref, lo, hi);
+          *reinterpret_cast<uint4*>(s_k + sw_off(p, 2 * c)) = lo;
+          *reinterpret_cast<uint4*>(s_k + sw_off(p, 2 * c + 1)) = hi;
+          decode16(rv[u], ref, lo, hi);
+          *reinterpret_cast<uint4*>(s_v + sw_off(p, 2 * c)) = lo;
+          *reinterpret_cast<uint4*>(s_v + sw_off(p, 2 * c + 1)) = hi;
+        }
+      }
+      __syncthreads();
+      const int wp0 = warp * 16;  // this warp's 16 positions inside the tile
+      if (t0 + wp0 >= p_hi) continue;
+      // S = Q . K^T for 16 vectors x 16 positions
+      float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int kk = 0; kk < kD / 16; ++kk) {
+        uint32_t qa[4], ql[4], kb[4];
+        const int qr = (lane & 7) + ((lane >> 3) & 1) * 8, qc = 2 * kk + (lane >> 4);
+        ldsm_x4(qh_base + sw_off(qr, qc), qa);
+        ldsm_x4(ql_base + sw_off(qr, qc), ql);
+        const int kr = wp0 + (lane & 7) + (lane >> 4) * 8, kc = 2 * kk + ((lane >> 3) & 1);
+        ldsm_x4(k_base + sw_off(kr, kc), kb);
+        mma_f16(s[0], qa, kb[0], kb[1]);
+        mma_f16(s[0], ql, kb[0], kb[1]);
+        mma_f16(s[1], qa, kb[2], kb[3]);
+        mma_f16(s[1], ql, kb[2], kb[3]);
+      }
+      // scale, mask, online softmax per row (the 4 lanes of a quad share a row)
+      float p[2][4];
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        float x[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int pos = t0 + wp0 + (j >> 1) * 8 + 2 * tig + (j & 1);
+          const bool live = pos < p_hi && pos <= row_pos[hr];
+          x[j] = live ? s[j >> 1][2 * hr + (j & 1)] * qscale : -INFINITY;
+        }
+        float tmax = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
+        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
+        const float nmax = fmaxf(mx[hr], tmax);
+        float corr = 1.0f, psum = 0.0f;
+        if (nmax == -INFINITY) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) p[hr][j] = 0.0f;
+        } else {
+          corr = expf(mx[hr] - nmax);  // 0 on the row's first live tile
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            p[hr][j] = x[j] == -INFINITY ? 0.0f : expf(x[j] - nmax);
+            psum += p[hr][j];
+          }
+          mx[hr] = nmax;
+        }
+        psum += __shfl_xor_sync(0xffffffffu, psum, 1);
+        psum += __shfl_xor_sync(0xffffffffu, psum, 2);
+        sm[hr] = sm[hr] * corr + psum;
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+          o[n][2 * hr] *= corr;
+          o[n][2 * hr + 1] *= corr;
+        }
+      }
+      // P as the A operand (rows = vectors, k = the 16 positions), hi and lo
+      uint32_t ph[4], pl[4];
+      split_f16x2(p[0][0], p[0][1], ph[0], pl[0]);  // row gid,     positions 2tig..
+      split_f16x2(p[1][0], p[1][1], ph[1], pl[1]);  // row gid + 8
+      split_f16x2(p[0][2], p[0][3], ph[2], pl[2]);  // row gid,     positions 8 + 2tig..
+      split_f16x2(p[1][2], p[1][3], ph[3], pl[3]);  // row gid + 8
+      // O += P . V, 16 dims (two n-tiles) per ldmatrix
+#pragma unroll
+      for (int q = 0; q < kD / 16; ++q) {
+        uint32_t vb[4];
+        const int vr = wp0 + (lane & 7) + ((lane >> 3) & 1) * 8, vc = 2 * q + (lane >> 4);
+        ldsm_x4_t(v_base + sw_off(vr, vc), vb);
+        mma_f16(o[2 * q], ph, vb[0], vb[1]);
+        mma_f16(o[2 * q], pl, vb[0], vb[1]);
+        mma_f16(o[2 * q + 1], ph, vb[2], vb[3]);
+        mma_f16(o[2 * q + 1], pl, vb[2], vb[3]);
+      }
+    }
+    // merge the 8 warps' running states (warp order) and write this split's
+    // partial of every vector of the pass
+    __syncthreads();  // the tiles are consumed: their memory holds the merge
+    if (tig == 0) {
+      s_ml[(warp * 16 + gid) * 2] = mx[0];
+      s_ml[(warp * 16 + gid) * 2 + 1] = sm[0];
+      s_ml[(warp * 16 + gid + 8) * 2] = mx[1];
+      s_ml[(warp * 16 + gid + 8) * 2 + 1] = sm[1];
+    }
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      *reinterpret_cast<float2*>(s_acc + (warp * 16 + gid) * kAccStride + 8 * n + 2 * tig) =
+          make_float2(o[n][0], o[n][1]);
+      *reinterpret_cast<float2*>(s_acc + (warp * 16 + gid + 8) * kAccStride + 8 * n + 2 * tig) =
+          make_float2(o[n][2], o[n][3]);
+    }
+    __syncthreads();
+    {
+      const int r = threadIdx.x >> 4, d0 = (threadIdx.x & 15) * 8;
+      float gmax = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kAWarps; ++w) gmax = fmaxf(gmax, s_ml[(w * 16 + r) * 2]);
+      float den = 0.0f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int w = 0; w < kAWarps; ++w) {
+        const float mw = s_ml[(w * 16 + r) * 2];
+        const float c = (gmax == -INFINITY || mw == -INFINITY) ? 0.0f : expf(mw - gmax);
+        den = fmaf(c, s_ml[(w * 16 + r) * 2 + 1], den);
+        const float* src = s_acc + (w * 16 + r) * kAccStride + d0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = fmaf(c, src[i], acc[i]);
+      }
+      const int v = v0 + r;
+      if (v < NV) {
+        const int m = v / G, h = v % G;
+        float* pp = a.part + ((size_t(m) * a.Hq + size_t(g) * G + h) * a.nsplit + split) * kPartStride;
+        *reinterpret_cast<float4*>(pp + d0) =
+            make_float4(acc[0] * vs, acc[1] * vs, acc[2] * vs, acc[3] * vs);
+        *reinterpret_cast<float4*>(pp + d0 + 4) =
+            make_float4(acc[4] * vs, acc[5] * vs, acc[6] * vs, acc[7] * vs);
+        if (d0 == 0) {
+          pp[kD] = gmax;
+          pp[kD + 1] = den;
+        }
+      }
+    }
+  }
+  // the merge kernel (launched with programmatic serialization) may start
+  // its prologue; it waits for this grid's memory before reading partials
+  tc::grid_dep_launch();
+}
+
+// One CTA of 256 threads per (row, head): o = sum_j acc_j e^(max_j - M) /
+// sum_j sum_j e^(max_j - M), M the largest split maximum.  A row whose base
+// position lies outside the cache has no live position and gets zeros.  The
+// 8 warps take every 8th split (each lane 4 dims), so each thread issues its
+// few accumulator loads at once; the 8 partial sums are added in warp order.
+constexpr int kMaxSplits = 1024;
+constexpr int kMergeThreads = 256;
+
+__global__ void __launch_bounds__(kMergeThreads) attn_merge_kernel(AttnArgs a_all) {
+  tc::grid_dep_wait();  // the partials come from the previous kernel
+  const AttnArgs a = for_sequence(a_all, blockIdx.z);
+  const int m = blockIdx.x, h = blockIdx.y;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const float* pp = a.part + (size_t(m) * a.Hq + h) * a.nsplit * size_t(kPartStride);
-  // every split's (max, sum) staged in shared memory by the whole block, the
-  // largest maximum by a block reduction, then each split's weight
-  // e^(max_j - M); the accumulators are read with independent loads
   __shared__ float s_c[kMaxSplits], s_den[kMaxSplits];
-  __shared__ float s_red[kD / 32];
+  __shared__ float s_red[kMergeThreads / 32];
+  __shared__ __align__(16) float s_acc[kMergeThreads / 32][kD];
   float lmax = -INFINITY;
-  for (int j = d; j < a.nsplit; j += kD) {
+  for (int j = t; j < a.nsplit; j += kMergeThreads) {
     s_c[j] = pp[j * kPartStride + kD];
     s_den[j] = pp[j * kPartStride + kD + 1];
     lmax = fmaxf(lmax, s_c[j]);
   }
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, off));
-  if ((d & 31) == 0) s_red[d >> 5] = lmax;
+  if (lane == 0) s_red[warp] = lmax;
   __syncthreads();
   float gmax = s_red[0];
 #pragma unroll
-  for (int w = 1; w < kD / 32; ++w) gmax = fmaxf(gmax, s_red[w]);
-  for (int j = d; j < a.nsplit; j += kD)
+  for (int w = 1; w < kMergeThreads / 32; ++w) gmax = fmaxf(gmax, s_red[w]);
+  for (int j = t; j < a.nsplit; j += kMergeThreads)
     s_c[j] = (gmax == -INFINITY || s_c[j] == -INFINITY) ? 0.0f : expf(s_c[j] - gmax);
   __syncthreads();
-  float num = 0.0f, den = 0.0f;
-#pragma unroll 8
-  for (int j = 0; j < a.nsplit; ++j) {
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+  for (int j = warp; j < a.nsplit; j += kMergeThreads / 32) {
     const float c = s_c[j];
-    num = fmaf(pp[j * kPartStride + d], c, num);
-    den = fmaf(s_den[j], c, den);
+    const float4 v = *reinterpret_cast<const float4*>(pp + j * kPartStride + 4 * lane);
+    acc.x = fmaf(v.x, c, acc.x);
+    acc.y = fmaf(v.y, c, acc.y);
+    acc.z = fmaf(v.z, c, acc.z);
+    acc.w = fmaf(v.w, c, acc.w);
   }
-  a.o[(size_t(m) * a.Hq + h) * kD + d] = den > 0.0f ? num / den : 0.0f;
+  *reinterpret_cast<float4*>(&s_acc[warp][4 * lane]) = acc;
+  __syncthreads();
+  if (t < kD) {
+    float num = 0.0f, den = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kMergeThreads / 32; ++w) num += s_acc[w][t];
+    for (int j = 0; j < a.nsplit; ++j) den = fmaf(s_den[j], s_c[j], den);
+    a.o[(size_t(m) * a.Hq + h) * kD + t] = den > 0.0f ? num / den : 0.0f;
+  }
 }
 
-// Split layout from max_pos: about two CTAs per SM over the KV heads, at
-// least one 32-position tile per split.
+// Split layout from max_pos: about one CTA per SM over the KV heads and
+// sequences (one wave), splits a multiple of 16 positions (one warp's share of
+// a tile).
 void split_layout(int max_pos, int Hkv, int n_seq, int& nsplit, int& chunk) {
   const int per = Hkv * n_seq;  // CTAs per split
-  const int target = (2 * 148 + per - 1) / per;
+  const int target = (148 + per - 1) / per;
   chunk = (max_pos + target - 1) / target;
-  chunk = (chunk + kTile - 1) / kTile * kTile;
-  if (chunk < kTile) chunk = kTile;
+  chunk = (chunk + 15) / 16 * 16;
   nsplit = (max_pos + chunk - 1) / chunk;
 }
 
@@ -463,11 +640,21 @@ extern "C" int mfi_attn_decode_batched(const void* q, const uint8_t* kvk, const 
   cudaError_t e = mfi::ensure_dynamic_smem(reinterpret_cast<const void*>(mfi::attn_partial_kernel),
                                            mfi::kAttnSmem);
   if (e != cudaSuccess) return mfi::set_last_error(MFI_ERR_CUDA, cudaGetErrorString(e));
-  mfi::attn_partial_kernel<<<dim3(a.nsplit, Hkv, n_seq), mfi::kThreads, mfi::kAttnSmem, st>>>(a);
+  mfi::attn_partial_kernel<<<dim3(a.nsplit, Hkv, n_seq), mfi::kAThreads, mfi::kAttnSmem, st>>>(a);
   e = cudaGetLastError();
   if (e == cudaSuccess) {
-    mfi::attn_merge_kernel<<<dim3(M, Hq, n_seq), mfi::kD, 0, st>>>(a);
-    e = cudaGetLastError();
+    // programmatic serialization: the merge grid is scheduled while the
+    // partial kernel finishes and waits (griddepcontrol) for its memory
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(M, Hq, n_seq);
+    cfg.blockDim = dim3(mfi::kMergeThreads);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, mfi::attn_merge_kernel, a);
   }
   return e == cudaSuccess ? MFI_OK
                           : mfi::set_last_error(MFI_ERR_CUDA, cudaGetErrorString(e));

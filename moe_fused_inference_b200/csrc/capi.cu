@@ -717,8 +717,29 @@ int mfi_moe_layer_ex(const mfi_moe_weights* w, const void* x_bf16, int T, float*
 // Routing alone and expert compute on pre-routed rows: the two halves of
 // mfi_moe_layer that expert parallelism puts a token exchange between.
 
+namespace {
+// Scratch of the tensor-core router (route_tc.cu) for T tokens: the int8 token
+// tiles (T rounded up to 128 rows x hidden bytes) and the int8 router blocks
+// (n_experts x hidden bytes); 0 where that router does not apply.
+size_t route_tc_scratch(int T, int H, int E) {
+  if (T < 512 || E != 128 || H < 128 || H % 128 != 0) return 0;
+  return (size_t(T) + 127) / 128 * 128 * size_t(H) + size_t(E) * H + 512;
+}
+}  // namespace
+
+size_t mfi_moe_route_workspace_bytes(int T, int hidden, int n_experts) {
+  if (T < 0 || hidden <= 0 || n_experts <= 0) return 0;
+  return route_tc_scratch(T, hidden, n_experts);
+}
+
 int mfi_moe_route(const mfi_moe_weights* w, const void* x_bf16, int T, uint8_t* xq, uint8_t* xsc,
                   int32_t* topi, float* topw, float* logits, void* stream) {
+  return mfi_moe_route_ex(w, x_bf16, T, xq, xsc, topi, topw, logits, nullptr, 0, stream);
+}
+
+int mfi_moe_route_ex(const mfi_moe_weights* w, const void* x_bf16, int T, uint8_t* xq,
+                     uint8_t* xsc, int32_t* topi, float* topw, float* logits, void* workspace,
+                     size_t workspace_bytes, void* stream) {
   if (!w) return fail(MFI_ERR_ARG, "null weights");
   const int E = w->n_experts, H = w->hidden, k = w->top_k;
   if (E <= 0 || E > mfi::kRouteMaxE) return fail(MFI_ERR_ARG, "n_experts must be in [1, 256]");
@@ -742,6 +763,15 @@ int mfi_moe_route(const mfi_moe_weights* w, const void* x_bf16, int T, uint8_t* 
   ra.logit_bias = w->logit_bias;
   ra.norm_w = static_cast<const __nv_bfloat16*>(w->norm_weight);
   ra.norm_eps = w->norm_eps;
+  // many tokens: one token per warp, or the tensor-core router when the
+  // caller gave its scratch
+  ra.batch = T >= 512;
+  const size_t need = route_tc_scratch(T, H, E);
+  if (need && workspace && workspace_bytes >= need &&
+      (reinterpret_cast<uintptr_t>(workspace) & 255) == 0) {
+    ra.x8 = static_cast<uint8_t*>(workspace);
+    ra.r8 = ra.x8 + (size_t(T) + 127) / 128 * 128 * size_t(H);
+  }
   // no work lists, no expert regions: the kernel stops after the routing
   return cuda_status(mfi::launch_route(ra, as_stream(stream)), "moe_route launch");
 }

@@ -179,6 +179,7 @@ class CudaEPOps:
         self._exp_w.prepared = self.prepared.data_ptr()
         _lib.check(lib.mfi_moe_prepare(ctypes.byref(self._exp_w), self.prepared.data_ptr(), nprep,
                                        _stream(dev)), "moe_prepare")
+        self.route_ws = None
         self.R = world * (capacity + 1)
         nws = int(lib.mfi_moe_experts_workspace_bytes(self.R, H, Mi, El, top_k))
         # zero once: the peer-memory transport keeps its counters here between
@@ -187,10 +188,18 @@ class CudaEPOps:
 
     def route(self, x, xq, xsc, topi, topw, logits=None):
         T = x.shape[0]
-        _lib.check(self.lib.mfi_moe_route(ctypes.byref(self._route_w), x.data_ptr(), T,
-                                          xq.data_ptr(), xsc.data_ptr(), topi.data_ptr(),
-                                          topw.data_ptr(), 0 if logits is None else logits.data_ptr(),
-                                          _stream(x.device)), "moe_route")
+        nws = int(self.lib.mfi_moe_route_workspace_bytes(T, self.H, self.shard.n_experts))
+        if nws and (self.route_ws is None or self.route_ws.numel() < nws):
+            # the tensor-core router's scratch (prefill-sized batches)
+            self.route_ws = torch.empty(nws, dtype=torch.uint8, device=x.device)
+        ws = self.route_ws if nws else None
+        _lib.check(self.lib.mfi_moe_route_ex(ctypes.byref(self._route_w), x.data_ptr(), T,
+                                             xq.data_ptr(), xsc.data_ptr(), topi.data_ptr(),
+                                             topw.data_ptr(),
+                                             0 if logits is None else logits.data_ptr(),
+                                             0 if ws is None else ws.data_ptr(),
+                                             0 if ws is None else ws.numel(),
+                                             _stream(x.device)), "moe_route")
 
     def pack(self, xq, xsc, topi, topw, T, counts, send, pack_pos):
         _lib.check(self.lib.mfi_ep_pack(xq.data_ptr(), xsc.data_ptr(), topi.data_ptr(),

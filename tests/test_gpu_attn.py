@@ -164,3 +164,55 @@ def test_kv_write_attn_graph_replay_with_moving_position():
         want = oa.attn_decode(q32.float().cpu().numpy()[None], kc, vc, step)
         assert max_rel_err(o32.cpu().numpy(), want) <= 2e-5
     del g
+
+
+@pytest.mark.parametrize("scaled", [False, True])
+def test_attn_decode_every_byte_code(scaled):
+    """Caches of uniformly random bytes, so every E4M3 code occurs —
+    exponent fields 0 and 15 included, where the reference's decoder differs
+    from the standard one (m 2^-6, 448 (1 + m/8)).  Small queries keep the
+    scores moderate for the 2e-5 bound.  With scales the standard format has
+    no value for 0x7F / 0xFF (NaN), so those bytes are left out."""
+    rng = np.random.default_rng(77 + scaled)
+    M, base, max_pos, Hq, Hkv, D = 2, 300, 400, 32, 4, 128
+    kvk = rng.integers(0, 256, (max_pos, Hkv, D)).astype(np.uint8)
+    kvv = rng.integers(0, 256, (max_pos, Hkv, D)).astype(np.uint8)
+    ks = vs = None
+    if scaled:
+        for c in (kvk, kvv):
+            c[(c & 0x7F) == 0x7F] = 0x11
+        ks = np.array([0.5, 0.25, 1.0, 2.0], np.float32)
+        vs = np.array([0.125, 1.0, 0.5, 4.0], np.float32)
+    q = torch.from_numpy(rng.standard_normal((M, Hq, D)).astype(np.float32) * 0.01).bfloat16().cuda()
+    kw = {} if not scaled else {"k_scale": torch.from_numpy(ks), "v_scale": torch.from_numpy(vs)}
+    o = fp4_ext.get_decode_ext().attn_decode(q, torch.from_numpy(kvk).cuda(),
+                                             torch.from_numpy(kvv).cuda(), _dpos(base), None, M,
+                                             **kw)
+    torch.cuda.synchronize()
+    want = oa.attn_decode(q.float().cpu().numpy(), kvk, kvv, base, k_scale=ks, v_scale=vs)
+    assert max_rel_err(o.cpu().numpy(), want) <= 2e-5
+
+
+def test_attn_decode_batched_sequences():
+    """mfi_attn_decode_batched: 6 sequences with their own caches (stride
+    between them) and one device position, M = 3 rows each, as the batched
+    model runner calls it; every sequence equals its single-sequence oracle."""
+    rng = np.random.default_rng(5)
+    S, M, base, max_pos, Hq, Hkv, D = 6, 3, 700, 720, 32, 4, 128
+    caches = [_cache(rng, max_pos, Hkv, D, base + M) for _ in range(S)]
+    kvk = torch.from_numpy(np.stack([c[0] for c in caches])).cuda()
+    kvv = torch.from_numpy(np.stack([c[1] for c in caches])).cuda()
+    q = torch.from_numpy(rng.standard_normal((S, M, Hq, D)).astype(np.float32)).bfloat16().cuda()
+    o = torch.empty((S, M, Hq, D), dtype=torch.float32, device="cuda")
+    lib = _lib.load()
+    nws = int(lib.mfi_attn_decode_batched_workspace_bytes(S, M, Hq, Hkv, D, max_pos))
+    ws = torch.empty(nws, dtype=torch.uint8, device="cuda")
+    st = lib.mfi_attn_decode_batched(q.data_ptr(), kvk.data_ptr(), kvv.data_ptr(),
+                                     max_pos * Hkv * D, _dpos(base).data_ptr(), o.data_ptr(), S, M,
+                                     Hq, Hkv, D, max_pos, None, None, ws.data_ptr(), nws, None)
+    assert st == 0, lib.mfi_last_error()
+    torch.cuda.synchronize()
+    qn = q.float().cpu().numpy()
+    for s in range(S):
+        want = oa.attn_decode(qn[s], caches[s][0], caches[s][1], base)
+        assert max_rel_err(o[s].cpu().numpy(), want) <= 2e-5
