@@ -292,7 +292,8 @@ class Runner:
         the draft_len tokens that followed the last earlier occurrence of the
         current n-gram, verified in one forward of 1 + draft_len rows; the
         longest agreeing prefix plus the model's own next token are kept.
-        Returns (token ids, verify forwards, drafted tokens accepted)."""
+        Returns (token ids, verify forwards, drafted tokens accepted);
+        ``self.spec_stats`` also counts the drafted tokens proposed."""
         assert self.B == 1
         self.prefill(prompt)
         hist = [int(t) for t in prompt[0]]
@@ -302,7 +303,7 @@ class Runner:
         first = {}
         for i in range(len(hist) - n_gram + 1):
             first.setdefault(tuple(hist[i:i + n_gram]), i)
-        forwards = accepted = 0
+        forwards = accepted = drafted = 0
         while len(hist) - P < steps:
             tail = tuple(hist[-n_gram:])
             j = first.get(tail)
@@ -312,6 +313,7 @@ class Runner:
             logits, _ = self.forward(ids, pos - 1)
             am = logits[0].argmax(-1).tolist()
             forwards += 1
+            drafted += len(drafts)
             a = 0
             while a < len(drafts) and am[a] == drafts[a]:
                 a += 1
@@ -322,6 +324,7 @@ class Runner:
                 if len(hist) >= n_gram:
                     first.setdefault(tuple(hist[-n_gram:]), len(hist) - n_gram)
             pos += len(new)
+        self.spec_stats = {"forwards": forwards, "drafted": drafted, "accepted": accepted}
         return torch.tensor(hist[P:P + steps]), forwards, accepted
 
 
