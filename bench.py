@@ -1037,7 +1037,11 @@ def run_ep(args, world, rank, local):
             uniq += int(torch.unique(ids[ids >= 0]).numel())
     w_bytes = uniq * EXPERT_BYTES
     peak, peak_kind = measured_peaks()
-    achieved = w_bytes / (experts_ms / 1e3) / 1e9
+    # the rate of the rank's local expert weights over the device-timed step
+    # (graph replay, max over ranks): the eager stage times below include
+    # each rank's waits on the other ranks' launches, so they cannot serve as
+    # the kernel's duration
+    achieved = w_bytes / (ms_per_step / 1e3) / 1e9
     stats = torch.tensor([achieved, experts_ms, rows_recv / NL, uniq / NL] + stage_ms,
                          dtype=torch.float64, device=dev)
     allstats = [torch.zeros_like(stats) for _ in range(world)]
@@ -1103,10 +1107,12 @@ def run_ep(args, world, rank, local):
         # per layer: p2p route+dispatch, scatter, experts, combine+return, unpack;
         # nccl: route, pack, header, mask, scatter, experts, combine, unpack (+ NCCL's own)
         "gpu_launches": (5 if args.ep_transport == "p2p" else 8) * NL * args.steps,
-        "roofline": {"bound": "hbm", "kernel": "mfi_moe_experts (scatter, gate/up, down, combine)",
+        "roofline": {"bound": "hbm", "kernel": "expert-parallel layer (local expert weights)",
                      "achieved": float(allstats[worst, 0]), "peak": peak, "unit": "GB/s",
                      "frac": float(allstats[worst, 0]) / peak, "peak_kind": peak_kind,
-                     "rank": worst, "experts_ms_per_step": float(allstats[worst, 1]),
+                     "basis": "local expert weight bytes per step / device-timed step "
+                              "(max over ranks), lowest rank",
+                     "rank": worst, "experts_ms_per_step_eager": float(allstats[worst, 1]),
                      "traffic": None},
         # one eager step with events between the calls (plain launches; each
         # call's time includes its waits on the other ranks)
