@@ -431,14 +431,16 @@ __global__ void __launch_bounds__(kPThreads, 1)
         // this warp takes h block `half` (outputs half*32 .. +31) whole, so
         // the block maximum needs no exchange with another warp
         // h goes through this warp's staging tile in shared memory (lane l
-        // keeps its 32 values in its own 128-byte row, element i at word
-        // i ^ l, so neither pass has bank conflicts), and gate / up come in
-        // loads of 4 columns: the SwiGLU pass and the quantisation pass then
-        // each hold only a few values, and the warp stays within the 96
-        // registers a thread of this 18-warp block has, without spilling
-        float* hs = reinterpret_cast<float*>(out_stage + ew * kPOutStage) + lane * 32;
+        // keeps its 32 values in its own 128-byte row, 16-byte chunk c at
+        // chunk c ^ (l & 7), so the 16-byte stores and loads of both passes
+        // are free of bank conflicts), and gate / up come in loads of 4 TMEM
+        // columns: the SwiGLU pass and the quantisation pass each hold only a
+        // few values, and the warp stays within the 96 registers a thread of
+        // this 18-warp block has, without spilling.  The block maximum uses a
+        // NaN-propagating max, so a NaN anywhere in the block gives code 127
+        // (scale 1), like quant_group8.
+        float4* hs4 = reinterpret_cast<float4*>(out_stage + ew * kPOutStage) + lane * 8;
         float am = 0.0f;
-        bool nan = false;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           uint32_t gq[4], u[4];
@@ -450,20 +452,25 @@ __global__ void __launch_bounds__(kPThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
           }
+          float h[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const float h = swiglu(__uint_as_float(gq[i]), __uint_as_float(u[i]));
-            hs[(q * 4 + i) ^ lane] = h;
-            am = fmaxf(am, fabsf(h));
-            nan |= (h != h);
+            h[i] = swiglu(__uint_as_float(gq[i]), __uint_as_float(u[i]));
+            am = fmax_nan(am, fabsf(h[i]));
           }
+          hs4[q ^ (lane & 7)] = make_float4(h[0], h[1], h[2], h[3]);
         }
-        // a NaN anywhere in the block gives code 127, like quant_group8
-        const BlockScale bs = block_scale(nan ? __uint_as_float(0x7fc00000u) : am);
+        const BlockScale bs = block_scale(am);
         uint32_t w[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          w[i >> 3] |= quant_nibble(hs[i ^ lane], bs.inv) << (4 * (i & 7));
+        for (int c = 0; c < 8; ++c) {
+          const float4 v = hs4[c ^ (lane & 7)];
+          const int i = 4 * c;
+          w[i >> 3] |= (quant_nibble(v.x, bs.inv) << (4 * (i & 7))) |
+                       (quant_nibble(v.y, bs.inv) << (4 * ((i + 1) & 7))) |
+                       (quant_nibble(v.z, bs.inv) << (4 * ((i + 2) & 7))) |
+                       (quant_nibble(v.w, bs.inv) << (4 * ((i + 3) & 7)));
+        }
         if (valid) {
           *reinterpret_cast<uint4*>(p.hp + size_t(row) * (p.inter / 2) + tile * 32 + half * 16) =
               make_uint4(w[0], w[1], w[2], w[3]);

@@ -154,6 +154,13 @@ __device__ __forceinline__ float swiglu(float g, float u) {
   return __fmul_rn(swiglu_quotient(g), u);
 }
 
+// max(a, b) that returns NaN when either is NaN (PTX max.NaN).
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
 // 2^e as float for e in the normal range; ldexpf outside it.
 __device__ __forceinline__ float exp2i(int e) {
   if (e >= -126 && e <= 127) return __uint_as_float(uint32_t(e + 127) << 23);
