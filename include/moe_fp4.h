@@ -192,9 +192,9 @@ int mfi_kv_write(const void* k, const void* v, uint8_t* kvk, uint8_t* kvv, const
  * o fp32 (M, Hq, D) = softmax(q k^T / sqrt(D)) v with the cache decoded by the
  * reference's decoder (scales NULL) or as standard e4m3fn times the per-head
  * scales.  A row with no live position gets zeros.  D must be 128 and
- * Hq / Hkv <= 16.  The positions are split over the grid; the partial
- * results need mfi_attn_decode_workspace_bytes() of workspace (16-byte
- * aligned).
+ * Hq / Hkv <= 16.  q, kvk, kvv, o and the workspace must be 16-byte
+ * aligned.  The positions are split over the grid; the partial results need
+ * mfi_attn_decode_workspace_bytes() of workspace.
  * Replaces mxfp4v2::launch_attn_decode_v2 (src/ext/mxfp4_decode.cu:424-437),
  * bound by attn_decode() (src/ext/mxfp4_decode_binding.cpp:213-230), whose
  * score buffer `sc` this library does not need. */
@@ -207,7 +207,7 @@ int mfi_attn_decode(const void* q, const uint8_t* kvk, const uint8_t* kvv, const
  * reference counterpart: the reference decodes one sequence per call):
  * sequence s has q rows [s*M, (s+1)*M) of q (n_seq*M, Hq, D), its cache at
  * kvk/kvv + s * kv_seq_stride bytes (kv_seq_stride >= max_pos*Hkv*D, a
- * multiple of 4) and o rows [s*M, (s+1)*M). */
+ * multiple of 16) and o rows [s*M, (s+1)*M). */
 size_t mfi_attn_decode_batched_workspace_bytes(int n_seq, int M, int Hq, int Hkv, int D,
                                                int max_pos);
 int mfi_attn_decode_batched(const void* q, const uint8_t* kvk, const uint8_t* kvv,

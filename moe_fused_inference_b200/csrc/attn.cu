@@ -610,12 +610,13 @@ extern "C" int mfi_attn_decode_batched(const void* q, const uint8_t* kvk, const 
     return mfi::set_last_error(MFI_ERR_ARG, "null pointer");
   if ((k_scale == nullptr) != (v_scale == nullptr))
     return mfi::set_last_error(MFI_ERR_ARG, "attn_decode: give both scales or neither");
-  if ((reinterpret_cast<uintptr_t>(kvk) & 3) || (reinterpret_cast<uintptr_t>(kvv) & 3) ||
-      (kv_seq_stride & 3) || (reinterpret_cast<uintptr_t>(o) & 15) ||
-      (reinterpret_cast<uintptr_t>(workspace) & 15))
+  // the partial kernel reads q, K and V rows in 16-byte loads
+  if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(kvk) & 15) ||
+      (reinterpret_cast<uintptr_t>(kvv) & 15) || (kv_seq_stride & 15) ||
+      (reinterpret_cast<uintptr_t>(o) & 15) || (reinterpret_cast<uintptr_t>(workspace) & 15))
     return mfi::set_last_error(MFI_ERR_ARG,
-                               "attn_decode: kvk, kvv and the sequence stride 4-byte, o and the "
-                               "workspace 16-byte aligned");
+                               "attn_decode: q, kvk, kvv, o, the workspace and the sequence "
+                               "stride must be 16-byte aligned");
   if (n_seq > 1 && kv_seq_stride < (long long)max_pos * Hkv * D)
     return mfi::set_last_error(MFI_ERR_ARG, "attn_decode: sequence caches overlap");
   if (workspace_bytes < mfi_attn_decode_batched_workspace_bytes(n_seq, M, Hq, Hkv, D, max_pos))
