@@ -76,11 +76,14 @@ def parse():
     ap.add_argument("--tokens", type=int, default=64, help="decode tokens per GPU (T)")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="distinct MoE layers per step (48 = the model; fewer for profiling)")
-    ap.add_argument("--workload", choices=["decode", "prefill", "linear"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "linear", "model"],
+                    default="decode",
                     help="decode (BASELINE config 2, the headline, with every other "
                          "configuration in the same line), prefill (config 3 alone: T = 16384 "
-                         "by default, Zipf(1.2)-skewed routing) or linear (the static decode "
-                         "projections and lm_head through lin_pq)")
+                         "by default, Zipf(1.2)-skewed routing), linear (the static decode "
+                         "projections and lm_head through lin_pq) or model (config 4: greedy "
+                         "decode of the 48-layer synthetic model at batch 1 / 16 / 64, each "
+                         "step one CUDA graph)")
     ap.add_argument("--headline-only", action="store_true",
                     help="decode: skip the sweep, prefill, drop-in and T=4 blocks")
     ap.add_argument("--zipf-alpha", type=float, default=0.5,
@@ -790,7 +793,70 @@ def run_linear(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def run_model(args, world, rank, local):
+    """the random-init 48-layer Qwen3-30B-A3B-shaped model
+    on the library (model.py), 1024-token prompts with the repeated motif,
+    then greedy decode steps, each replayed from one CUDA graph
+    (GraphDecoder), at batch 1, 16 and 64.  Decode tokens/s = batch x steps /
+    the device time of the steps; the eager step time is reported beside it."""
+    from moe_fused_inference_b200.model import (GraphDecoder, LibBackend, QwenConfig, Runner,
+                                                SyntheticQwen, synthetic_prompts)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    stream = torch.cuda.current_stream(dev)
+    t0 = time.time()
+    model = SyntheticQwen.build(QwenConfig(), seed=1, device=dev)
+    lib = LibBackend(model)
+    torch.cuda.synchronize(dev)
+    build_s = time.time() - t0
+    P, S = 1024, max(args.steps, 8)
+    per = {}
+    sampler = ClockSampler(dev.index if dev.index is not None else 0)
+    sampler.start()
+    for B in (1, 16, 64):
+        prompt = synthetic_prompts(B, P, model.cfg.vocab, seed=101 + B, device=dev)
+        runner = Runner(model, lib, B, P + S + 8)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        runner.prefill(prompt)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        prefill_ms = e0.elapsed_time(e1)
+        # eager decode steps (for comparison), then the graph
+        pos = P - 1
+        last = prompt[:, -1:]
+        eager_ms = event_time(dev, stream, lambda: runner.forward(last, pos, last_only=True), 3) / 3
+        gd = GraphDecoder(runner, S)
+        gd.start(prompt, prefill=False)
+        ms = event_time(dev, stream, lambda: gd.decode(S), 1)
+        per[f"B{B}"] = {"decode_tokens_per_s": B * S / (ms / 1e3), "ms_per_step": ms / S,
+                        "eager_ms_per_step": eager_ms, "steps": S,
+                        "prefill_ms": prefill_ms, "prefill_tokens_per_s": B * (P - 1) / (prefill_ms / 1e3)}
+        del gd, runner
+        torch.cuda.empty_cache()
+    clocks = sampler.stop()
+    if rank != 0:
+        return
+    line = {
+        "metric": "config 4 greedy decode tokens/s (48-layer synthetic Qwen3-30B-A3B)",
+        "value": per["B64"]["decode_tokens_per_s"], "unit": "tokens/s", "n_gpus": 1,
+        "steps": S, "warmup": 1, "ms_per_step": per["B64"]["ms_per_step"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "mxfp4 experts and projections, bf16 activations, FP8 KV cache",
+        "data": "synthetic (random-init weights, uniform random prompts with a repeated "
+                "32-token motif, seeded)",
+        "config": {"workload": "config 4: 48 layers, 32/4 heads, head_dim 128, vocab 151936, "
+                               "128 experts top-8; 1024-token prompts, greedy decode",
+                   "step": "one decode step of B sequences, replayed from one CUDA graph "
+                           "(GraphDecoder); prefill in 64-token chunks, eager",
+                   "model_build_s": build_s},
+        "per_batch": per, "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_ours(args, world, rank, local):
+    if args.workload == "model":
+        return run_model(args, world, rank, local)
     if args.workload == "prefill":
         return run_prefill(args, world, rank, local)
     if args.workload == "linear":

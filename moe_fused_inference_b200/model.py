@@ -79,6 +79,17 @@ def apply_rope(x: torch.Tensor, positions: torch.Tensor, theta: float) -> torch.
 
 
 _E2M1 = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0]
+_E2M1_DEV: dict = {}
+
+
+def _e2m1_table(device) -> torch.Tensor:
+    """The E2M1 magnitudes on `device` (made once, so the gather can run while
+    a CUDA graph is being captured)."""
+    key = str(device)
+    t = _E2M1_DEV.get(key)
+    if t is None:
+        t = _E2M1_DEV[key] = torch.tensor(_E2M1, device=device)
+    return t
 
 
 def dequant_rows(wp: torch.Tensor, wsc: torch.Tensor, K: int, ids: torch.Tensor) -> torch.Tensor:
@@ -91,8 +102,7 @@ def dequant_rows(wp: torch.Tensor, wsc: torch.Tensor, K: int, ids: torch.Tensor)
     codes[:, 1::2] = (data >> 4) & 0xF
     codes = codes.view(T, kp // 32, 32)
     sign = torch.where((codes & 0x8) != 0, -1.0, 1.0)
-    table = torch.tensor(_E2M1, device=wp.device)
-    vals = table[(codes & 0x7).long()]
+    vals = _e2m1_table(wp.device)[(codes & 0x7).long()]
     scales = torch.exp2(wsc[ids].float() - 127.0)
     return ((sign * vals) * scales[..., None]).reshape(T, kp)[:, :K].to(torch.bfloat16)
 
@@ -169,13 +179,17 @@ class LibBackend:
         """q (B, M, Hq, D) bf16 of B sequences at the same base position,
         kvk/kvv (B, max_pos, Hkv, D) -> (B, M, Hq, D) fp32: one
         mfi_attn_decode_batched launch (the reference's attn_decode per
-        sequence)."""
+        sequence).  `base` is an int or a device int32 tensor of one element
+        (read by the kernel, as in a captured decode step)."""
         from . import _lib
         lib = _lib.load()
         B, _, Hq, D = q.shape
         max_pos, Hkv = kvk.shape[1], kvk.shape[2]
         q = q.contiguous()
-        dpos = torch.full((1,), base, dtype=torch.int32, device=q.device)
+        if torch.is_tensor(base):
+            dpos = base
+        else:
+            dpos = torch.full((1,), base, dtype=torch.int32, device=q.device)
         o = torch.empty((B, M, Hq, D), dtype=torch.float32, device=q.device)
         nws = int(lib.mfi_attn_decode_batched_workspace_bytes(B, M, Hq, Hkv, D, max_pos))
         ws = torch.empty(nws, dtype=torch.uint8, device=q.device)
@@ -208,7 +222,14 @@ class Runner:
         T = B * M
         H, Hq, Hkv, D = cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim
         x = dequant_rows(m.embed[0], m.embed[1], H, ids.reshape(-1))
-        positions = torch.arange(base, base + M, device=ids.device).repeat(B)
+        # `base` may be a device int32 tensor of one element (a captured
+        # decode step): positions and the KV rows then come from the device
+        on_device = torch.is_tensor(base)
+        if on_device:
+            kv_idx = base.long() + torch.arange(M, device=ids.device)
+            positions = kv_idx.repeat(B)
+        else:
+            positions = torch.arange(base, base + M, device=ids.device).repeat(B)
         routing = []
         for L, lw in enumerate(m.layers):
             hp = rms_norm(x, lw.in_norm, cfg.eps)
@@ -223,8 +244,14 @@ class Runner:
             k = apply_rope(k, positions, cfg.rope_theta)
             kb = k.view(B, M, Hkv, D)
             vb = v.view(B, M, Hkv, D)
-            self.kvk[L, :, base:base + M] = kb.to(torch.float8_e4m3fn).view(torch.uint8)
-            self.kvv[L, :, base:base + M] = vb.to(torch.float8_e4m3fn).view(torch.uint8)
+            k8 = kb.to(torch.float8_e4m3fn).view(torch.uint8)
+            v8 = vb.to(torch.float8_e4m3fn).view(torch.uint8)
+            if on_device:
+                self.kvk[L].index_copy_(1, kv_idx, k8)
+                self.kvv[L].index_copy_(1, kv_idx, v8)
+            else:
+                self.kvk[L, :, base:base + M] = k8
+                self.kvv[L, :, base:base + M] = v8
             o = be.attention(q.view(B, M, Hq, D), self.kvk[L], self.kvv[L], base, M)
             of = o.reshape(T, Hq * D).to(torch.bfloat16).contiguous()
             aq, asc = be.prequant(of)
@@ -326,6 +353,75 @@ class Runner:
             pos += len(new)
         self.spec_stats = {"forwards": forwards, "drafted": drafted, "accepted": accepted}
         return torch.tensor(hist[P:P + steps]), forwards, accepted
+
+
+class GraphDecoder:
+    """Greedy decoding of a Runner on the library backend with every decode
+    step replayed from one captured CUDA graph.
+
+    The reference's own graph attempt for its runner failed on the per-layer
+    `.tolist()` of the routing (runtime/model_runner_v2.py:194); with the
+    device-routed MoE layer nothing on the step needs the host, so the whole
+    step — 48 layers of projections, FP8 KV write, attention, MoE block, the
+    lm_head and the argmax — is one graph.  The position lives in a device
+    tensor that the graph advances; each replay feeds the previous step's
+    token and records the new one.  Same kernels in the same order as
+    Runner.greedy, so the tokens are identical (tests/test_gpu_model.py)."""
+
+    def __init__(self, runner: "Runner", max_steps: int):
+        dev = runner.model.final_norm.device
+        B = runner.B
+        self.runner, self.max_steps = runner, max_steps
+        self.ids = torch.zeros((B, 1), dtype=torch.long, device=dev)
+        self.base = torch.zeros((1,), dtype=torch.int32, device=dev)
+        self.step = torch.zeros((1,), dtype=torch.long, device=dev)
+        self.tokens = torch.zeros((B, max_steps), dtype=torch.long, device=dev)
+        self.graph = None
+
+    def _body(self):
+        logits, _ = self.runner.forward(self.ids, self.base, last_only=True)
+        nxt = logits.argmax(-1)
+        self.tokens.index_copy_(1, self.step, nxt[:, None])
+        self.ids.copy_(nxt[:, None])
+        self.base.add_(1)
+        self.step.add_(1)
+
+    def _set(self, last_ids: torch.Tensor, base: int):
+        self.ids.copy_(last_ids)
+        self.base.fill_(base)
+        self.step.zero_()
+
+    def start(self, prompt: torch.Tensor, chunk: int = 64, prefill: bool = True) -> None:
+        """Prefill the prompt (eager; skipped with prefill=False when the
+        runner's caches already hold it) and make the graph of one decode step
+        (captured once, after an eager warm-up step whose KV row and token
+        the replays then write again)."""
+        r = self.runner
+        if prefill:
+            r.prefill(prompt, chunk)
+        pos = prompt.shape[1] - 1
+        dev = self.ids.device
+        if self.graph is None:
+            self._set(prompt[:, -1:], pos)
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                self._body()  # allocates the layers' workspaces, initialises state
+                torch.cuda.synchronize(dev)
+                self.graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(self.graph, stream=side):
+                    self._body()
+            torch.cuda.current_stream(dev).wait_stream(side)
+            torch.cuda.synchronize(dev)
+        self._set(prompt[:, -1:], pos)
+
+    def decode(self, steps: int) -> torch.Tensor:
+        """`steps` greedy tokens (B, steps) after start()."""
+        if steps > self.max_steps:
+            raise RuntimeError(f"at most {self.max_steps} steps")
+        for _ in range(steps):
+            self.graph.replay()
+        return self.tokens[:, :steps]
 
 
 def synthetic_prompts(batch: int, length: int, vocab: int, seed: int = 0, motif: int = 32,

@@ -124,3 +124,22 @@ def test_speculative_decode_is_lossless(model, backends):
           f"{r.spec_stats['drafted']} drafted tokens proposed, {accepted} accepted")
     assert torch.equal(spec.to(greedy.device), greedy[0])
     assert r.spec_stats["drafted"] > 0
+
+
+@pytest.mark.parametrize("batch", [1, 16])
+def test_graph_decode_matches_eager_greedy(model, backends, batch):
+    """Config 4's decode as one captured CUDA graph per step (the device-
+    routed MoE layer leaves nothing on the step for the host; the reference's
+    graph attempt failed on its routing .tolist()): the replayed steps emit
+    exactly the eager greedy tokens."""
+    from moe_fused_inference_b200.model import GraphDecoder
+    lib, _ = backends
+    steps = 24
+    prompt = synthetic_prompts(batch, 256, model.cfg.vocab, seed=31)
+    max_len = 256 + steps + 8
+    greedy, _ = Runner(model, lib, batch, max_len).greedy(prompt, steps)
+    gd = GraphDecoder(Runner(model, lib, batch, max_len), steps)
+    gd.start(prompt)
+    toks = gd.decode(steps)
+    torch.cuda.synchronize()
+    assert torch.equal(toks, greedy)
