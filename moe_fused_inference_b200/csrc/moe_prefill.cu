@@ -49,11 +49,18 @@ constexpr int kPStages = MFI_PF_STAGES;
 // g, g + 2, g + 4, ... of the CTA, so one group's SwiGLU overlaps the other's
 // (no CTA-wide barrier between items).  Inside a group two warps share each
 // TMEM lane quadrant, each taking one 32-element block of h (gate/up) or 64
-// output columns (down) of its 32 token rows.
+// output columns (down) of its 32 token rows.  The last warp publishes the
+// finished h slices of each gate/up item to the down items of every CTA: the
+// epilogue warps hand it each accumulator use through an mbarrier and go on
+// to their next item, so the fences that make h visible at GPU scope (and to
+// the async proxy that reads it) stay off the epilogue's path.
 constexpr int kPEpiWarps = 16;
 constexpr int kPGroups = 2;
 constexpr int kPGroupWarps = kPEpiWarps / kPGroups;
-constexpr int kPThreads = 64 + 32 * kPEpiWarps;
+constexpr int kPPubWarp = 2 + kPEpiWarps;
+constexpr int kPThreads = 64 + 32 * kPEpiWarps + 32;
+// publisher hand-off markers (besides a gate/up item's tile index)
+constexpr int kPubDown = -1, kPubStop = -2;
 constexpr int kPTile = 128;                    // token rows per tile (MMA M)
 constexpr int kPA = 16384;                     // 128 token rows x 128 B
 constexpr int kPSF = 1024;                     // two scale atoms
@@ -207,6 +214,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_empty + kPAccBufs);
   __shared__ int s_item[kPAccBufs];
   __shared__ uint64_t drain[1];  // the MMA issuer's error-path drain
+  // epilogue group -> publisher, one slot per accumulator buffer
+  __shared__ uint64_t pub_full[kPAccBufs], pub_empty[kPAccBufs];
+  __shared__ int pub_tl[kPAccBufs];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_gu = p.inter / 64, tiles_dn = p.hidden / 128;
@@ -223,6 +233,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
       mbar_init(&acc_empty[b], kPGroupWarps);
       mbar_init(&item_full[b], 1);
       mbar_init(&item_empty[b], 1 + kPGroupWarps);  // the MMA thread + one epilogue group
+      mbar_init(&pub_full[b], kPGroupWarps);
+      mbar_init(&pub_empty[b], 1);
     }
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -400,12 +412,44 @@ __global__ void __launch_bounds__(kPThreads, 1)
       }
       if (!ok) drain_mma(drain);
     }
+  } else if (warp == kPPubWarp) {
+    if (lane == 0) {
+      int stops = 0;
+      for (uint32_t acc_it = 0;; ++acc_it) {
+        const uint32_t buf = acc_it % kPAccBufs;
+        if (!mbar_wait(&pub_full[buf], (acc_it / kPAccBufs) & 1, p.err, 3)) break;
+        const int tl = pub_tl[buf];
+        mbar_arrive(&pub_empty[buf]);
+        if (tl == kPubStop) {
+          if (++stops == kPGroups) break;
+          continue;
+        }
+        if (tl >= 0) {
+          // the group's 8 warps wrote their h slices (and released them to
+          // this thread through the barrier): make them visible to the
+          // down items' producers, which read h with TMA
+          fence_proxy_async_global();
+          __threadfence();
+          atomicAdd(p.ready + tl, unsigned(kPGroupWarps));
+          atomicAdd(p.gu_done, unsigned(kPGroupWarps));
+        }
+      }
+    }
   } else {
     const int ew = warp - 2;             // 0..15
     const int quad = warp & 3;           // TMEM lane quadrant of this warp
     const int grp = ew / kPGroupWarps;   // epilogue group
     const int half = (ew >> 2) & 1;      // which half of the tile's columns
     const int r = quad * 32 + lane;      // token row inside the tile
+    // lane 0 hands accumulator use acc_it to the publisher (after the warp's
+    // stores: the __syncwarp before the call orders them)
+    auto hand_off = [&](uint32_t acc_it, int tl) -> bool {
+      const uint32_t buf = acc_it % kPAccBufs;
+      if (!mbar_wait(&pub_empty[buf], ((acc_it / kPAccBufs) & 1) ^ 1, p.err, 3)) return false;
+      pub_tl[buf] = tl;
+      mbar_arrive(&pub_full[buf]);
+      return true;
+    };
     for (uint32_t acc_it = grp;; acc_it += kPGroups) {
       const uint32_t buf = acc_it % kPAccBufs;
       if (!mbar_wait(&item_full[buf], (acc_it / kPAccBufs) & 1, p.err, 3)) break;
@@ -414,6 +458,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
       if (lane == 0) mbar_arrive(&item_empty[buf]);
       if (item < 0) {
         mbar_wait(&acc_full[buf], (acc_it / kPAccBufs) & 1, p.err, 3);
+        if (lane == 0) hand_off(acc_it, kPubStop);
         break;
       }
       bool gu;
@@ -478,15 +523,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
           p.ha[(size_t(row / kPTile) * kc_dn + kb / 4) * 512 + (row % 32) * 16 +
                ((row % kPTile) / 32) * 4 + (kb & 3)] = bs.code;
         }
-        // publish this warp's slice (32 rows x one block) of the tile's h
-        // rows to its down items
+        // this warp's slice (32 rows x one block) of the tile's h rows goes
+        // to the publisher
         __syncwarp();
-        if (lane == 0) {
-          fence_proxy_async_global();
-          __threadfence();
-          atomicAdd(p.ready + tl, 1u);
-          atomicAdd(p.gu_done, 1u);
-        }
+        int handed = 1;
+        if (lane == 0) handed = hand_off(acc_it, tl) ? 1 : 0;
+        if (__shfl_sync(0xffffffffu, handed, 0) == 0) break;
       } else {
         // this warp stores output columns half*64 .. +63 of its token rows in
         // bf16 (each expert's output row is rounded to the activation type,
@@ -525,6 +567,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
                                       chunk * 8) = v;
         }
         __syncwarp();
+        int handed = 1;
+        if (lane == 0) handed = hand_off(acc_it, kPubDown) ? 1 : 0;
+        if (__shfl_sync(0xffffffffu, handed, 0) == 0) break;
       }
     }
   }
