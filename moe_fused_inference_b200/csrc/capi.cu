@@ -198,7 +198,7 @@ int grouped_launch(const mfi::GroupDesc* groups, const int* ng, int P,
     const long long items = (long long)P * ((N + 127) / 128);
     return cuda_status(mfi::launch_grouped_tc(groups, ng, items > (1 << 30) ? (1 << 30) : int(items),
                                               entries, xq, xsc, y, N, Kp,
-                                              mfi::device_error_flag(), s),
+                                              mfi::device_error_flag(), s, true),
                        w.c_str());
   }
   return cuda_status(mfi::launch_grouped_gemv(groups, ng, P, entries, xq, xsc, y, N, Kp,
@@ -235,7 +235,7 @@ int mfi_moe_gateup(const uint8_t* xq, const uint8_t* xsc, const uint8_t* const* 
   auto* entries = c.take<mfi::EntryDesc>(P);
   cudaStream_t s = as_stream(stream);
   int st = cuda_status(mfi::launch_build_groups(wp_tab, wsc_tab, int(P), 0, E, N, groups, ng,
-                                                entries, s),
+                                                entries, s, true),
                        "moe_gateup grouping launch");
   if (st != MFI_OK) return st;
   return grouped_launch(groups, ng, int(P), entries, xq, xsc, gu, N, Kp, s, "moe_gateup");
@@ -272,11 +272,11 @@ int mfi_moe_down(const float* gu, const uint8_t* const* wp_tab, const uint8_t* c
   uint8_t* hsc = c.take<uint8_t>(P * (Kp / 32));
   cudaStream_t s = as_stream(stream);
   int st = cuda_status(mfi::launch_swiglu_quant(gu, 2L * K, nullptr, int(P), nullptr, hq, hsc, K,
-                                                Kp, s),
+                                                Kp, s, true),
                        "moe_down swiglu launch");
   if (st != MFI_OK) return st;
   st = cuda_status(mfi::launch_build_groups(wp_tab, wsc_tab, int(P), 1, E, N, groups, ng, entries,
-                                            s),
+                                            s, true),
                    "moe_down grouping launch");
   if (st != MFI_OK) return st;
   return grouped_launch(groups, ng, int(P), entries, hq, hsc, yd, N, Kp, s, "moe_down");

@@ -260,6 +260,8 @@ __global__ void __launch_bounds__(kBgThreads) build_groups_kernel(
     const uint8_t* const* __restrict__ wp_tab, const uint8_t* const* __restrict__ wsc_tab, int P,
     int mode, int E, int N, GroupDesc* __restrict__ groups, int* __restrict__ n_groups,
     EntryDesc* __restrict__ entries) {
+  tc::grid_dep_wait();  // the tables may come from the kernel before
+  tc::grid_dep_launch();
   extern __shared__ __align__(16) unsigned char shraw[];
   const uint8_t** s_wp = reinterpret_cast<const uint8_t**>(shraw);  // P
   const uint8_t** s_ws = s_wp + P;                                    // P
@@ -322,7 +324,7 @@ __global__ void __launch_bounds__(kBgThreads) build_groups_kernel(
 
 cudaError_t launch_build_groups(const uint8_t* const* wp_tab, const uint8_t* const* wsc_tab, int P,
                                 int mode, int E, int N, GroupDesc* groups, int* n_groups,
-                                EntryDesc* entries, cudaStream_t stream) {
+                                EntryDesc* entries, cudaStream_t stream, bool pdl) {
   if (P <= 0 || P > 4 * kBgThreads) return cudaErrorInvalidValue;
   const size_t smem = size_t(P) * (2 * sizeof(void*) + 4 * sizeof(int));
   if (smem > 48 * 1024) {
@@ -330,9 +332,18 @@ cudaError_t launch_build_groups(const uint8_t* const* wp_tab, const uint8_t* con
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
   }
-  build_groups_kernel<<<1, kBgThreads, smem, stream>>>(wp_tab, wsc_tab, P, mode, E, N, groups,
-                                                        n_groups, entries);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kBgThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, build_groups_kernel, wp_tab, wsc_tab, P, mode, E, N, groups,
+                            n_groups, entries);
 }
 
 // ---------------------------------------------------------------------------

@@ -114,6 +114,9 @@ __global__ void __launch_bounds__(kGtThreads, 1) grouped_tc_kernel(GtArgs p) {
     cta_abort_init();
   }
   if (warp == 4) tmem_alloc(tmem_slot, kGtTmemCols);
+  // the groups, entries and activation rows come from the kernels before
+  grid_dep_wait();
+  grid_dep_launch();
   // chunk table: every group's rows in chunks of 32, groups in order
   if (warp == 5) {
     const int ng = *p.n_groups;
@@ -326,7 +329,7 @@ bool grouped_tc_supported(int N, int Kp) { return Kp % 256 == 0 && Kp >= 256 && 
 
 cudaError_t launch_grouped_tc(const GroupDesc* groups, const int* n_groups, int max_items,
                               const EntryDesc* entries, const uint8_t* xq, const uint8_t* xsc,
-                              float* y, int N, int Kp, int* err, cudaStream_t stream) {
+                              float* y, int N, int Kp, int* err, cudaStream_t stream, bool pdl) {
   if (!grouped_tc_supported(N, Kp)) return cudaErrorNotSupported;
   cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(grouped_tc_kernel),
                                       grouped_tc_smem());
@@ -336,8 +339,17 @@ cudaError_t launch_grouped_tc(const GroupDesc* groups, const int* n_groups, int 
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int grid = max_items < sms ? (max_items > 0 ? max_items : 1) : sms;
   GtArgs a{groups, n_groups, entries, xq, xsc, y, N, Kp, err};
-  grouped_tc_kernel<<<grid, kGtThreads, grouped_tc_smem(), stream>>>(a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kGtThreads);
+  cfg.dynamicSmemBytes = grouped_tc_smem();
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, grouped_tc_kernel, a);
 }
 
 }  // namespace mfi

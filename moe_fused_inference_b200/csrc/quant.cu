@@ -13,6 +13,7 @@
 // Kp/2 + Kp/32 bytes per row).
 #include "mx_common.cuh"
 #include "work.cuh"
+#include "tc_ptx.cuh"
 
 namespace mfi {
 
@@ -92,6 +93,8 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const float* __restri
                                                            const int* __restrict__ n_rows_dev,
                                                            uint8_t* __restrict__ hq,
                                                            uint8_t* __restrict__ hsc, int K, int Kp) {
+  tc::grid_dep_wait();  // gu (and the row list) come from the kernel before
+  tc::grid_dep_launch();
   const int nr = n_rows_dev ? *n_rows_dev : n_rows;
   const int per_row = Kp >> 3;
   const long total = long(nr) * per_row;
@@ -138,15 +141,23 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const float* __restri
 
 cudaError_t launch_swiglu_quant(const float* gu, long ld_gu, const int* rows, int n_rows,
                                 const int* n_rows_dev, uint8_t* hq, uint8_t* hsc, int K, int Kp,
-                                cudaStream_t stream) {
+                                cudaStream_t stream, bool pdl) {
   const long total = long(n_rows) * (Kp >> 3);
   if (total == 0) return cudaSuccess;
   const int threads = 256;
   long blocks = (total + threads - 1) / threads;
   if (blocks > 148 * 16) blocks = 148 * 16;
-  swiglu_quant_kernel<<<unsigned(blocks), threads, 0, stream>>>(gu, ld_gu, rows, n_rows, n_rows_dev,
-                                                                 hq, hsc, K, Kp);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(blocks));
+  cfg.blockDim = dim3(threads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, swiglu_quant_kernel, gu, ld_gu, rows, n_rows, n_rows_dev, hq, hsc,
+                            K, Kp);
 }
 
 }  // namespace mfi

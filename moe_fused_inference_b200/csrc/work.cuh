@@ -136,7 +136,7 @@ cudaError_t launch_route_tc(const RouteArgs& a, cudaStream_t stream);
 
 cudaError_t launch_swiglu_quant(const float* gu, long ld_gu, const int* rows, int n_rows,
                                 const int* n_rows_dev, uint8_t* hq, uint8_t* hsc, int K, int Kp,
-                                cudaStream_t stream);
+                                cudaStream_t stream, bool pdl = false);
 size_t gemv_smem_bytes(int Kp);
 cudaError_t launch_grouped_gemv(const GroupDesc* groups, const int* n_groups_dev, int n_groups_host,
                                 const EntryDesc* entries, const uint8_t* xq, const uint8_t* xsc,
@@ -150,10 +150,15 @@ cudaError_t launch_dense_gemv(const uint8_t* xq, const uint8_t* xsc, const uint8
 bool grouped_tc_supported(int N, int Kp);
 cudaError_t launch_grouped_tc(const GroupDesc* groups, const int* n_groups, int max_items,
                               const EntryDesc* entries, const uint8_t* xq, const uint8_t* xsc,
-                              float* y, int N, int Kp, int* err, cudaStream_t stream);
+                              float* y, int N, int Kp, int* err, cudaStream_t stream,
+                              bool pdl = false);
 cudaError_t launch_build_groups(const uint8_t* const* wp_tab, const uint8_t* const* wsc_tab, int P,
                                 int mode, int E, int N, GroupDesc* groups, int* n_groups,
-                                EntryDesc* entries, cudaStream_t stream);
+                                EntryDesc* entries, cudaStream_t stream, bool pdl = false);
+// pdl (the three launchers above): programmatic dependent launch.  Each of
+// these kernels waits for the kernel before it before it reads or writes
+// global memory, so only its launch and prologue overlap that kernel's tail.
+
 // clear/n_clear: counters zeroed by the launch once the previous kernel is
 // complete (the fused layer's per-call counters), or null
 // Prefill combine: out[m] = sum over slots e (ascending) of w[m][e] * y[m][e],
