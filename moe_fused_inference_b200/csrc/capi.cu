@@ -186,21 +186,36 @@ int mfi_device_error(int clear) {
 
 // ---------------------------------------------------------------------------
 namespace {
-// The grouped GEMM of the drop-in operators over the grouped pointer tables:
-// the tcgen05 kernel when K tiles by 256 and the activations are aligned for
-// 16-byte copies (every Qwen3-MoE expert shape), else the CUDA-core GEMV.
-int grouped_launch(const mfi::GroupDesc* groups, const int* ng, int P,
-                   const mfi::EntryDesc* entries, const uint8_t* xq, const uint8_t* xsc, float* y,
-                   int N, int Kp, cudaStream_t s, const char* what) {
+// The grouped GEMM of the drop-in operators over the caller's pointer
+// tables: the tcgen05 kernel when K tiles by 256 and the activations are
+// aligned for 16-byte copies (every Qwen3-MoE expert shape), else the
+// CUDA-core GEMV.  The tables are grouped by build_groups_kernel first,
+// except for the tensor-core kernel at decode sizes (at most
+// grouped_tc_local_max() entries), which groups them itself.
+int grouped_launch(const uint8_t* const* wp_tab, const uint8_t* const* wsc_tab, int mode, int E,
+                   mfi::GroupDesc* groups, int* ng, int P, mfi::EntryDesc* entries,
+                   const uint8_t* xq, const uint8_t* xsc, float* y, int N, int Kp, cudaStream_t s,
+                   const char* what) {
   const std::string w = std::string(what) + " grouped GEMM launch";
-  if (mfi::grouped_tc_supported(N, Kp) && (reinterpret_cast<uintptr_t>(xq) & 15) == 0 &&
-      (reinterpret_cast<uintptr_t>(xsc) & 7) == 0) {
-    const long long items = (long long)P * ((N + 127) / 128);
-    return cuda_status(mfi::launch_grouped_tc(groups, ng, items > (1 << 30) ? (1 << 30) : int(items),
-                                              entries, xq, xsc, y, N, Kp,
-                                              mfi::device_error_flag(), s, true),
+  const bool tc = mfi::grouped_tc_supported(N, Kp) && (reinterpret_cast<uintptr_t>(xq) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(xsc) & 7) == 0;
+  const long long items = (long long)P * ((N + 127) / 128);
+  const int max_items = items > (1 << 30) ? (1 << 30) : int(items);
+  if (tc && P <= mfi::grouped_tc_local_max()) {
+    const mfi::GtTables tab{wp_tab, wsc_tab, P, mode, E};
+    return cuda_status(mfi::launch_grouped_tc(groups, ng, max_items, entries, xq, xsc, y, N, Kp,
+                                              mfi::device_error_flag(), s, true, &tab),
                        w.c_str());
   }
+  const std::string wg = std::string(what) + " grouping launch";
+  int st = cuda_status(mfi::launch_build_groups(wp_tab, wsc_tab, P, mode, E, N, groups, ng, entries,
+                                                s, true),
+                       wg.c_str());
+  if (st != MFI_OK) return st;
+  if (tc)
+    return cuda_status(mfi::launch_grouped_tc(groups, ng, max_items, entries, xq, xsc, y, N, Kp,
+                                              mfi::device_error_flag(), s, true),
+                       w.c_str());
   return cuda_status(mfi::launch_grouped_gemv(groups, ng, P, entries, xq, xsc, y, N, Kp,
                                               kGemvMaxCtas, s),
                      w.c_str());
@@ -234,11 +249,8 @@ int mfi_moe_gateup(const uint8_t* xq, const uint8_t* xsc, const uint8_t* const* 
   auto* groups = c.take<mfi::GroupDesc>(P);
   auto* entries = c.take<mfi::EntryDesc>(P);
   cudaStream_t s = as_stream(stream);
-  int st = cuda_status(mfi::launch_build_groups(wp_tab, wsc_tab, int(P), 0, E, N, groups, ng,
-                                                entries, s, true),
-                       "moe_gateup grouping launch");
-  if (st != MFI_OK) return st;
-  return grouped_launch(groups, ng, int(P), entries, xq, xsc, gu, N, Kp, s, "moe_gateup");
+  return grouped_launch(wp_tab, wsc_tab, 0, E, groups, ng, int(P), entries, xq, xsc, gu, N, Kp, s,
+                        "moe_gateup");
 }
 
 size_t mfi_moe_down_workspace_bytes(int E, int M, int K) {
@@ -275,11 +287,8 @@ int mfi_moe_down(const float* gu, const uint8_t* const* wp_tab, const uint8_t* c
                                                 Kp, s, true),
                        "moe_down swiglu launch");
   if (st != MFI_OK) return st;
-  st = cuda_status(mfi::launch_build_groups(wp_tab, wsc_tab, int(P), 1, E, N, groups, ng, entries,
-                                            s, true),
-                   "moe_down grouping launch");
-  if (st != MFI_OK) return st;
-  return grouped_launch(groups, ng, int(P), entries, hq, hsc, yd, N, Kp, s, "moe_down");
+  return grouped_launch(wp_tab, wsc_tab, 1, E, groups, ng, int(P), entries, hq, hsc, yd, N, Kp, s,
+                        "moe_down");
 }
 
 int mfi_moe_combine(const float* yd, int ystride, const float* w, int E, float* out, int M, int N,

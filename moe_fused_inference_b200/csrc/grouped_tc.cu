@@ -55,6 +55,9 @@ constexpr uint32_t kGtTmemCols = 256;
 constexpr uint32_t kGtTmemSF = kGtAccBufs * 32;  // + 16 per ring slot
 static_assert(kGtTmemSF + 16 * kGtStages <= kGtTmemCols, "scale columns exceed the allocation");
 constexpr int kGtMaxChunks = kBuildGroupsMaxP + kBuildGroupsMaxP / kGtTok;
+// tables of at most this many entries are grouped inside the kernel (one
+// warp, shared memory) instead of by build_groups_kernel before it
+constexpr int kGtLocalP = 64;
 
 struct GtArgs {
   const GroupDesc* groups;
@@ -65,7 +68,110 @@ struct GtArgs {
   float* y;
   int N, Kp;
   int* err;
+  // in-kernel grouping (wp_tab non-null, P <= kGtLocalP): the caller's
+  // pointer tables and their layout (mode 0: gate/up, 2·E entries per
+  // activation row; mode 1: down, one entry per row), as build_groups_kernel
+  // takes them; groups / n_groups / entries are then unused
+  const uint8_t* const* wp_tab;
+  const uint8_t* const* wsc_tab;
+  int P, mode, E;
 };
+
+// Group the P <= 64 entries of the caller's tables with one warp, exactly as
+// build_groups_kernel does (gemv.cu): entries with the same (weights, codes)
+// pair form one group, groups in order of first appearance, entries of a
+// group in table order; lane l handles entries l and l + 32.
+__device__ void group_tables_warp(const GtArgs& p, GroupDesc* s_groups, EntryDesc* s_entries,
+                                  int* s_cnt, int* s_ng) {
+  const int lane = threadIdx.x & 31;
+  const unsigned full = 0xffffffffu;
+  const int P = p.P;
+  const uint8_t* wa[2];
+  const uint8_t* sa[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int z = lane + 32 * i;
+    wa[i] = z < P ? p.wp_tab[z] : nullptr;
+    sa[i] = z < P ? p.wsc_tab[z] : nullptr;
+  }
+  int lead[2] = {lane, lane + 32}, rank[2] = {0, 0};
+  for (int j = 0; j < P; ++j) {
+    const unsigned long long wj =
+        __shfl_sync(full, reinterpret_cast<unsigned long long>(j < 32 ? wa[0] : wa[1]), j & 31);
+    const unsigned long long sj =
+        __shfl_sync(full, reinterpret_cast<unsigned long long>(j < 32 ? sa[0] : sa[1]), j & 31);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int z = lane + 32 * i;
+      if (j < z && z < P && wj == reinterpret_cast<unsigned long long>(wa[i]) &&
+          sj == reinterpret_cast<unsigned long long>(sa[i])) {
+        if (lead[i] == z) lead[i] = j;
+        ++rank[i];
+      }
+    }
+  }
+  const bool is0 = lane < P && lead[0] == lane;
+  const bool is1 = lane + 32 < P && lead[1] == lane + 32;
+  const unsigned b0 = __ballot_sync(full, is0), b1 = __ballot_sync(full, is1);
+  const unsigned lt = (1u << lane) - 1u;
+  const int g0 = __popc(b0 & lt), g1 = __popc(b0) + __popc(b1 & lt);
+  const int ng = __popc(b0) + __popc(b1);
+  // group of each entry: the index of its lead
+  int g[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int v0 = __shfl_sync(full, g0, lead[i] & 31);
+    const int v1 = __shfl_sync(full, g1, lead[i] & 31);
+    g[i] = lead[i] < 32 ? v0 : v1;
+  }
+  s_cnt[lane] = 0;
+  s_cnt[lane + 32] = 0;
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    if (lane + 32 * i < P) atomicAdd(&s_cnt[g[i]], 1);
+  __syncwarp();
+  // exclusive scan of the counts: lane l owns groups 2l and 2l + 1
+  const int c0 = s_cnt[2 * lane], c1 = s_cnt[2 * lane + 1];
+  int inc = c0 + c1;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int u = __shfl_up_sync(full, inc, off);
+    if (lane >= off) inc += u;
+  }
+  const int first0 = inc - c0 - c1;
+  __syncwarp();
+  s_cnt[2 * lane] = first0;
+  s_cnt[2 * lane + 1] = first0 + c0;
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int z = lane + 32 * i;
+    if (z >= P) continue;
+    const int first = s_cnt[g[i]];
+    if (lead[i] == z) {
+      GroupDesc gd;
+      gd.wp = wa[i];
+      gd.wsc = sa[i];
+      gd.first = first;
+      gd.count = (g[i] + 1 < ng ? s_cnt[g[i] + 1] : P) - first;
+      s_groups[g[i]] = gd;
+    }
+    EntryDesc ed;
+    ed.pad = 0;
+    if (p.mode == 0) {
+      const int m = z / (2 * p.E), pair = z % (2 * p.E), proj = pair / p.E, e = pair % p.E;
+      ed.act_row = m;
+      ed.out_off = (long long)(m * p.E + e) * 2 * p.N + (long long)proj * p.N;
+    } else {
+      ed.act_row = z;
+      ed.out_off = (long long)z * p.N;
+    }
+    s_entries[first + rank[i]] = ed;
+  }
+  if (lane == 0) *s_ng = ng;
+  __syncwarp();
+}
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
@@ -95,6 +201,13 @@ __global__ void __launch_bounds__(kGtThreads, 1) grouped_tc_kernel(GtArgs p) {
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   __shared__ int s_chunk[kGtMaxChunks];  // (group << 8) | chunk index within the group
   __shared__ int s_nchunks;
+  __shared__ GroupDesc s_groups[kGtLocalP];
+  __shared__ EntryDesc s_entries[kGtLocalP];
+  __shared__ int s_gcnt[kGtLocalP];
+  __shared__ int s_ng;
+  const bool local = p.wp_tab != nullptr;
+  const GroupDesc* groups = local ? s_groups : p.groups;
+  const EntryDesc* entries = local ? s_entries : p.entries;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nks = p.Kp / 256, nb = p.Kp / 32;
@@ -119,11 +232,12 @@ __global__ void __launch_bounds__(kGtThreads, 1) grouped_tc_kernel(GtArgs p) {
   grid_dep_launch();
   // chunk table: every group's rows in chunks of 32, groups in order
   if (warp == 5) {
-    const int ng = *p.n_groups;
+    if (local) group_tables_warp(p, s_groups, s_entries, s_gcnt, &s_ng);
+    const int ng = local ? s_ng : *p.n_groups;
     int run = 0;
     for (int g0 = 0; g0 < ng; g0 += 32) {
       const int g = g0 + lane;
-      const int nch = g < ng ? (p.groups[g].count + kGtTok - 1) / kGtTok : 0;
+      const int nch = g < ng ? (groups[g].count + kGtTok - 1) / kGtTok : 0;
       int inc = nch;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
@@ -158,7 +272,7 @@ __global__ void __launch_bounds__(kGtThreads, 1) grouped_tc_kernel(GtArgs p) {
       ItemDesc d;
       const int cv = s_chunk[item / n_tiles];
       d.tile = item % n_tiles;
-      const GroupDesc gd = p.groups[cv >> 8];
+      const GroupDesc gd = groups[cv >> 8];
       const int c0 = (cv & 255) * kGtTok;
       const int cnt = min(kGtTok, gd.count - c0);
       // the caller's weight pointers come from device tables: a tensor not
@@ -170,9 +284,9 @@ __global__ void __launch_bounds__(kGtThreads, 1) grouped_tc_kernel(GtArgs p) {
       d.wp = gd.wp;
       d.wsc = gd.wsc;
       d.n_live = w_ok ? p.N : 0;
-      d.ar0 = j0 < cnt ? p.entries[gd.first + c0 + j0].act_row : -1;
-      d.ar1 = j1 < cnt ? p.entries[gd.first + c0 + j1].act_row : -1;
-      d.ar_sf = t < cnt ? p.entries[gd.first + c0 + t].act_row : -1;
+      d.ar0 = j0 < cnt ? entries[gd.first + c0 + j0].act_row : -1;
+      d.ar1 = j1 < cnt ? entries[gd.first + c0 + j1].act_row : -1;
+      d.ar_sf = t < cnt ? entries[gd.first + c0 + t].act_row : -1;
       return d;
     };
     // the activation atoms' unused words (words 1-3 of each row line) stay zero
@@ -287,10 +401,10 @@ __global__ void __launch_bounds__(kGtThreads, 1) grouped_tc_kernel(GtArgs p) {
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++ti) {
       const int cv = s_chunk[item / n_tiles];
       const int tile = item % n_tiles;
-      const GroupDesc gd = p.groups[cv >> 8];
+      const GroupDesc gd = groups[cv >> 8];
       const int c0 = (cv & 255) * kGtTok;
       const int cnt = min(kGtTok, gd.count - c0);
-      const long long my_off = lane < cnt ? p.entries[gd.first + c0 + lane].out_off : 0;
+      const long long my_off = lane < cnt ? entries[gd.first + c0 + lane].out_off : 0;
       const uint32_t buf = ti % kGtAccBufs;
       if (!mbar_wait(&acc_full[buf], (ti / kGtAccBufs) & 1, p.err, 3)) break;
       tc_fence_after();
@@ -326,10 +440,12 @@ static_assert(grouped_tc_smem() + kGtMaxChunks * 4 + 64 <= 232448, "shared memor
 }  // namespace
 
 bool grouped_tc_supported(int N, int Kp) { return Kp % 256 == 0 && Kp >= 256 && N > 0; }
+int grouped_tc_local_max() { return kGtLocalP; }
 
 cudaError_t launch_grouped_tc(const GroupDesc* groups, const int* n_groups, int max_items,
                               const EntryDesc* entries, const uint8_t* xq, const uint8_t* xsc,
-                              float* y, int N, int Kp, int* err, cudaStream_t stream, bool pdl) {
+                              float* y, int N, int Kp, int* err, cudaStream_t stream, bool pdl,
+                              const GtTables* tables) {
   if (!grouped_tc_supported(N, Kp)) return cudaErrorNotSupported;
   cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(grouped_tc_kernel),
                                       grouped_tc_smem());
@@ -338,7 +454,15 @@ cudaError_t launch_grouped_tc(const GroupDesc* groups, const int* n_groups, int 
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int grid = max_items < sms ? (max_items > 0 ? max_items : 1) : sms;
-  GtArgs a{groups, n_groups, entries, xq, xsc, y, N, Kp, err};
+  GtArgs a{};
+  a.groups = groups; a.n_groups = n_groups; a.entries = entries;
+  a.xq = xq; a.xsc = xsc; a.y = y; a.N = N; a.Kp = Kp; a.err = err;
+  a.wp_tab = tables ? tables->wp_tab : nullptr;
+  a.wsc_tab = tables ? tables->wsc_tab : nullptr;
+  a.P = tables ? tables->P : 0;
+  a.mode = tables ? tables->mode : 0;
+  a.E = tables ? tables->E : 0;
+  if (tables && (tables->P <= 0 || tables->P > kGtLocalP)) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kGtThreads);

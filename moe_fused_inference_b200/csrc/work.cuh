@@ -148,10 +148,19 @@ cudaError_t launch_dense_gemv(const uint8_t* xq, const uint8_t* xsc, const uint8
 // multiple of 256, xq rows 16-byte and xsc rows 8-byte aligned; max_items
 // bounds (groups' 32-row chunks) x (128-row tiles) for the grid size.
 bool grouped_tc_supported(int N, int Kp);
+// The caller's pointer tables, for a grouped_tc launch that groups them
+// itself (P <= grouped_tc_local_max()); groups / n_groups / entries are then
+// not read.
+struct GtTables {
+  const uint8_t* const* wp_tab;
+  const uint8_t* const* wsc_tab;
+  int P, mode, E;
+};
+int grouped_tc_local_max();
 cudaError_t launch_grouped_tc(const GroupDesc* groups, const int* n_groups, int max_items,
                               const EntryDesc* entries, const uint8_t* xq, const uint8_t* xsc,
                               float* y, int N, int Kp, int* err, cudaStream_t stream,
-                              bool pdl = false);
+                              bool pdl = false, const GtTables* tables = nullptr);
 cudaError_t launch_build_groups(const uint8_t* const* wp_tab, const uint8_t* const* wsc_tab, int P,
                                 int mode, int E, int N, GroupDesc* groups, int* n_groups,
                                 EntryDesc* entries, cudaStream_t stream, bool pdl = false);

@@ -82,10 +82,12 @@ def _experts(rng, E, N, K):
     return g, u, d
 
 
-@pytest.mark.parametrize("M", [1, 5])
+@pytest.mark.parametrize("M", [1, 4, 5])
 def test_moe_gateup_down_combine_chain(M):
     """Grouped chain with the reference's pointer-table order
-    (runtime/model_runner_v2.py:279-289), M tokens, E = 8 slots, shared experts."""
+    (runtime/model_runner_v2.py:279-289), M tokens, E = 8 slots, shared experts.
+    Tables of at most 64 entries (M <= 4 for gate/up, M <= 8 for down) are
+    grouped inside the tensor-core kernel; larger ones by build_groups_kernel."""
     rng = np.random.default_rng(2 + M)
     E, N, K, NE = 8, 768, 2048, 12
     g, u, d = _experts(rng, NE, N, K)
@@ -147,11 +149,14 @@ def test_moe_tab_variants_and_legacy_arity():
     assert torch.equal(dext.moe_combine(yd, w), dext.moe_combine(yd, w.view(1, E), 1))
 
 
-def test_all_tokens_one_expert_and_duplicates():
+@pytest.mark.parametrize("N,K,M", [(64, 128, 20), (128, 256, 4), (128, 256, 20)])
+def test_all_tokens_one_expert_and_duplicates(N, K, M):
     """Edge case: every token picks the same experts (one weight shared by all
-    entries) — each weight is streamed once for all its tokens."""
+    entries) — each weight is streamed once for all its tokens.  K = 128 runs
+    the CUDA-core GEMV; K = 256 the tensor-core kernel, with the tables grouped
+    inside it (M = 4: 32 entries) or by build_groups_kernel (M = 20)."""
     rng = np.random.default_rng(5)
-    E, N, K, M = 4, 64, 128, 20
+    E = 4
     g, u, d = _experts(rng, E, N, K)
     x = make_x(rng, M, K)
     dext = fp4_ext.get_decode_ext()
