@@ -76,14 +76,17 @@ def parse():
     ap.add_argument("--tokens", type=int, default=64, help="decode tokens per GPU (T)")
     ap.add_argument("--layers", type=int, default=N_LAYERS,
                     help="distinct MoE layers per step (48 = the model; fewer for profiling)")
-    ap.add_argument("--workload", choices=["decode", "prefill", "linear", "model"],
+    ap.add_argument("--workload", choices=["decode", "prefill", "linear", "model", "dropin",
+                                           "attn"],
                     default="decode",
                     help="decode (BASELINE config 2, the headline, with every other "
                          "configuration in the same line), prefill (config 3 alone: T = 16384 "
                          "by default, Zipf(1.2)-skewed routing), linear (the static decode "
-                         "projections and lm_head through lin_pq) or model (config 4: greedy "
+                         "projections and lm_head through lin_pq), model (config 4: greedy "
                          "decode of the 48-layer synthetic model at batch 1 / 16 / 64, each "
-                         "step one CUDA graph)")
+                         "step one CUDA graph), dropin (the decode line's drop-in block "
+                         "alone: the reference's call sequence at T = 1 and 16 over --layers "
+                         "layers) or attn (the decode line's attention block alone)")
     ap.add_argument("--headline-only", action="store_true",
                     help="decode: skip the sweep, prefill, drop-in and T=4 blocks")
     ap.add_argument("--zipf-alpha", type=float, default=0.5,
@@ -854,7 +857,65 @@ def run_model(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def run_dropin(args, world, rank, local):
+    """--workload dropin: the decode line's drop-in block alone (the
+    reference's decode MoE block through moe_gateup / moe_down / moe_combine
+    with its host steps, T = 1 and 16), for profiling that chain."""
+    from moe_fused_inference_b200.layer import MoELayer, random_layer_weights
+
+    dev = torch.device("cuda", local if world > 1 else 0)
+    stream = torch.cuda.current_stream(dev)
+    peak, peak_kind = measured_peaks()
+    layers = [MoELayer(random_layer_weights(E, H, MI, 0.02, seed=l, device=dev), TOPK)
+              for l in range(args.layers)]
+    res = {f"T{t}": dropin_point(layers, t, dev, stream, args.steps, max(args.warmup, 1), peak)
+           for t in (1, 16)}
+    if rank != 0:
+        return
+    head = res["T1"]
+    line = {
+        "metric": "drop-in decode MoE block tokens/s (T=1, the reference's call sequence)",
+        "value": head["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["us_per_layer"] / 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "mxfp4 (e2m1 x e2m1, fp32 accumulate)",
+        "data": "synthetic (random-init weights N(0,0.02), activations N(0,1), seeded)",
+        "config": {"workload": f"drop-in moe_gateup/moe_down/moe_combine chain, {args.layers} "
+                               "layers, T in {1, 16}", "peak_kind": peak_kind},
+        "dropin": res,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_attn(args, world, rank, local):
+    """--workload attn: the decode line's attention block alone (FP8-KV
+    decode attention, context 4096, M = 1 and 5 query rows)."""
+    dev = torch.device("cuda", local if world > 1 else 0)
+    stream = torch.cuda.current_stream(dev)
+    peak, peak_kind = measured_peaks()
+    res = {f"M{m}_ctx4096": attn_point(dev, stream, args.steps, max(args.warmup, 1), peak, M=m)
+           for m in (1, 5)}
+    if rank != 0:
+        return
+    head = res["M1_ctx4096"]
+    line = {
+        "metric": "FP8-KV decode attention us per call (M=1, context 4096)", "value": head["us"],
+        "unit": "us", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": head["us"] / 1e3, "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp8 e4m3 KV, fp32 softmax",
+        "data": "synthetic (seeded queries and caches)",
+        "config": {"workload": "mfi_attn_decode, 32 query / 4 KV heads, head_dim 128, "
+                               "context 4096, M in {1, 5}", "peak_kind": peak_kind},
+        "attn_decode": res,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_ours(args, world, rank, local):
+    if args.workload == "dropin":
+        return run_dropin(args, world, rank, local)
+    if args.workload == "attn":
+        return run_attn(args, world, rank, local)
     if args.workload == "model":
         return run_model(args, world, rank, local)
     if args.workload == "prefill":
