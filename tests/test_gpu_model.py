@@ -18,7 +18,7 @@ What is asserted:
 * the library against the torch arm on the prompt's forward pass: the
   residual stream agrees layer by layer (cosine >= 0.995) and the logits
   (cosine >= 0.99).
-What is reported (printed, and recorded in DESIGN.md): the first step at
+What is reported (printed): the first step at
 which the two arms' greedy tokens differ and both arms' top-2 logit margins
 there.  Exact identity over 128 steps is not attainable against an
 independent arithmetic on this model: the library's softmax, attention and
