@@ -366,13 +366,32 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
   const float* wb = w + long(m) * E;
   if (c4 + 4 <= N && (ystride % 4) == 0 && (N % 4) == 0) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int e = 0; e < E_sum; ++e) {
-      const float we = wb[e];
-      const float4 v = *reinterpret_cast<const float4*>(yb + long(e) * ystride + c4);
-      acc.x = __fadd_rn(acc.x, __fmul_rn(we, v.x));
-      acc.y = __fadd_rn(acc.y, __fmul_rn(we, v.y));
-      acc.z = __fadd_rn(acc.z, __fmul_rn(we, v.z));
-      acc.w = __fadd_rn(acc.w, __fmul_rn(we, v.w));
+    if (E_sum == 8) {
+      // the usual top-8: every slot's row and weight is loaded before the
+      // (unchanged, sequential) sums, so the loads overlap
+      float we[8];
+      float4 v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        we[e] = wb[e];
+        v[e] = *reinterpret_cast<const float4*>(yb + long(e) * ystride + c4);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        acc.x = __fadd_rn(acc.x, __fmul_rn(we[e], v[e].x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(we[e], v[e].y));
+        acc.z = __fadd_rn(acc.z, __fmul_rn(we[e], v[e].z));
+        acc.w = __fadd_rn(acc.w, __fmul_rn(we[e], v[e].w));
+      }
+    } else {
+      for (int e = 0; e < E_sum; ++e) {
+        const float we = wb[e];
+        const float4 v = *reinterpret_cast<const float4*>(yb + long(e) * ystride + c4);
+        acc.x = __fadd_rn(acc.x, __fmul_rn(we, v.x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(we, v.y));
+        acc.z = __fadd_rn(acc.z, __fmul_rn(we, v.z));
+        acc.w = __fadd_rn(acc.w, __fmul_rn(we, v.w));
+      }
     }
     *reinterpret_cast<float4*>(out + long(m) * N + c4) = acc;
   } else {
